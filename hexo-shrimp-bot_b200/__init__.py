@@ -17,10 +17,17 @@ __all__ = [
 ]
 
 
+_SUBMODULES = ("_lib", "ops", "model", "evaluator", "vocab", "engine", "builder", "config", "build", "sharding")
+
+
 def __getattr__(name):
     # The model and evaluator import torch CUDA bindings and the native
     # library lazily, so host-only users (builders, tests) need neither.
-    if name in ("MantisNet", "ModelOutput", "compose_q", "compose_acting_q", "return_mass"):
+    if name in _SUBMODULES:
+        import importlib
+
+        return importlib.import_module(f".{name}", __name__)
+    if name in ("MantisNet", "ModelOutput", "compose_q", "compose_acting_q", "return_mass", "Engine"):
         from . import model
 
         return getattr(model, name)

@@ -1,0 +1,7 @@
+// Single translation unit of libmantis_b200.so: the kernels share one device
+// error word, so they are compiled together.
+#include "api.cu"
+#include "tables.cu"
+#include "rows.cu"
+#include "attention.cu"
+#include "gemm_simt.cu"

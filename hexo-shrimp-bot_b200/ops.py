@@ -1,0 +1,592 @@
+"""Tensor-level wrappers over the C ABI.
+
+Two layers:
+
+1. Thin wrappers (``run_reduce``, ``segment_attention``, ...) used by the
+   model: they take CUDA tensors (row-major, unit inner stride, views allowed)
+   and launch on the current stream.
+2. The reference's operator surface, same names, argument meaning and error
+   classes (``ValueError`` for bad arguments): ``fused_attention``,
+   ``aggregate_to_windows``, ``aggregate_to_stones``, ``class_row_sum``,
+   ``incidence_row_sum``, ``cell_attention``, ``cell_attention_plain``,
+   ``read_attention``/``broadcast_attention``, ``window_latent_layout``,
+   ``encode_rows``, ``cell_pass``, ``cell_tables``, ``edge_tables``,
+   ``incidence_plan`` (reference python/mantisnet/mantisnet/{attention,
+   message_passing,cell_latents,cell_nodes,window_latents,row_encoder,
+   relay}.py). There is no CPU path: a non-CUDA tensor raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import NamedTuple
+
+import torch
+
+from . import _lib
+from ._lib import call, dtype_code, ptr, stream_of
+
+_I64 = torch.int64
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("the B200 kernels take CUDA tensors only (no CPU fallback)")
+
+
+def _rowmajor(t, name):
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"{name} must be a row-major 2-D tensor with unit inner stride")
+
+
+def _i64(t, name):
+    if t.dtype != _I64:
+        raise ValueError(f"{name} must have dtype int64")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _bits(n: int) -> int:
+    return max(1, int(n - 1).bit_length()) if n > 1 else 1
+
+
+# --------------------------------------------------------------- tables
+
+def csr(keys: torch.Tensor, n_dest: int) -> torch.Tensor:
+    """ptr[d] = searchsorted(keys, d, left) for d in [0, n_dest]."""
+    _cuda(keys)
+    _i64(keys, "keys")
+    out = torch.empty(n_dest + 1, dtype=_I64, device=keys.device)
+    call("mb_csr_from_sorted", ptr(keys), keys.numel(), n_dest, ptr(out), stream_of(keys.device))
+    return out
+
+
+def argsort(keys: torch.Tensor, bound: int):
+    """Stable argsort of int64 keys in [0, bound): (sorted_keys, order)."""
+    _cuda(keys)
+    _i64(keys, "keys")
+    n = keys.numel()
+    sk = torch.empty_like(keys)
+    order = torch.empty_like(keys)
+    if n == 0:
+        return sk, order
+    bits = _bits(bound)
+    need = ctypes.c_int64(0)
+    call("mb_argsort_workspace", n, bits, ctypes.byref(need))
+    ws = torch.empty(need.value, dtype=torch.uint8, device=keys.device)
+    call("mb_argsort", ptr(keys), n, bits, ptr(sk), ptr(order), ptr(ws), need.value, stream_of(keys.device))
+    return sk, order
+
+
+def gather_i64(src: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
+    out = torch.empty(idx.shape[0], dtype=_I64, device=idx.device)
+    call("mb_gather_i64", ptr(src), src.numel(), ptr(idx), idx.numel(), ptr(out), stream_of(idx.device))
+    return out
+
+
+def radius_class(orbit, own, on_axis, order=None) -> torch.Tensor:
+    out = torch.empty(orbit.shape[0], dtype=_I64, device=orbit.device)
+    call("mb_radius_class", ptr(orbit), ptr(own), ptr(on_axis), ptr(order), orbit.numel(), ptr(out),
+         stream_of(orbit.device))
+    return out
+
+
+def div_i64(x: torch.Tensor, divisor: int) -> torch.Tensor:
+    out = torch.empty_like(x)
+    call("mb_div_i64", ptr(x), x.numel(), int(divisor), ptr(out), stream_of(x.device))
+    return out
+
+
+# ------------------------------------------------------- thin wrappers
+
+def run_reduce(values, gather, ptr_, n_dest, add=None, add_idx=None, out=None, out_dtype=torch.float32):
+    """out[d] = sum_{e in run d} values[gather[e]] (+ add[add_idx[d]]), fp32 accumulation."""
+    _cuda(values, gather, ptr_)
+    _rowmajor(values, "values")
+    width = values.shape[1]
+    if out is None:
+        out = torch.empty(n_dest, width, dtype=out_dtype, device=values.device)
+    n_add = 0
+    if add is not None:
+        _rowmajor(add, "add")
+        n_add = add.shape[0]
+    call("mb_run_reduce", ptr(values), dtype_code(values.dtype), values.stride(0), values.shape[0], ptr(gather),
+         ptr(ptr_), n_dest, width, ptr(add), add.stride(0) if add is not None else 0, ptr(add_idx), n_add,
+         ptr(out), dtype_code(out.dtype), out.stride(0), stream_of(values.device))
+    return out
+
+
+def row_encode(pre, table, edge_window, edge_class, cell_ptr, n_cells, empty_counts=None, empty_base=None,
+               empty_cls=None, out_dtype=torch.float32):
+    _cuda(pre, table, edge_window, edge_class, cell_ptr)
+    h = pre.shape[1]
+    out = torch.empty(n_cells, h, dtype=out_dtype, device=pre.device)
+    n_empty = empty_cls.numel() if empty_cls is not None else 0
+    call("mb_row_encode", ptr(pre), dtype_code(pre.dtype), pre.shape[0], ptr(table), table.shape[0],
+         ptr(edge_window), ptr(edge_class), ptr(cell_ptr), n_cells,
+         ptr(empty_counts), ptr(empty_base), ptr(empty_cls), n_empty, h, ptr(out), dtype_code(out.dtype),
+         stream_of(pre.device))
+    return out
+
+
+def segment_attention(q, k, v, bias, vcls, seg_ptr, src, cls, skip_ptr=None, out=None, out_dtype=torch.float32,
+                      stats=False):
+    """Typed segment attention (K3). q (n_q, A, d) or (n_q, H) rows; k/v may
+    be column views of one fused projection (same row stride)."""
+    _cuda(q, k, v, bias, seg_ptr)
+    heads = bias.shape[0]
+    q2 = q.reshape(q.shape[0], -1) if q.dim() == 3 else q
+    k2 = k.reshape(k.shape[0], -1) if k.dim() == 3 else k
+    v2 = v.reshape(v.shape[0], -1) if v.dim() == 3 else v
+    for t, n in ((q2, "q"), (k2, "k"), (v2, "v")):
+        _rowmajor(t, n)
+    if k2.stride(0) != v2.stride(0):
+        raise ValueError("k and v must share a row stride")
+    if not (q2.dtype == k2.dtype == v2.dtype):
+        raise ValueError("q, k, and v must have one dtype")
+    n_q, width = q2.shape
+    hd = width // heads
+    if out is None:
+        out = torch.empty(n_q, width, dtype=out_dtype, device=q.device)
+    m = l = None
+    if stats:
+        m = torch.empty(n_q, heads, dtype=torch.float32, device=q.device)
+        l = torch.empty_like(m)
+    bias32 = bias.float().contiguous()
+    vcls32 = vcls.float().contiguous() if vcls is not None else None
+    call("mb_segment_attention", ptr(q2), q2.stride(0), ptr(k2), ptr(v2), k2.stride(0), dtype_code(q2.dtype),
+         n_q, k2.shape[0], heads, hd, ptr(bias32), bias32.shape[1], ptr(vcls32), ptr(seg_ptr), ptr(src), ptr(cls),
+         ptr(skip_ptr), ptr(out), dtype_code(out.dtype), out.stride(0), ptr(m), ptr(l), stream_of(q.device))
+    return (out, m, l) if stats else out
+
+
+def stone_attention_ragged(qkv, tok_off, heads, max_tokens, max_queries=-1, out=None, out_dtype=None):
+    """Attention over [latents; stones] per position on the token layout:
+    qkv (N_tok, 3H) = [q | k | v]. With max_queries=4 the output is compact
+    (P*4, H); otherwise (N_tok, H)."""
+    _rowmajor(qkv, "qkv")
+    h = qkv.shape[1] // 3
+    hd = h // heads
+    n_pos = tok_off.shape[0] - 1
+    out_dtype = out_dtype or qkv.dtype
+    compact = max_queries >= 0
+    if out is None:
+        rows = n_pos * max_queries if compact else qkv.shape[0]
+        out = torch.empty(rows, h, dtype=out_dtype, device=qkv.device)
+    es = qkv.element_size()
+    call("mb_stone_attention", ptr(qkv), qkv.data_ptr() + h * es, qkv.data_ptr() + 2 * h * es,
+         dtype_code(qkv.dtype), n_pos, heads, hd, 0, hd, qkv.stride(0), None, 0, ptr(tok_off), max_tokens,
+         max_queries, ptr(out), dtype_code(out.dtype), max_queries * out.stride(0) if compact else 0, hd,
+         out.stride(0), stream_of(qkv.device))
+    return out
+
+
+def latent_read(q, k, v, heads, offsets, order, out_dtype=torch.float32, stats=False):
+    """q (P*4, H) rows, k/v (N_w, H) rows (views of a fused kv allowed)."""
+    _rowmajor(q, "q"); _rowmajor(k, "k"); _rowmajor(v, "v")
+    n_pos = offsets.shape[0] - 1
+    h = q.shape[1]
+    out = torch.empty(n_pos * 4, h, dtype=out_dtype, device=q.device)
+    m = l = None
+    if stats:
+        m = torch.empty(n_pos * 4, heads, dtype=torch.float32, device=q.device)
+        l = torch.empty_like(m)
+    call("mb_window_latent_read", ptr(q), q.stride(0), ptr(k), ptr(v), k.stride(0), dtype_code(q.dtype), n_pos,
+         k.shape[0], heads, h // heads, ptr(offsets), ptr(order), ptr(out), dtype_code(out_dtype), ptr(m), ptr(l),
+         stream_of(q.device))
+    return (out, m, l) if stats else out
+
+
+def latent_broadcast(q, k, v, heads, window_pos, n_pos, out_dtype=torch.float32, stats=False):
+    _rowmajor(q, "q"); _rowmajor(k, "k"); _rowmajor(v, "v")
+    n_w, h = q.shape
+    out = torch.empty(n_w, h, dtype=out_dtype, device=q.device)
+    m = l = None
+    if stats:
+        m = torch.empty(n_w, heads, dtype=torch.float32, device=q.device)
+        l = torch.empty_like(m)
+    call("mb_window_latent_broadcast", ptr(q), q.stride(0), ptr(k), ptr(v), k.stride(0), dtype_code(q.dtype),
+         n_pos, n_w, heads, h // heads, ptr(window_pos), ptr(out), dtype_code(out_dtype), ptr(m), ptr(l),
+         stream_of(q.device))
+    return (out, m, l) if stats else out
+
+
+def latent_mix(qkv, heads, out_dtype):
+    """qkv (P*4, 3H) = [q | k | v] -> (P*4, H)."""
+    _rowmajor(qkv, "qkv")
+    h = qkv.shape[1] // 3
+    n_pos = qkv.shape[0] // 4
+    out = torch.empty(n_pos * 4, h, dtype=out_dtype, device=qkv.device)
+    es = qkv.element_size()
+    call("mb_latent_mix", ptr(qkv), qkv.data_ptr() + h * es, qkv.data_ptr() + 2 * h * es, qkv.stride(0),
+         dtype_code(qkv.dtype), n_pos, heads, h // heads, ptr(out), dtype_code(out_dtype), stream_of(qkv.device))
+    return out
+
+
+def layer_norm(x, gamma, beta, out_dtype=None, out=None, rows=None, eps=1e-5):
+    _rowmajor(x, "x")
+    n = rows.shape[0] if rows is not None else x.shape[0]
+    h = x.shape[1]
+    if out is None:
+        out = torch.empty(n, h, dtype=out_dtype or x.dtype, device=x.device)
+    call("mb_layer_norm", ptr(x), dtype_code(x.dtype), x.stride(0), ptr(rows), n, h, ptr(gamma), ptr(beta),
+         float(eps), ptr(out), dtype_code(out.dtype), out.stride(0), stream_of(x.device))
+    return out
+
+
+def embed(ta, ia, tb=None, ib=None, n=None):
+    n = n if n is not None else ia.shape[0]
+    h = ta.shape[1]
+    out = torch.empty(n, h, dtype=torch.float32, device=ta.device)
+    call("mb_embed", ptr(ta), ta.shape[0], ptr(ia), ptr(tb), tb.shape[0] if tb is not None else 0, ptr(ib), n, h,
+         ptr(out), stream_of(ta.device))
+    return out
+
+
+def cell_init(cov_ptr, cell_nearest, nearest_table, covered_row, covered_add=None):
+    n, h = cell_nearest.shape[0], nearest_table.shape[1]
+    out = torch.empty(n, h, dtype=torch.float32, device=nearest_table.device)
+    call("mb_cell_init", ptr(cov_ptr), ptr(cell_nearest), ptr(nearest_table), nearest_table.shape[0],
+         ptr(covered_row), ptr(covered_add), n, h, ptr(out), stream_of(out.device))
+    return out
+
+
+def residual_add(x, y, rows=None):
+    """x[rows[i]] += y[i] (x f32 or bf16, in place)."""
+    _rowmajor(x, "x"); _rowmajor(y, "y")
+    n = y.shape[0]
+    call("mb_residual_add", ptr(x), dtype_code(x.dtype), x.stride(0), ptr(rows), ptr(y), dtype_code(y.dtype),
+         y.stride(0), n, y.shape[1], stream_of(x.device))
+    return x
+
+
+def add_gather(x, t, idx, relu=False):
+    """x[i] = act(x[i] + t[idx[i]]) in place."""
+    _rowmajor(x, "x"); _rowmajor(t, "t")
+    call("mb_add_gather", ptr(x), dtype_code(x.dtype), x.stride(0), ptr(t), dtype_code(t.dtype), t.stride(0),
+         t.shape[0], ptr(idx), x.shape[0], x.shape[1], int(relu), stream_of(x.device))
+    return x
+
+
+def tokens_gather(g, s, stone_off, tok_off, n_tok):
+    h = g.shape[1]
+    tok = torch.empty(n_tok, h, dtype=torch.float32, device=g.device)
+    call("mb_tokens_gather", ptr(g), ptr(s), ptr(stone_off), ptr(tok_off), tok_off.shape[0] - 1, h, ptr(tok),
+         stream_of(g.device))
+    return tok
+
+
+def tokens_scatter_add(g, s, stone_off, tok_off, tok_out, update_stones=True):
+    call("mb_tokens_scatter_add", ptr(g), ptr(s), ptr(stone_off), ptr(tok_off), tok_off.shape[0] - 1, g.shape[1],
+         ptr(tok_out), dtype_code(tok_out.dtype), int(update_stones), stream_of(g.device))
+
+
+def latent_mean(g_ln, n_pos):
+    h = g_ln.shape[1]
+    out = torch.empty(n_pos, h, dtype=torch.float32, device=g_ln.device)
+    call("mb_latent_mean", ptr(g_ln), n_pos, h, ptr(out), stream_of(g_ln.device))
+    return out
+
+
+def compose(critic, offsets, mass_floor):
+    """(q_score, q_values) from (N, 3) fp32 logits (model.py:177-220)."""
+    critic = critic.float()
+    _rowmajor(critic, "critic")
+    n = critic.shape[0]
+    q_score = torch.empty(n, dtype=torch.float32, device=critic.device)
+    q_values = torch.empty_like(q_score)
+    call("mb_compose_q", ptr(critic), critic.stride(0), ptr(offsets), offsets.shape[0] - 1, float(mass_floor),
+         ptr(q_score), ptr(q_values), stream_of(critic.device))
+    return q_score, q_values
+
+
+def linear_native(a, w, bias=None, relu=False, out_dtype=None, out=None):
+    """CUDA-core GEMM with fp32 accumulation: act(a @ w^T + bias)."""
+    _rowmajor(a, "a")
+    w = w.contiguous()
+    m, k = a.shape
+    n = w.shape[0]
+    if out is None:
+        out = torch.empty(m, n, dtype=out_dtype or a.dtype, device=a.device)
+    b = bias.float().contiguous() if bias is not None else None
+    call("mb_linear", ptr(a), dtype_code(a.dtype), a.stride(0), m, k, ptr(w), dtype_code(w.dtype), ptr(b), n,
+         int(relu), ptr(out), dtype_code(out.dtype), out.stride(0), stream_of(a.device))
+    return out
+
+
+# ================================================= reference op surface
+
+class CellTables(NamedTuple):
+    """cell_latents.py:78-93 (same field order and meaning)."""
+
+    covered: torch.Tensor
+    cell_ptr: torch.Tensor
+    edge_window: torch.Tensor
+    edge_class: torch.Tensor
+    edge_cell: torch.Tensor
+    win_ptr: torch.Tensor
+    edge_wcell: torch.Tensor
+    edge_wclass: torch.Tensor
+    edge_wwin: torch.Tensor
+    cls_ptr: torch.Tensor
+    cedge_cell: torch.Tensor
+    cedge_win: torch.Tensor
+
+
+class IncidencePlan(NamedTuple):
+    run_stone: torch.Tensor
+    run_window: torch.Tensor
+    run_class: torch.Tensor
+
+
+def incidence_plan(inc_stone, inc_window, inc_class) -> IncidencePlan:
+    """message_passing.py:495-517: the stone-major stable view."""
+    if inc_class.shape != inc_stone.shape or inc_class.dtype != _I64:
+        raise ValueError("inc_class must be int64 and one length with inc_stone")
+    _cuda(inc_stone, inc_window, inc_class)
+    bound = int(inc_stone.max().item()) + 1 if inc_stone.numel() else 1
+    sk, order = argsort(inc_stone, bound)
+    return IncidencePlan(sk, gather_i64(inc_window, order), gather_i64(inc_class, order))
+
+
+def _covered_from_ptr(p: torch.Tensor) -> torch.Tensor:
+    return torch.nonzero(p[1:] > p[:-1]).reshape(-1)
+
+
+def cell_tables(dec_cell, dec_window, dec_class, n_windows, n_classes, n_cells=-1) -> CellTables:
+    """cell_latents.py:96-165 on the device; bit-exact with the reference."""
+    if not (dec_cell.shape == dec_window.shape == dec_class.shape):
+        raise ValueError("dec_cell, dec_window, and dec_class must be one length")
+    if dec_cell.ndim != 1:
+        raise ValueError("decoder incidence arrays must be one-dimensional")
+    _cuda(dec_cell, dec_window, dec_class)
+    if dec_window.numel():
+        if int(dec_window.min()) < 0 or int(dec_window.max()) >= n_windows:
+            raise ValueError(f"dec_window entries must lie in [0, {n_windows})")
+        if int(dec_class.min()) < 0 or int(dec_class.max()) >= n_classes:
+            raise ValueError(f"dec_class entries must lie in [0, {n_classes})")
+    bound = n_cells if n_cells >= 0 else (int(dec_cell.max()) + 1 if dec_cell.numel() else 1)
+    if n_cells >= 0 and dec_cell.numel() and (int(dec_cell.min()) < 0 or int(dec_cell.max()) >= n_cells):
+        raise ValueError(f"dec_cell entries must lie in [0, {n_cells})")
+    sorted_cell, order = argsort(dec_cell, max(bound, 1))
+    edge_window = gather_i64(dec_window, order)
+    edge_class = gather_i64(dec_class, order)
+    full_ptr = csr(sorted_cell, max(bound, 0))
+    covered = _covered_from_ptr(full_ptr)
+    if n_cells < 0:
+        cell_ptr = torch.cat([full_ptr[covered], full_ptr[-1:]])
+        compact = torch.cumsum((full_ptr[1:] > full_ptr[:-1]).to(_I64), 0) - 1
+        edge_cell = gather_i64(compact, sorted_cell)
+    else:
+        cell_ptr = full_ptr
+        edge_cell = sorted_cell
+    win_sorted, worder = argsort(edge_window, max(n_windows, 1))
+    win_ptr = csr(win_sorted, n_windows)
+    cls_sorted, cedge_cell = argsort(edge_class, max(n_classes, 1))
+    _, cedge_win = argsort(gather_i64(edge_class, worder), max(n_classes, 1))
+    cls_ptr = csr(cls_sorted, n_classes)
+    return CellTables(covered, cell_ptr, edge_window, edge_class, edge_cell, win_ptr, gather_i64(edge_cell, worder),
+                      gather_i64(edge_class, worder), win_sorted, cls_ptr, cedge_cell, cedge_win)
+
+
+def edge_tables(src, dst, cls, covered_destinations, n_sources, n_destinations, n_classes,
+                uncovered_only) -> CellTables:
+    """cell_nodes.py:23-94 on the device; bit-exact with the reference."""
+    if not (src.shape == dst.shape == cls.shape) or src.ndim != 1:
+        raise ValueError("src, dst, and cls must be one-dimensional and one length")
+    _cuda(src, dst, cls, covered_destinations)
+    if src.numel():
+        if int(src.min()) < 0 or int(src.max()) >= n_sources:
+            raise ValueError(f"src entries must lie in [0, {n_sources})")
+        if int(dst.min()) < 0 or int(dst.max()) >= n_destinations:
+            raise ValueError(f"dst entries must lie in [0, {n_destinations})")
+        if int(cls.min()) < 0 or int(cls.max()) >= n_classes:
+            raise ValueError(f"cls entries must lie in [0, {n_classes})")
+    if uncovered_only:
+        keep = ~torch.isin(dst, covered_destinations)
+        src, dst, cls = src[keep], dst[keep], cls[keep]
+    dst_sorted, order = argsort(dst, max(n_destinations, 1))
+    edge_src = gather_i64(src, order)
+    edge_class = gather_i64(cls, order)
+    covered = torch.unique_consecutive(dst_sorted)
+    dst_ptr = csr(dst_sorted, n_destinations)
+    src_sorted, sorder = argsort(edge_src, max(n_sources, 1))
+    src_ptr = csr(src_sorted, n_sources)
+    edge_sclass = gather_i64(edge_class, sorder)
+    cls_sorted, cedge_dst = argsort(edge_class, max(n_classes, 1))
+    _, cedge_src = argsort(edge_sclass, max(n_classes, 1))
+    cls_ptr = csr(cls_sorted, n_classes)
+    return CellTables(covered, dst_ptr, edge_src, edge_class, dst_sorted, src_ptr, gather_i64(dst_sorted, sorder),
+                      edge_sclass, src_sorted, cls_ptr, cedge_dst, cedge_src)
+
+
+def window_latent_layout(window_pos, positions):
+    """window_latents.py:38-56: position CSR offsets and stable order."""
+    if window_pos.ndim != 1:
+        raise ValueError("window_pos must have shape (N_w,)")
+    if positions < 0:
+        raise ValueError("positions must be nonnegative")
+    _cuda(window_pos)
+    if window_pos.numel():
+        lo, hi = int(window_pos.min()), int(window_pos.max())
+        if lo < 0 or hi >= positions:
+            raise ValueError("window_pos entries must be in [0, positions)")
+    sk, order = argsort(window_pos, max(positions, 1))
+    return csr(sk, positions), order
+
+
+def _validate_agg(values, inc_stone, inc_window, run_stone, run_window, n_dest):
+    if values.ndim != 2:
+        raise ValueError("values must have shape (N, H)")
+    idx = (inc_stone, inc_window, run_stone, run_window)
+    if inc_stone.ndim != 1 or any(i.shape != inc_stone.shape for i in idx):
+        raise ValueError("the incidence views must be one length")
+    if any(i.dtype != _I64 for i in idx):
+        raise ValueError("incidence tensors must have dtype int64")
+    if not values.is_floating_point():
+        raise ValueError("values must have floating-point dtype")
+    if n_dest < 0:
+        raise ValueError(f"destination count must be nonnegative, got {n_dest}")
+    _cuda(values, *idx)
+
+
+def aggregate_to_windows(values, inc_stone, inc_window, run_stone, run_window, n_windows):
+    """message_passing.py:283-297: sum stone rows into windows, output in values.dtype."""
+    _validate_agg(values, inc_stone, inc_window, run_stone, run_window, n_windows)
+    return run_reduce(values.contiguous(), inc_stone, csr(inc_window, n_windows), n_windows, out_dtype=values.dtype)
+
+
+def aggregate_to_stones(values, inc_stone, inc_window, run_stone, run_window, n_stones):
+    """message_passing.py:300-320: sum window rows into stones, fp32."""
+    _validate_agg(values, inc_stone, inc_window, run_stone, run_window, n_stones)
+    return run_reduce(values.contiguous(), run_window, csr(run_stone, n_stones), n_stones, out_dtype=torch.float32)
+
+
+def class_row_sum(weight, gather, runs, n_dest, run_len=18):
+    """message_passing.py:444-458: fp32 class-row sums per destination run."""
+    if gather.ndim != 1 or gather.shape != runs.shape:
+        raise ValueError("the incidence views must be one-dimensional and one length")
+    if gather.dtype != _I64 or runs.dtype != _I64:
+        raise ValueError("incidence tensors must have dtype int64")
+    if n_dest < 0:
+        raise ValueError(f"destination count must be nonnegative, got {n_dest}")
+    _cuda(weight, gather, runs)
+    w = weight.float().contiguous()
+    return run_reduce(w, gather, csr(runs, n_dest), n_dest, out_dtype=torch.float32)
+
+
+def incidence_row_sum(values, gather, runs, rev_gather, rev_runs, n_dest, run_len=18, rev_run_len=6):
+    """message_passing.py:461-484 (forward): fp32 row sums per destination."""
+    views = (gather, runs, rev_gather, rev_runs)
+    if gather.ndim != 1 or any(v.shape != gather.shape for v in views):
+        raise ValueError("the incidence views must be one-dimensional and one length")
+    if any(v.dtype != _I64 for v in views):
+        raise ValueError("incidence tensors must have dtype int64")
+    _cuda(values, *views)
+    return run_reduce(values.contiguous(), gather, csr(runs, n_dest), n_dest, out_dtype=torch.float32)
+
+
+def _validate_cell_attention(q, k, v, bias, seg_ptr, src, cls, qid, sseg_ptr, sqid, scls):
+    if q.ndim != 3 or k.shape != v.shape or q.shape[1:] != k.shape[1:]:
+        raise ValueError("q and k/v must share (heads, head_dim)")
+    if bias.ndim != 2 or bias.shape[0] != q.shape[1]:
+        raise ValueError("bias must have shape (heads, classes)")
+    if seg_ptr.numel() != q.shape[0] + 1:
+        raise ValueError("seg_ptr must have one entry per query row plus one")
+    if sseg_ptr.numel() != k.shape[0] + 1:
+        raise ValueError("sseg_ptr must have one entry per source row plus one")
+    if any(t.shape != src.shape for t in (cls, qid, sqid, scls)) or src.ndim != 1:
+        raise ValueError("the edge views must have one length")
+    _cuda(q, k, v, bias, seg_ptr, src, cls)
+
+
+def cell_attention(q, k, v, bias, vcls, seg_ptr, src, cls, qid, sseg_ptr, sqid, scls, cptr, cedge_q):
+    """cell_latents.py:834-856: (out fp32 (n_q, A, d), m, l)."""
+    _validate_cell_attention(q, k, v, bias, seg_ptr, src, cls, qid, sseg_ptr, sqid, scls)
+    if vcls.shape != (bias.shape[1], q.shape[1] * q.shape[2]):
+        raise ValueError("vcls must have shape (classes, heads * head_dim)")
+    out, m, l = segment_attention(q.contiguous(), k.contiguous(), v.contiguous(), bias, vcls, seg_ptr, src, cls,
+                                  stats=True)
+    return out.view(q.shape), m, l
+
+
+def cell_attention_plain(q, k, v, bias, seg_ptr, src, cls, qid, sseg_ptr, sqid, scls, cptr, cedge_q):
+    """cell_latents.py:922-940: score bias only."""
+    _validate_cell_attention(q, k, v, bias, seg_ptr, src, cls, qid, sseg_ptr, sqid, scls)
+    out, m, l = segment_attention(q.contiguous(), k.contiguous(), v.contiguous(), bias, None, seg_ptr, src, cls,
+                                  stats=True)
+    return out.view(q.shape), m, l
+
+
+def read_attention(q, k, v, window_pos, offsets, order):
+    """window_latents.py:717-720: (P, 4, A, d) latent queries over windows, fp32."""
+    if q.ndim != 4 or q.shape[1] != 4:
+        raise ValueError("read q must have shape (P, 4, heads, head_dim)")
+    if k.ndim != 3 or k.shape != v.shape or q.shape[2:] != k.shape[1:]:
+        raise ValueError("read q, k, and v must share heads and head_dim")
+    _cuda(q, k, v, offsets, order)
+    p, _, heads, hd = q.shape
+    out = latent_read(q.reshape(p * 4, -1).contiguous(), k.reshape(k.shape[0], -1).contiguous(),
+                      v.reshape(v.shape[0], -1).contiguous(), heads, offsets, order)
+    return out.view(q.shape)
+
+
+def broadcast_attention(q, k, v, window_pos, offsets, order):
+    """window_latents.py:723-726: windows over their position's 4 latents, fp32."""
+    if q.ndim != 3 or k.ndim != 4 or k.shape != v.shape or k.shape[1] != 4 or q.shape[1:] != k.shape[2:]:
+        raise ValueError("broadcast q (N_w, A, d) and k/v (P, 4, A, d) shapes disagree")
+    _cuda(q, k, v, window_pos)
+    n_w, heads, hd = q.shape
+    out = latent_broadcast(q.reshape(n_w, -1).contiguous(), k.reshape(-1, heads * hd).contiguous(),
+                           v.reshape(-1, heads * hd).contiguous(), heads, window_pos, k.shape[0])
+    return out.view(q.shape)
+
+
+def encode_rows(pre_w, table, edge_window, edge_class, edge_cell, edge_rev, n_cells):
+    """row_encoder.py:416-447: fp32 sum of relu(pre_w[window] + table[class]) per cell."""
+    views = (edge_window, edge_class, edge_cell, edge_rev)
+    if any(v.shape != edge_window.shape for v in views) or edge_window.ndim != 1:
+        raise ValueError("edge views must be one-dimensional and one length")
+    _cuda(pre_w, table, *views)
+    return row_encode(pre_w.contiguous(), table.float().contiguous(), edge_window, edge_class,
+                      csr(edge_cell, n_cells), n_cells)
+
+
+def cell_pass(x, emb, cell_ptr, edge_window, edge_class, win_ptr, edge_wcell, cls_ptr, edge_ccell):
+    """relay.py:577-591: the (N_w, H) window aggregate, in x's dtype."""
+    _cuda(x, emb, cell_ptr, edge_window, edge_class, win_ptr, edge_wcell)
+    n_cov = cell_ptr.numel() - 1
+    h = x.shape[1]
+    x = x.contiguous()
+    out = torch.empty_like(x)
+    scratch = torch.empty(max(n_cov, 1), h, dtype=torch.float32, device=x.device)
+    e = emb.float().contiguous()
+    call("mb_cell_pass", ptr(x), dtype_code(x.dtype), x.shape[0], ptr(e), e.shape[0], ptr(cell_ptr), n_cov,
+         ptr(edge_window), ptr(edge_class), ptr(win_ptr), ptr(edge_wcell), h, ptr(scratch), ptr(out),
+         dtype_code(out.dtype), stream_of(x.device))
+    return out
+
+
+def fused_attention(q, k, v, seq_lens):
+    """attention.py:892-904: block-diagonal attention over (P, A, T, D)
+    (strided views allowed, inner stride 1); keys >= seq_lens[p] masked, pad
+    query rows zero. Output preserves q's strides like ``empty_like``."""
+    if q.ndim != 4 or q.shape != k.shape or q.shape != v.shape:
+        raise ValueError("q, k, and v must have the same (P, A, T, D) shape")
+    p, heads, t, d = q.shape
+    if seq_lens.shape != (p,) or seq_lens.dtype != torch.int32:
+        raise ValueError("seq_lens must be int32 with shape (P,)")
+    if k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("q, k, and v must have one dtype")
+    _cuda(q, k, v, seq_lens)
+    if not (q.stride() == k.stride() == v.stride()) or q.stride(3) != 1:
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    out = torch.empty_like(q)
+    sp, sa, st, _ = q.stride()
+    op, oa, ot, _ = out.stride()
+    call("mb_stone_attention", ptr(q), ptr(k), ptr(v), dtype_code(q.dtype), p, heads, d, sp, sa, st,
+         ptr(seq_lens.contiguous()), t, None, 0, -1, ptr(out), dtype_code(out.dtype), op, oa, ot,
+         stream_of(q.device))
+    return out

@@ -1,0 +1,213 @@
+/*
+ * mantis_b200.h — C ABI of the B200-native MantisNet evaluator kernels.
+ *
+ * Every entry point takes caller-owned DEVICE pointers, sizes and a CUDA
+ * stream (cudaStream_t passed as void*), launches asynchronously on that
+ * stream, allocates nothing, and returns an mb_status. Host-side argument
+ * validation happens before any launch; a failing check returns
+ * MB_INVALID_ARGUMENT and mb_last_error() describes it. Index values are
+ * validated inside the kernels: an out-of-range index skips the access and
+ * records a code in the device error word, read with mb_device_error().
+ *
+ * dtype codes: MB_F32 = 0, MB_BF16 = 1. Index arrays are int64 (the
+ * reference's torch.long) unless the name says i32. Row-major matrices take a
+ * leading dimension `ld*` in elements.
+ *
+ * Each declaration names the reference interface it replaces, by path inside
+ * the reference project (Cmiller132/Hexo-Shrimp-Bot).
+ */
+#ifndef MANTIS_B200_H
+#define MANTIS_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  MB_OK = 0,
+  MB_INVALID_ARGUMENT = 1,
+  MB_LAUNCH_FAILED = 2,
+  MB_TIMEOUT = 3,
+  MB_UNSUPPORTED = 4,
+  MB_DEVICE_ERROR = 5
+} mb_status;
+
+enum { MB_F32 = 0, MB_BF16 = 1 };
+
+/* Library identity and diagnostics. */
+int mb_version(void);
+const char* mb_last_error(void);
+/* Copies and optionally clears the device error word (synchronises `stream`). */
+int mb_device_error(void* stream, uint32_t* code, int clear);
+
+/* ---------------------------------------------------------------- tables --
+ * Integer CSR derivations, bit-exact with the reference's torch.argsort(
+ * stable=True) / torch.searchsorted(left) compositions.
+ */
+
+/* ptr[d] = first e with keys[e] >= d for d in [0, n_dest]; keys sorted,
+ * in [0, n_dest). Replaces torch.searchsorted(sorted, arange(n+1)) at
+ * python/mantisnet/mantisnet/cell_latents.py:146-160, cell_nodes.py:63-72,
+ * window_latents.py:52-55. */
+int mb_csr_from_sorted(const int64_t* keys, int64_t n, int64_t n_dest, int64_t* ptr, void* stream);
+
+/* Stable argsort of non-negative int64 keys < 2^key_bits (LSD radix).
+ * order[i] = index of the i-th smallest key, ties in input order; also writes
+ * the sorted keys. Workspace size from mb_argsort_workspace. Replaces
+ * torch.argsort(stable=True) at message_passing.py:511, cell_latents.py:133,148,
+ * cell_nodes.py:60-70, window_latents.py:52. */
+int mb_argsort_workspace(int64_t n, int key_bits, int64_t* bytes);
+int mb_argsort(const int64_t* keys, int64_t n, int key_bits, int64_t* sorted_keys, int64_t* order,
+               void* workspace, int64_t workspace_bytes, void* stream);
+
+/* out[i] = src[idx[i]] for int64 arrays (index_select on the edge views). */
+int mb_gather_i64(const int64_t* src, int64_t n_src, const int64_t* idx, int64_t n, int64_t* out, void* stream);
+
+/* Radius class orbit + 48 * (own + 2 * on_axis), gathered through `order`
+ * (order may be NULL for identity). model.py:867-869. */
+int mb_radius_class(const int64_t* orbit, const int64_t* own, const int64_t* on_axis, const int64_t* order,
+                    int64_t n, int64_t* out, void* stream);
+
+/* window_pos[i] = window_slot[i] / max_w (model.py:919). */
+int mb_div_i64(const int64_t* x, int64_t n, int64_t divisor, int64_t* out, void* stream);
+
+/* ------------------------------------------------------- run reductions --
+ * out[d, :] = sum_{e in [ptr[d], ptr[d+1])} values[gather[e], :]  (+ addend)
+ * fp32 accumulation; `values` f32 or bf16, `out` f32 or bf16.
+ * Optional addend: add[(add_idx ? add_idx[d] : d) * ld_add + col] (fp32).
+ * Replaces mantisnet::aggregate_to_windows / aggregate_to_stones /
+ * class_row_sum / incidence_row_sum (message_passing.py:191-227, 344-365;
+ * kernel message_passing.py:40-99). */
+int mb_run_reduce(const void* values, int values_dtype, int64_t ld_values, int64_t n_values,
+                  const int64_t* gather, const int64_t* ptr, int64_t n_dest, int64_t width,
+                  const float* add, int64_t ld_add, const int64_t* add_idx, int64_t n_add,
+                  void* out, int out_dtype, int64_t ld_out, void* stream);
+
+/* Action-row encoder: out[c] = sum_e relu(pre[win[e]] + table[cls[e]])
+ *   + sum_o empty_counts[c, o] * relu(empty_base + table[empty_cls[o]]),
+ * fp32 accumulation, run ptr over cells. Replaces mantisnet::action_row_encode
+ * (row_encoder.py:368-380, 416-447) fused with the EMPTY-row term
+ * (model.py:1049-1057). empty_counts may be NULL. */
+int mb_row_encode(const void* pre, int pre_dtype, int64_t n_pre, const float* table, int64_t n_table,
+                  const int64_t* edge_window, const int64_t* edge_class, const int64_t* cell_ptr, int64_t n_cells,
+                  const int64_t* empty_counts, const float* empty_base, const int64_t* empty_cls, int n_empty,
+                  int64_t h, void* out, int out_dtype, void* stream);
+
+/* Relay cell pass (default config, §5.1b): pre[c] = sum x[w] + emb[cls];
+ * val = relu(pre); out[w] = sum val over the window's cells. `scratch` holds
+ * n_cov * h floats. Replaces mantisnet::cell_pass (relay.py:452-591). */
+int mb_cell_pass(const void* x, int x_dtype, int64_t n_windows, const float* emb, int64_t n_cls,
+                 const int64_t* cell_ptr, int64_t n_cov, const int64_t* edge_window, const int64_t* edge_class,
+                 const int64_t* win_ptr, const int64_t* edge_wcell, int64_t h, float* scratch,
+                 void* out, int out_dtype, void* stream);
+
+/* ------------------------------------------------------------ attention --
+ * Typed segment attention: per query row and head, online softmax over its
+ * CSR run of sources; score = q.k / sqrt(hd) + bias[head, cls]; value =
+ * v[src] (+ vcls[cls] when vcls != NULL). Empty runs (or rows whose
+ * skip_ptr run is non-empty) read zero with m = -inf, l = 0. m/l may be NULL.
+ * Replaces mantisnet::cell_attention and mantisnet::cell_attention_plain
+ * (cell_latents.py:834-940; kernel cell_latents.py:213-285). */
+int mb_segment_attention(const void* q, int64_t ldq, const void* k, const void* v, int64_t ldkv, int dtype,
+                         int64_t n_q, int64_t n_src, int heads, int head_dim,
+                         const float* bias, int64_t n_cls, const float* vcls,
+                         const int64_t* seg_ptr, const int64_t* src, const int64_t* cls, const int64_t* skip_ptr,
+                         void* out, int out_dtype, int64_t ldo, float* m, float* l, void* stream);
+
+/* Block-diagonal stone attention over [4 latents; stones] per position.
+ * Padded mode (tok_off == NULL): q/k/v/out element (p, a, t, d) at
+ * p*s_pos + a*s_head + t*s_row + d, keys t < seq_lens[p] live, query rows
+ * past seq_lens[p] (up to t_pad) written as zeros — mantisnet::fused_attention
+ * (attention.py:719-753, 892-904). Ragged mode: rows of position p are
+ * [tok_off[p], tok_off[p+1]) with head stride s_head and row stride s_row;
+ * only the first `max_queries` rows of each position are queries (4 = the
+ * last block's latent-only read, model.py:647-669; -1 = all). In ragged mode
+ * o_pos > 0 writes position p's rows at p*o_pos (a compact output), else at
+ * the token rows themselves. */
+int mb_stone_attention(const void* q, const void* k, const void* v, int dtype, int64_t n_pos, int heads, int head_dim,
+                       int64_t s_pos, int64_t s_head, int64_t s_row, const int32_t* seq_lens, int64_t t_pad,
+                       const int64_t* tok_off, int64_t max_tokens, int max_queries,
+                       void* out, int out_dtype, int64_t o_pos, int64_t o_head, int64_t o_row, void* stream);
+
+/* Window-latent read: four latent queries per position attend over the
+ * position's windows (order[offsets[p]..offsets[p+1]]). q (P, 4, H), k/v
+ * (N_w, H), out (P, 4, H). m/l (P, 4, heads) may be NULL.
+ * Replaces mantisnet::window_latent_read (window_latents.py:553-600). */
+int mb_window_latent_read(const void* q, int64_t ldq, const void* k, const void* v, int64_t ldkv, int dtype,
+                          int64_t n_pos, int64_t n_windows, int heads, int head_dim, const int64_t* offsets,
+                          const int64_t* order, void* out, int out_dtype, float* m, float* l, void* stream);
+
+/* Window-latent broadcast: each window attends over its position's four
+ * latent slots. q (N_w, H), k/v (P, 4, H), out (N_w, H).
+ * Replaces mantisnet::window_latent_broadcast (window_latents.py:640-714). */
+int mb_window_latent_broadcast(const void* q, int64_t ldq, const void* k, const void* v, int64_t ldkv, int dtype,
+                               int64_t n_pos, int64_t n_windows, int heads, int head_dim, const int64_t* window_pos,
+                               void* out, int out_dtype, float* m, float* l, void* stream);
+
+/* Dense 4x4 latent self-mix per position and head, fp32 softmax
+ * (model.py:516-526). q/k/v/out (P, 4, H). */
+int mb_latent_mix(const void* q, const void* k, const void* v, int64_t ld, int dtype, int64_t n_pos, int heads,
+                  int head_dim, void* out, int out_dtype, void* stream);
+
+/* ------------------------------------------------------- rows and norms -- */
+
+/* LayerNorm over rows of width h (fp32 statistics, eps), input f32 or bf16,
+ * optional row gather in_rows[i] (NULL = identity). torch.nn.LayerNorm as
+ * used throughout model.py. */
+int mb_layer_norm(const void* x, int x_dtype, int64_t ldx, const int64_t* in_rows, int64_t n, int64_t h,
+                  const float* gamma, const float* beta, float eps, void* out, int out_dtype, int64_t ldo,
+                  void* stream);
+
+/* out[i] = ta[ia[i]] + (tb ? tb[ib ? ib[i] : i] : 0): embedding lookups and
+ * their sums (model.py:909-912, 929). fp32 tables and output. */
+int mb_embed(const float* ta, int64_t n_ta, const int64_t* ia, const float* tb, int64_t n_tb, const int64_t* ib,
+             int64_t n, int64_t h, float* out, void* stream);
+
+/* Initial cell state: covered cells (cov_ptr run non-empty) take
+ * `covered_row` (+ optional per-cell addend rows), the rest take
+ * nearest_table[cell_nearest]. model.py:926-935. */
+int mb_cell_init(const int64_t* cov_ptr, const int64_t* cell_nearest, const float* nearest_table, int64_t n_nearest,
+                 const float* covered_row, const float* covered_add, int64_t n_cells, int64_t h, float* out,
+                 void* stream);
+
+/* Residual update: x[row(i)] += y[i]; x and y each f32 or bf16 (row map may
+ * be NULL). */
+int mb_residual_add(void* x, int x_dtype, int64_t ldx, const int64_t* rows, const void* y, int y_dtype, int64_t ldy,
+                    int64_t n, int64_t h, void* stream);
+
+/* x[i] = act(x[i] + t[idx[i]]) with act = relu when relu != 0: the per-position
+ * token half of the decoder MLP joined per legal cell (model.py:1091). */
+int mb_add_gather(void* x, int x_dtype, int64_t ldx, const void* t, int t_dtype, int64_t ldt, int64_t n_t,
+                  const int64_t* idx, int64_t n, int64_t h, int relu, void* stream);
+
+/* Token layout for stone attention: tokens of position p are its 4 latent
+ * rows then its stones. gather: tok = [g; s] per position; scatter-add:
+ * g += tok_out[latent rows], s += tok_out[stone rows] (model.py:622-646). */
+int mb_tokens_gather(const float* g, const float* s, const int64_t* stone_off, const int64_t* tok_off,
+                     int64_t n_pos, int64_t h, float* tok, void* stream);
+int mb_tokens_scatter_add(float* g, float* s, const int64_t* stone_off, const int64_t* tok_off, int64_t n_pos,
+                          int64_t h, const void* tok_out, int dtype, int update_stones, void* stream);
+
+/* Mean of ln(g) over the 4 latent rows: out (P, h) fp32 (model.py:973). */
+int mb_latent_mean(const float* g_ln, int64_t n_pos, int64_t h, float* out, void* stream);
+
+/* Q composition (model.py:177-220, segments.py:24-31): per cell
+ * p = softmax(critic[c, 0:3]); q_values = p0 - p1;
+ * q_score = q_values / max(max over the position's cells of (p0 + p1), floor). */
+int mb_compose_q(const float* critic, int64_t ld_critic, const int64_t* offsets, int64_t n_pos, float mass_floor,
+                 float* q_score, float* q_values, void* stream);
+
+/* ------------------------------------------------------------- GEMM ------
+ * out = act(A @ W^T + bias) (+ residual) for row-major A (M, K), W (N, K).
+ * Replaces the nn.Linear calls of model.py (the reference runs them through
+ * cuBLAS under autocast). */
+int mb_linear(const void* a, int a_dtype, int64_t lda, int64_t m, int64_t k, const void* w, int w_dtype,
+              const float* bias, int64_t n, int relu, void* out, int out_dtype, int64_t ldo, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MANTIS_B200_H */

@@ -1,0 +1,235 @@
+"""Op-level parity of the CUDA kernels (through the C ABI) against the CPU
+oracle, on seeded inputs and the reference's op fixtures (tests/golden/ops.npz).
+
+Tolerances: fp32 inputs 1e-5 abs / 1e-5 rel (fp32 math, different summation
+order); bf16 inputs are compared against the oracle run on the same
+bf16-rounded values, so the only differences are fp32 accumulation order:
+2e-5 abs. Integer tables are bit-exact.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+import golden_io
+from golden_io import mb
+from oracle import forward as O
+
+pytestmark = pytest.mark.gpu
+ops = mb.ops
+DEV = "cuda"
+
+
+def _fx():
+    d = golden_io.load("ops.npz")
+    return {k: torch.from_numpy(d[k]) for k in d.files}
+
+
+def test_fused_attention_matches_reference_fixture():
+    t = _fx()
+    q, k, v, seq = (t[x].to(DEV) for x in ("att.q", "att.k", "att.v", "att.seq_lens"))
+    out = ops.fused_attention(q, k, v, seq)
+    torch.testing.assert_close(out.cpu(), t["att.out"], rtol=1e-5, atol=1e-5)
+    # pad query rows are exactly zero (reference test_attention_kernel.py:202-228)
+    assert torch.count_nonzero(out[2, :, 4:]) == 0
+
+
+@pytest.mark.parametrize("d", [16, 32, 64])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_fused_attention_strided_ragged(d, dtype):
+    """(P, T, A, D) storage viewed as (P, A, T, D), ragged seq_lens — the
+    model's call pattern (model.py:633-640) on the reference's shape grid."""
+    g = torch.Generator().manual_seed(d)
+    for p, t in ((1, 2), (3, 65), (5, 200)):
+        base = torch.randn(3, p, t, 2, d, generator=g).to(dtype)
+        q, k, v = (base[i].to(DEV).transpose(1, 2) for i in range(3))
+        seq = torch.randint(1, t + 1, (p,), generator=g, dtype=torch.int32)
+        seq[0] = t
+        out = ops.fused_attention(q, k, v, seq.to(DEV))
+        assert out.stride() == q.stride()
+        want = O.stone_attention(q.float().cpu(), k.float().cpu(), v.float().cpu(), seq.long())
+        torch.testing.assert_close(out.float().cpu(), want, rtol=2e-2 if dtype == torch.bfloat16 else 1e-5,
+                                   atol=2e-2 if dtype == torch.bfloat16 else 1e-5)
+
+
+def test_segment_attention_matches_reference_fixture():
+    t = _fx()
+    qid, src, cls = t["seg.qid"], t["seg.src"], t["seg.cls"]
+    n_q = t["seg.q"].shape[0]
+    seg_ptr = torch.searchsorted(qid, torch.arange(n_q + 1))
+    args = [x.to(DEV) for x in (t["seg.q"], t["seg.k"], t["seg.v"], t["seg.bias"])]
+    out = ops.segment_attention(*args, t["seg.vcls"].to(DEV), seg_ptr.to(DEV), src.to(DEV), cls.to(DEV))
+    torch.testing.assert_close(out.view(n_q, -1, t["seg.q"].shape[2]).cpu(), t["seg.out"], rtol=1e-5, atol=1e-5)
+    plain = ops.segment_attention(*args, None, seg_ptr.to(DEV), src.to(DEV), cls.to(DEV))
+    torch.testing.assert_close(plain.view(n_q, -1, t["seg.q"].shape[2]).cpu(), t["seg.out_plain"], rtol=1e-5,
+                               atol=1e-5)
+    assert torch.count_nonzero(out[2]) == 0
+
+
+@pytest.mark.parametrize("heads,hd", [(2, 16), (4, 32), (8, 32), (2, 32)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_segment_attention_random_runs(heads, hd, dtype):
+    g = torch.Generator().manual_seed(heads * 100 + hd)
+    n_q, n_src, n_cls = 300, 90, 37
+    runs = torch.randint(0, 19, (n_q,), generator=g)
+    runs[::7] = 0  # empty runs
+    qid = torch.repeat_interleave(torch.arange(n_q), runs)
+    e = qid.numel()
+    src = torch.randint(0, n_src, (e,), generator=g)
+    cls = torch.randint(0, n_cls, (e,), generator=g)
+    q = torch.randn(n_q, heads, hd, generator=g).to(dtype)
+    k = torch.randn(n_src, heads, hd, generator=g).to(dtype)
+    v = torch.randn(n_src, heads, hd, generator=g).to(dtype)
+    bias = torch.randn(heads, n_cls, generator=g)
+    vcls = torch.randn(n_cls, heads * hd, generator=g)
+    seg_ptr = torch.cat([torch.zeros(1, dtype=torch.long), runs.cumsum(0)])
+    out, m, l = ops.segment_attention(q.to(DEV), k.to(DEV), v.to(DEV), bias.to(DEV), vcls.to(DEV), seg_ptr.to(DEV),
+                                      src.to(DEV), cls.to(DEV), stats=True)
+    want = O.segment_attention(q.float(), k.float(), v.float(), bias, vcls, src, cls, qid)
+    torch.testing.assert_close(out.view(n_q, heads, hd).cpu(), want, rtol=1e-5, atol=2e-5)
+    empty = runs == 0
+    assert torch.all(l.cpu()[empty] == 0) and torch.all(torch.isinf(m.cpu()[empty]))
+    # skip_ptr: rows whose skip run is non-empty read zero
+    skip = torch.cat([torch.zeros(1, dtype=torch.long), (torch.arange(n_q) % 3 == 0).long().cumsum(0)])
+    out2 = ops.segment_attention(q.to(DEV), k.to(DEV), v.to(DEV), bias.to(DEV), vcls.to(DEV), seg_ptr.to(DEV),
+                                 src.to(DEV), cls.to(DEV), skip_ptr=skip.to(DEV))
+    masked = (torch.arange(n_q) % 3 == 0)
+    assert torch.count_nonzero(out2.cpu()[masked]) == 0
+    torch.testing.assert_close(out2.cpu()[~masked], out.cpu()[~masked])
+
+
+def test_segment_attention_bad_index_is_reported_not_faulted():
+    q = torch.randn(2, 1, 32, device=DEV)
+    k = torch.randn(3, 1, 32, device=DEV)
+    bias = torch.zeros(1, 4, device=DEV)
+    seg_ptr = torch.tensor([0, 2, 3], device=DEV)
+    src = torch.tensor([0, 7, 1], device=DEV)  # 7 is out of range
+    cls = torch.tensor([0, 1, 2], device=DEV)
+    mb._lib.check_device_error()  # clear
+    ops.segment_attention(q, k, k, bias, None, seg_ptr, src, cls)
+    with pytest.raises(ValueError, match="out of range"):
+        mb._lib.check_device_error()
+    mb._lib.check_device_error()  # cleared
+
+
+def test_window_latents_match_reference_fixture():
+    t = _fx()
+    pos = t["win.pos"].to(DEV)
+    offsets, order = ops.window_latent_layout(pos, 4)
+    rd = ops.read_attention(t["win.rq"].to(DEV), t["win.rk"].to(DEV), t["win.rv"].to(DEV), pos, offsets, order)
+    torch.testing.assert_close(rd.cpu(), t["win.read"], rtol=1e-5, atol=1e-5)
+    assert torch.count_nonzero(rd[1]) == 0
+    bc = ops.broadcast_attention(t["win.bq"].to(DEV), t["win.bk"].to(DEV), t["win.bv"].to(DEV), pos, offsets, order)
+    torch.testing.assert_close(bc.cpu(), t["win.bcast"], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("heads,hd", [(4, 32), (8, 32), (2, 16)])
+def test_window_latents_random(heads, hd):
+    g = torch.Generator().manual_seed(hd + heads)
+    p = 7
+    counts = torch.tensor([0, 1, 40, 300, 5, 1000, 33])
+    pos = torch.repeat_interleave(torch.arange(p), counts)
+    nw = pos.numel()
+    q = torch.randn(p, 4, heads, hd, generator=g)
+    k = torch.randn(nw, heads, hd, generator=g)
+    v = torch.randn(nw, heads, hd, generator=g)
+    offsets, order = ops.window_latent_layout(pos.to(DEV), p)
+    rd = ops.read_attention(q.to(DEV), k.to(DEV), v.to(DEV), pos.to(DEV), offsets, order)
+    torch.testing.assert_close(rd.cpu(), O.window_read(q, k, v, pos), rtol=1e-5, atol=2e-5)
+    bq = torch.randn(nw, heads, hd, generator=g)
+    bc = ops.broadcast_attention(bq.to(DEV), q.to(DEV), k[:p * 4].reshape(p, 4, heads, hd).to(DEV), pos.to(DEV),
+                                 offsets, order)
+    torch.testing.assert_close(bc.cpu(), O.window_broadcast(bq, q, k[:p * 4].reshape(p, 4, heads, hd), pos),
+                               rtol=1e-5, atol=2e-5)
+
+
+def test_row_encoder_matches_reference_fixture():
+    t = _fx()
+    out = ops.encode_rows(*(t[x].to(DEV) for x in ("row.pre", "row.table", "row.win", "row.cls", "row.cell")),
+                          t["row.cell"].to(DEV), 5)
+    torch.testing.assert_close(out.cpu(), t["row.out"], rtol=1e-5, atol=1e-5)
+
+
+def test_run_reductions_against_oracle():
+    g = torch.Generator().manual_seed(3)
+    n_src, n_dest, h = 50, 40, 256
+    runs = torch.randint(0, 7, (n_dest,), generator=g)
+    dest = torch.repeat_interleave(torch.arange(n_dest), runs)
+    gather = torch.randint(0, n_src, (dest.numel(),), generator=g)
+    vals = torch.randn(n_src, h, generator=g)
+    for dtype in (torch.float32, torch.bfloat16):
+        x = vals.to(dtype)
+        want = O.row_sum(x.float(), gather, dest, n_dest)
+        got = ops.class_row_sum(x.to(DEV), gather.to(DEV), dest.to(DEV), n_dest)
+        torch.testing.assert_close(got.cpu(), want, rtol=1e-5, atol=1e-5)
+        got = ops.aggregate_to_windows(x.to(DEV), gather.to(DEV), dest.to(DEV), dest.to(DEV), gather.to(DEV), n_dest)
+        assert got.dtype == dtype
+        torch.testing.assert_close(got.float().cpu(), want.to(dtype).float(), rtol=1e-2, atol=1e-2)
+
+
+def test_cell_pass_against_oracle():
+    cfg, P, batch, _, _ = golden_io.forward_case("default")
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(batch.n_windows, 32, generator=g)
+    emb = torch.randn(726, 32, generator=g)
+    b = batch.to(DEV)
+    got = ops.cell_pass(x.to(DEV), emb.to(DEV), b.relay_cell_ptr, b.relay_window, b.relay_class, b.relay_win_ptr,
+                        b.relay_wcell, b.relay_cls_ptr, b.relay_ccell)
+    want = O.cell_pass(x, emb, batch.dec_cell, batch.dec_window, batch.dec_class)
+    torch.testing.assert_close(got.cpu(), want, rtol=1e-5, atol=1e-4)
+
+
+@pytest.mark.parametrize("name", ["cellnodes", "full", "uncovered"])
+def test_integer_tables_bit_exact(name):
+    """Device CSR derivations equal the reference's torch compositions."""
+    cfg, P, batch, _, _ = golden_io.forward_case(name)
+    b = batch.to(DEV)
+    n_w, n_c, n_s = batch.n_windows, batch.n_cells, batch.n_stones
+    for n_cells in (n_c, -1):
+        got = ops.cell_tables(b.dec_cell, b.dec_window, b.dec_class, n_w, 726, n_cells)
+        want = O.cell_tables(batch.dec_cell, batch.dec_window, batch.dec_class, n_w, n_cells)
+        for k in ("covered", "cell_ptr", "edge_window", "edge_class", "edge_cell", "win_ptr", "edge_wcell",
+                  "edge_wclass", "edge_wwin"):
+            assert torch.equal(getattr(got, k).cpu(), want[k]), k
+    cov = O.cell_tables(batch.dec_cell, batch.dec_window, batch.dec_class, n_w, n_c)["covered"]
+    rcls = batch.radius_orbit + 48 * (batch.radius_own + 2 * batch.radius_on_axis)
+    for scope in (False, True):
+        got = ops.edge_tables(b.radius_src, b.radius_dst, rcls.to(DEV), cov.to(DEV), n_s, n_c, 192, scope)
+        want = O.edge_tables(batch.radius_src, batch.radius_dst, rcls, cov, n_s, n_c, scope)
+        pairs = dict(cell_ptr="dst_ptr", edge_window="edge_src", edge_class="edge_class", edge_cell="edge_dst",
+                     win_ptr="src_ptr", edge_wcell="edge_sdst", edge_wclass="edge_sclass", edge_wwin="edge_ssrc")
+        for k, kw in pairs.items():
+            assert torch.equal(getattr(got, k).cpu(), want[kw]), (scope, k)
+    plan = ops.incidence_plan(b.inc_stone, b.inc_window, b.inc_class)
+    want = O.incidence_plan(batch.inc_stone, batch.inc_window, batch.inc_class)
+    for a_, b_ in zip(plan, want):
+        assert torch.equal(a_.cpu(), b_)
+    pos = batch.window_slot // batch.value_valid.shape[1]
+    off, order = ops.window_latent_layout(pos.to(DEV), batch.n_pos)
+    woff, worder = O.window_latent_layout(pos, batch.n_pos)
+    assert torch.equal(off.cpu(), woff) and torch.equal(order.cpu(), worder)
+
+
+def test_layer_norm_and_compose():
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(333, 256, generator=g) * 3 + 1
+    gam, bet = torch.randn(256, generator=g), torch.randn(256, generator=g)
+    got = ops.layer_norm(x.to(DEV), gam.to(DEV), bet.to(DEV), out_dtype=torch.float32)
+    torch.testing.assert_close(got.cpu(), torch.nn.functional.layer_norm(x, (256,), gam, bet), rtol=1e-5, atol=1e-5)
+    critic = torch.randn(100, 3, generator=g) * 2
+    offs = torch.tensor([0, 1, 40, 100])
+    qs, qv = ops.compose(critic.to(DEV), offs.to(DEV), 0.2)
+    torch.testing.assert_close(qv.cpu(), O.compose_q(critic), rtol=1e-6, atol=1e-6)
+    torch.testing.assert_close(qs.cpu(), O.compose_acting_q(critic, offs, 0.2), rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_native_linear(dtype):
+    g = torch.Generator().manual_seed(1)
+    a = torch.randn(1000, 96, generator=g).to(dtype)
+    w = torch.randn(80, 96, generator=g).to(dtype)
+    b = torch.randn(80, generator=g)
+    got = ops.linear_native(a.to(DEV), w.to(DEV), b.to(DEV), relu=True, out_dtype=torch.float32)
+    want = torch.relu(a.float() @ w.float().t() + b)
+    torch.testing.assert_close(got.cpu(), want, rtol=1e-4, atol=1e-4)
