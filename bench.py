@@ -1,0 +1,390 @@
+#!/usr/bin/env python
+"""Benchmark: MantisNet evaluator positions/s (bf16, B=4096 per GPU) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the metric's own configuration; it fits one
+GPU in chunks): per GPU, B=4096 late-game positions of 150-300 stones from
+seeded uniform-random legal play, evaluated by the config-4 architecture
+(h=256, 8 blocks, 8 heads, F=4, cell_latents + cell_nodes, the production
+knobs) with random weights (std 0.02), bf16. A step is one pass of the
+evaluator forward over the 4096 positions, processed as chunks of ``--chunk``
+positions (the reference's cell-budget chunking). Positions are independent:
+N GPUs evaluate N x 4096 positions with no collective (weak scaling); the
+only cross-rank traffic is the timing barrier and the max-over-ranks reduce.
+
+Printed JSON line keys follow the driver contract; ``value`` is device-resident
+throughput (inputs already in HBM), ``e2e`` the same metric through the
+reference-facing evaluator call (host batch, H2D + D2H inside the timed
+region), ``roofline`` the dominant native kernel, ``cpu_baseline`` the CPU
+oracle port of the reference forward on a bounded sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from concurrent.futures import ProcessPoolExecutor
+from multiprocessing import get_context
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+ARCH = dict(h=256, blocks=8, heads=8, ffn_factor=4, cell_latents=True, cell_nodes=True)
+METRIC = "positions/sec evaluated (bf16, B=4096) at 1/2/4/8 B200; p50 batch-64 latency"
+
+
+def _pkg():
+    import importlib
+
+    return importlib.import_module("hexo-shrimp-bot_b200")
+
+
+def _build_graph(spec):
+    return _pkg().from_spec(spec)
+
+
+def make_specs(n, lo, hi, seed):
+    return _pkg().engine.random_positions(n, lo, hi, seed=seed)
+
+
+def build_graphs(specs, workers):
+    if workers <= 1 or len(specs) < 16:
+        return [_build_graph(s) for s in specs]
+    with ProcessPoolExecutor(max_workers=workers, mp_context=get_context("spawn")) as ex:
+        return list(ex.map(_build_graph, specs, chunksize=max(1, len(specs) // (4 * workers))))
+
+
+def batch_bytes(batch, fields):
+    import torch
+
+    return sum(getattr(batch, f).numel() * getattr(batch, f).element_size() for f in fields
+               if isinstance(getattr(batch, f), torch.Tensor))
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def peaks():
+    try:
+        return json.loads((REPO / "MEASURED_PEAKS.json").read_text()), "measured"
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# --------------------------------------------------------------- CPU side
+
+def cpu_forward_rate(specs, sample, threads):
+    """The CPU oracle (restatement of the reference's eager fp32 forward) on
+    ``sample`` positions: positions/s with ``threads`` torch threads."""
+    import torch
+
+    from oracle import forward as O
+
+    mb = _pkg()
+    torch.set_num_threads(threads)
+    cfg = mb.MantisConfig(**ARCH)
+    torch.manual_seed(0)
+    net = mb.MantisNet(cfg)
+    params = {k: v.detach().clone() for k, v in net.state_dict().items()}
+    c = O.Cfg(**{k: v for k, v in cfg.to_dict().items() if k != "dropout"})
+    batch = mb.collate([mb.from_spec(s) for s in specs[:sample]])
+    O.forward(c, params, mb.collate([mb.from_spec(specs[0])]), 0.2, value=False)  # warm
+    t0 = time.perf_counter()
+    O.forward(c, params, batch, 0.2, value=False)
+    dt = time.perf_counter() - t0
+    return sample / dt, dt
+
+
+def run_reference(args, rank):
+    """The reference arm: the CPU restatement of the reference's forward on
+    the host cores (the reference is Python; its CPU path is eager torch)."""
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    specs = make_specs(max(args.ref_sample, 1), args.lo, args.hi, seed=1234)
+    rates = []
+    for i in range(args.warmup + args.steps):
+        r, _ = cpu_forward_rate(specs, args.ref_sample, threads)
+        if i >= args.warmup:
+            rates.append(r)
+    v = statistics.median(rates)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "positions/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * args.ref_sample / v,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.ref_sample} late positions ({args.lo}-{args.hi} stones) per step, "
+                               "config-4 architecture (h256/8 blocks/8 heads/F4, cell_latents+cell_nodes)",
+                   "positions_per_step": args.ref_sample},
+        "cpu_baseline": {"value": v, "unit": "positions/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.ref_sample} positions per step, fp32 eager torch-CPU oracle"},
+        "e2e": {"value": v, "unit": "positions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------- GPU side
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    mb = _pkg()
+    ops = mb.ops
+    lib = mb._lib
+    lib.load()
+
+    # Inputs: build on the host before touching the GPU.
+    n_chunks = math.ceil(args.positions / args.chunk)
+    specs = make_specs(args.unique, args.lo, args.hi, seed=1000 + rank)
+    workers = min(32, os.cpu_count() or 1)
+    graphs = build_graphs(specs, workers)
+    reps = math.ceil(args.chunk / len(graphs))
+    chunk_graphs = (graphs * reps)[: args.chunk]
+    host = mb.collate(chunk_graphs)
+    fields = mb.evaluator.needed_fields(mb.MantisConfig(**ARCH))
+    host_pinned = host.pin_memory()
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device, timeout=__import__("datetime").timedelta(seconds=600))
+
+    cfg = mb.MantisConfig(**ARCH)
+    torch.manual_seed(0)
+    net = mb.MantisNet(cfg)
+    with torch.no_grad():
+        for head in (net.mlp_p, net.mlp_q):
+            head.out.weight.normal_(std=0.02)
+            head.out.bias.normal_(std=0.02)
+    net = net.to(device).eval()
+    eng = net.engine(torch.bfloat16)
+    dev_batch = mb.evaluator.to_device(host, device, fields)
+    torch.cuda.synchronize()
+
+    def step_device():
+        for _ in range(n_chunks):
+            w, g, cells = eng.trunk(dev_batch)
+            policy, critic = eng.heads(w, g, cells, dev_batch)
+            ops.compose(critic, dev_batch.legal_offsets, 0.2)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step_device()
+    barrier()
+    calls0 = lib.call_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        start.record()
+        for _ in range(args.steps):
+            step_device()
+        end.record()
+        torch.cuda.synchronize()
+    launches = (lib.call_count() - calls0) // max(args.steps, 1)
+    ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+    positions_per_step = n_chunks * args.chunk
+    value = world * positions_per_step / (ms / 1000.0)
+
+    # e2e through the evaluator closure (host batch, H2D + D2H per chunk)
+    ev = mb.network_evaluate(net, mb.evaluator.EvaluatorConfig(device=str(device), autocast=True, mass_floor=0.2))
+
+    def step_e2e():
+        for _ in range(n_chunks):
+            ev(host_pinned)
+
+    for _ in range(max(1, args.warmup)):
+        step_e2e()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step_e2e()
+    e1.record()
+    torch.cuda.synchronize()
+    ms_e2e = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    e2e_value = world * positions_per_step / (ms_e2e / 1000.0)
+    h2d = batch_bytes(host, fields) * n_chunks
+    d2h = 3 * host.n_cells * 4 * n_chunks
+
+    # Roofline of the dominant native kernel: the radius read (typed segment
+    # attention cells <- stones), timed alone on this chunk's tables.
+    roof = radius_roofline(eng, dev_batch, cfg, args) if rank == 0 else None
+
+    # p50 batch-64 latency (config-4 distribution: 40-150 stones), end to end
+    p50 = None
+    if rank == 0 and args.latency:
+        lat_specs = make_specs(64, 40, 150, seed=77)
+        lat_batch = mb.collate(build_graphs(lat_specs, workers)).pin_memory()
+        times = []
+        for i in range(3 + 20):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            ev(lat_batch)
+            dt = time.perf_counter() - t0
+            if i >= 3:
+                times.append(dt * 1000.0)
+        p50 = statistics.median(times)
+
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_sample > 0:
+        threads = os.cpu_count() or 1
+        rate, dt = cpu_forward_rate(specs, args.cpu_sample, threads)
+        cpu = {"value": rate, "unit": "positions/s", "cores": threads, "kind": "port",
+               "sample": f"{args.cpu_sample} late positions ({args.lo}-{args.hi} stones), fp32 eager torch-CPU "
+                         f"oracle forward, {dt:.1f} s"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "positions/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {
+                "workload": (f"config 5: {positions_per_step} late positions per GPU ({args.lo}-{args.hi} stones), "
+                             f"{n_chunks} chunks of {args.chunk} ({len(graphs)} distinct seeded positions per rank, "
+                             "repeated to fill a chunk); config-4 architecture"),
+                "arch": ARCH, "positions_per_gpu": positions_per_step, "chunk": args.chunk,
+                "cells_per_chunk": host.n_cells, "windows_per_chunk": host.n_windows,
+                "radius_edges_per_chunk": int(host.radius_src.numel()),
+                "l2": "inputs larger than L2 (one chunk's device tables exceed 126 MB)",
+            },
+            "e2e": {"value": e2e_value, "unit": "positions/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches,
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "clocks": clocks.summary(),
+            "p50_batch64_ms": p50,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def radius_roofline(eng, b, cfg, args):
+    import torch
+
+    mb = _pkg()
+    ops = mb.ops
+    T = mb.model._Tables(cfg, b)
+    h = cfg.h
+    blk = eng.blocks[0]
+    q = torch.randn(T.N_c, h, device=b.stone_own.device).to(torch.bfloat16)
+    kv = torch.randn(T.N_s, 2 * h, device=b.stone_own.device).to(torch.bfloat16)
+    out = torch.empty(T.N_c, h, dtype=torch.bfloat16, device=q.device)
+
+    def launch():
+        ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["radius_bias"], blk["radius_vclass"], T.r_ptr, T.r_src,
+                              T.r_cls, out=out, out_dtype=torch.bfloat16)
+
+    for _ in range(3):
+        launch()
+    torch.cuda.synchronize()
+    n = 20
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        launch()
+    e1.record()
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / n / 1000.0
+    e_r = int(T.r_src.numel())
+    algo = T.N_c * h * 2 * 2 + T.N_s * 2 * h * 2 + e_r * 16 + (T.N_c + 1) * 8 + 192 * h * 4
+    pk, kind = peaks()
+    achieved = algo / sec / 1e9
+    return {"kernel": "segment_attention (radius read, cells<-stones)", "bound": "hbm", "achieved": achieved,
+            "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": None,
+            "peak_kind": kind, "algorithmic_bytes": algo, "launch_ms": sec * 1000.0, "edges": e_r}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--positions", type=int, default=4096)
+    ap.add_argument("--chunk", type=int, default=512)
+    ap.add_argument("--unique", type=int, default=256)
+    ap.add_argument("--lo", type=int, default=150)
+    ap.add_argument("--hi", type=int, default=300)
+    ap.add_argument("--cpu-sample", type=int, default=4)
+    ap.add_argument("--ref-sample", type=int, default=4)
+    ap.add_argument("--latency", type=int, default=1)
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

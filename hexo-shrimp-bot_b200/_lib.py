@@ -80,8 +80,18 @@ def exported_symbols() -> list[str]:
     return list(SIGNATURES)
 
 
+_calls = 0
+
+
+def call_count() -> int:
+    """Native entry-point calls so far (each launches the op's kernels)."""
+    return _calls
+
+
 def call(name: str, *args) -> None:
+    global _calls
     lib = _lib or load()
+    _calls += 1
     status = getattr(lib, name)(*args)
     if status != 0:
         msg = lib.mb_last_error().decode(errors="replace")
