@@ -213,7 +213,7 @@ def run_ours(args, rank, world, local_rank):
             head.out.weight.normal_(std=0.02)
             head.out.bias.normal_(std=0.02)
     net = net.to(device).eval()
-    eng = net.engine(torch.bfloat16)
+    eng = net.engine(torch.bfloat16, gemm=args.gemm)
     dev_batch = mb.evaluator.to_device(host, device, fields)
     torch.cuda.synchronize()
 
@@ -252,7 +252,8 @@ def run_ours(args, rank, world, local_rank):
     value = world * positions_per_step / (ms / 1000.0)
 
     # e2e through the evaluator closure (host batch, H2D + D2H per chunk)
-    ev = mb.network_evaluate(net, mb.evaluator.EvaluatorConfig(device=str(device), autocast=True, mass_floor=0.2))
+    ev = mb.network_evaluate(net, mb.evaluator.EvaluatorConfig(device=str(device), autocast=True, mass_floor=0.2,
+                                                                gemm=args.gemm))
 
     def step_e2e():
         for _ in range(n_chunks):
@@ -308,7 +309,7 @@ def run_ours(args, rank, world, local_rank):
                 "workload": (f"config 5: {positions_per_step} late positions per GPU ({args.lo}-{args.hi} stones), "
                              f"{n_chunks} chunks of {args.chunk} ({len(graphs)} distinct seeded positions per rank, "
                              "repeated to fill a chunk); config-4 architecture"),
-                "arch": ARCH, "positions_per_gpu": positions_per_step, "chunk": args.chunk,
+                "arch": ARCH, "positions_per_gpu": positions_per_step, "chunk": args.chunk, "gemm": args.gemm,
                 "cells_per_chunk": host.n_cells, "windows_per_chunk": host.n_windows,
                 "radius_edges_per_chunk": int(host.radius_src.numel()),
                 "l2": "inputs larger than L2 (one chunk's device tables exceed 126 MB)",
@@ -376,6 +377,7 @@ def main():
     ap.add_argument("--cpu-sample", type=int, default=4)
     ap.add_argument("--ref-sample", type=int, default=4)
     ap.add_argument("--latency", type=int, default=1)
+    ap.add_argument("--gemm", default="cublas", help="dense projection path (see model.Engine)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))

@@ -33,7 +33,7 @@ SIGNATURES = {
     "mb_run_reduce": "pillppllplplpilp",
     "mb_row_encode": "pilplppplpppilpip",
     "mb_cell_pass": "pilplplpppplppip",
-    "mb_segment_attention": "plpplilliiplppppppilppp",
+    "mb_segment_attention": "plpplilliiplpipppppilppp",
     "mb_stone_attention": "pppiliilllplplipilllp",
     "mb_window_latent_read": "plpplilliipppippp",
     "mb_window_latent_broadcast": "plpplilliippippp",
@@ -48,6 +48,8 @@ SIGNATURES = {
     "mb_latent_mean": "pllpp",
     "mb_compose_q": "plplfppp",
     "mb_linear": "pilllpiplipilp",
+    "mb_gemm_weight_image": "pllpp",
+    "mb_gemm_rows": "pillppfppiplplp",
 }
 _CT = {"p": ctypes.c_void_p, "i": ctypes.c_int, "l": ctypes.c_int64, "f": ctypes.c_float}
 

@@ -24,14 +24,22 @@ namespace mb {
 constexpr float kNegInf = -INFINITY;
 
 // ------------------------------------------------------- segment attention
-template <typename T, typename TO, int VEC, bool HAS_VCLS>
-__global__ void __launch_bounds__(256) segment_attention_kernel(
+// One warp per query row, blocks of 8 warps over consecutive rows, scheduled
+// in row order: the GPU works on a narrow band of positions at a time, so the
+// gathered source rows stay L2-resident. Two edges per iteration keep two
+// K/V row pairs in flight per lane at 80 registers (3 blocks per SM); wider
+// per-lane pipelines were measured slower at the bench's sizes because they
+// cost resident warps.
+constexpr int kSegWarps = 8;
+
+template <typename T, typename TO, typename TV, int VEC, bool HAS_VCLS>
+__global__ void __launch_bounds__(kSegWarps * 32) segment_attention_kernel(
     const T* __restrict__ q, int64_t ldq, const T* __restrict__ k, const T* __restrict__ v, int64_t ldkv, int64_t n_q,
-    int64_t n_src, int heads, int hd, const float* __restrict__ bias, int64_t n_cls, const float* __restrict__ vcls,
+    int64_t n_src, int heads, int hd, const float* __restrict__ bias, int64_t n_cls, const TV* __restrict__ vcls,
     const int64_t* __restrict__ seg_ptr, const int64_t* __restrict__ src, const int64_t* __restrict__ cls,
     const int64_t* __restrict__ skip_ptr, TO* __restrict__ out, int64_t ldo, float* __restrict__ m_out,
     float* __restrict__ l_out, float scale) {
-  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t row = (int64_t)blockIdx.x * kSegWarps + (threadIdx.x >> 5);
   if (row >= n_q) return;
   const int lane = threadIdx.x & 31;
   const int lph = hd / VEC;  // lanes per head
@@ -63,6 +71,16 @@ __global__ void __launch_bounds__(256) segment_attention_kernel(
     for (int i = 0; i < VEC; ++i) acc[i] = acc[i] * corr + p * vv[i];
     m = m_new;
   };
+  auto add_class_row = [&](int64_t c, float* vv) {
+    if constexpr (HAS_VCLS) {
+      if (live) {
+        float a[VEC];
+        load_vec<VEC>(vcls + c * H + col, a);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) vv[i] += a[i];
+      }
+    }
+  };
 
   int64_t e = beg;
   for (; e + 1 < end; e += 2) {
@@ -83,15 +101,8 @@ __global__ void __launch_bounds__(256) segment_attention_kernel(
     for (int i = 0; i < VEC; ++i) { d0 += qv[i] * k0[i]; d1 += qv[i] * k1[i]; }
     d0 = group_sum(d0, lph) + __ldg(brow + c0);
     d1 = group_sum(d1, lph) + __ldg(brow + c1);
-    if constexpr (HAS_VCLS) {
-      if (live) {
-        float a0[VEC], a1[VEC];
-        load_vec<VEC>(vcls + c0 * H + col, a0);
-        load_vec<VEC>(vcls + c1 * H + col, a1);
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) { v0[i] += a0[i]; v1[i] += a1[i]; }
-      }
-    }
+    add_class_row(c0, v0);
+    add_class_row(c1, v1);
     consume(d0, v0);
     consume(d1, v1);
   }
@@ -109,14 +120,7 @@ __global__ void __launch_bounds__(256) segment_attention_kernel(
 #pragma unroll
       for (int i = 0; i < VEC; ++i) d0 += qv[i] * k0[i];
       d0 = group_sum(d0, lph) + __ldg(brow + c0);
-      if constexpr (HAS_VCLS) {
-        if (live) {
-          float a0[VEC];
-          load_vec<VEC>(vcls + c0 * H + col, a0);
-#pragma unroll
-          for (int i = 0; i < VEC; ++i) v0[i] += a0[i];
-        }
-      }
+      add_class_row(c0, v0);
       consume(d0, v0);
     }
   }
@@ -425,9 +429,9 @@ extern "C" {
 
 int mb_segment_attention(const void* q, int64_t ldq, const void* k, const void* v, int64_t ldkv, int dtype,
                          int64_t n_q, int64_t n_src, int heads, int head_dim, const float* bias, int64_t n_cls,
-                         const float* vcls, const int64_t* seg_ptr, const int64_t* src, const int64_t* cls,
-                         const int64_t* skip_ptr, void* out, int out_dtype, int64_t ldo, float* m, float* l,
-                         void* stream) {
+                         const void* vcls, int vcls_dtype, const int64_t* seg_ptr, const int64_t* src,
+                         const int64_t* cls, const int64_t* skip_ptr, void* out, int out_dtype, int64_t ldo, float* m,
+                         float* l, void* stream) {
   MB_REQUIRE(valid_dtype(dtype) && valid_dtype(out_dtype), "segment_attention: bad dtype");
   MB_REQUIRE(heads > 0 && head_dim > 0 && n_q >= 0, "segment_attention: bad sizes");
   if (n_q == 0) return MB_OK;
@@ -436,21 +440,23 @@ int mb_segment_attention(const void* q, int64_t ldq, const void* k, const void* 
   MB_REQUIRE(vec > 0 && H <= 32 * vec, "segment_attention: unsupported heads=%d head_dim=%d", heads, head_dim);
   MB_REQUIRE(q && out && seg_ptr && bias, "segment_attention: null pointer");
   MB_REQUIRE((m == nullptr) == (l == nullptr), "segment_attention: m and l go together");
+  MB_REQUIRE(valid_dtype(vcls_dtype), "segment_attention: bad vcls dtype");
   const float scale = 1.f / sqrtf((float)head_dim);
-  const int wpb = 8;
-  dim3 grid((unsigned)cdiv(n_q, wpb));
   cudaStream_t s = as_stream(stream);
+  dim3 grid((unsigned)cdiv(n_q, kSegWarps));
   MB_DISPATCH_T(dtype, T, [&] {
     MB_DISPATCH_T(out_dtype, TO, [&] {
-      MB_DISPATCH_VEC(vec, V, [&] {
-        if (vcls)
-          segment_attention_kernel<T, TO, V, true><<<grid, wpb * 32, 0, s>>>(
-              (const T*)q, ldq, (const T*)k, (const T*)v, ldkv, n_q, n_src, heads, head_dim, bias, n_cls, vcls,
-              seg_ptr, src, cls, skip_ptr, (TO*)out, ldo, m, l, scale);
-        else
-          segment_attention_kernel<T, TO, V, false><<<grid, wpb * 32, 0, s>>>(
-              (const T*)q, ldq, (const T*)k, (const T*)v, ldkv, n_q, n_src, heads, head_dim, bias, n_cls, vcls,
-              seg_ptr, src, cls, skip_ptr, (TO*)out, ldo, m, l, scale);
+      MB_DISPATCH_T(vcls_dtype, TV, [&] {
+        MB_DISPATCH_VEC(vec, V, [&] {
+          if (vcls)
+            segment_attention_kernel<T, TO, TV, V, true><<<grid, kSegWarps * 32, 0, s>>>(
+                (const T*)q, ldq, (const T*)k, (const T*)v, ldkv, n_q, n_src, heads, head_dim, bias, n_cls,
+                (const TV*)vcls, seg_ptr, src, cls, skip_ptr, (TO*)out, ldo, m, l, scale);
+          else
+            segment_attention_kernel<T, TO, TV, V, false><<<grid, kSegWarps * 32, 0, s>>>(
+                (const T*)q, ldq, (const T*)k, (const T*)v, ldkv, n_q, n_src, heads, head_dim, bias, n_cls,
+                (const TV*)vcls, seg_ptr, src, cls, skip_ptr, (TO*)out, ldo, m, l, scale);
+        });
       });
     });
   });

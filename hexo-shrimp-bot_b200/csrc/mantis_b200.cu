@@ -5,3 +5,4 @@
 #include "rows.cu"
 #include "attention.cu"
 #include "gemm_simt.cu"
+#include "gemm_sm100.cu"

@@ -69,11 +69,13 @@ class EvaluatorConfig:
     device: str = "cuda"
     autocast: bool = True
     mass_floor: float = 0.2
+    gemm: str = "cublas"
 
 
 def network_evaluate(model, cfg):
     """The self-play evaluator: CPU fp32 (policy, q_score, q_values)."""
     dtype = torch.bfloat16 if getattr(cfg, "autocast", True) else torch.float32
+    gemm = getattr(cfg, "gemm", "cublas")
     fields = needed_fields(model.cfg)
     device = torch.device(cfg.device)
     if device.type != "cuda":
@@ -82,7 +84,7 @@ def network_evaluate(model, cfg):
     def evaluate(batch: Batch):
         with _gpu_lock, torch.no_grad():
             b = to_device(batch, device, fields)
-            eng = model.engine(dtype)
+            eng = model.engine(dtype, gemm=gemm)
             w, g, cells = eng.trunk(b)
             policy, critic = eng.heads(w, g, cells, b)
             q_score, q_values = ops.compose(critic, b.legal_offsets, cfg.mass_floor)

@@ -245,7 +245,7 @@ class MantisNet(nn.Module):
                 nn.init.zeros_(block.mlp_c.out.bias)
 
     # --------------------------------------------------------------- engine
-    def engine(self, dtype: torch.dtype = torch.bfloat16, gemm: str = "torch") -> "Engine":
+    def engine(self, dtype: torch.dtype = torch.bfloat16, gemm: str = "cublas") -> "Engine":
         """The prepared-weight runner for the module's device and ``dtype``;
         rebuilt when any parameter changes (in-place updates bump versions)."""
         if self.training and self.cfg.dropout > 0:
@@ -301,15 +301,20 @@ def _f32(t: Tensor) -> Tensor:
 
 class _Lin:
     """A prepared projection: weight in the compute dtype, bias fp32 (or in
-    the compute dtype for cuBLAS epilogues)."""
+    the compute dtype for cuBLAS epilogues). In bf16 mode a 256-wide input
+    with a multiple of 256 outputs also carries the swizzled weight images of
+    the tcgen05 row GEMM, one per 256-row block of W."""
 
-    __slots__ = ("w", "b", "b_cd", "n", "k")
+    __slots__ = ("w", "b", "b_cd", "n", "k", "imgs")
 
     def __init__(self, w: Tensor, b: Tensor | None, cd: torch.dtype):
         self.w = w.detach().to(cd).contiguous()
         self.b = _f32(b) if b is not None else None
         self.b_cd = self.b.to(cd) if b is not None else None
         self.n, self.k = self.w.shape
+        self.imgs = None
+        if cd == torch.bfloat16 and self.k == ops.GEMM_K and self.n % ops.GEMM_N == 0 and self.w.is_cuda:
+            self.imgs = [ops.weight_image(self.w[j:j + ops.GEMM_N]) for j in range(0, self.n, ops.GEMM_N)]
 
 
 def _cat_lin(parts, cd) -> _Lin:
@@ -386,11 +391,21 @@ class _Tables:
 class Engine:
     """Prepared weights plus the forward schedule over the kernels."""
 
-    def __init__(self, model: MantisNet, dtype: torch.dtype, gemm: str = "torch"):
+    GEMM_MODES = ("tcgen05", "tcgen05-res", "cublas", "native")
+
+    def __init__(self, model: MantisNet, dtype: torch.dtype, gemm: str = "cublas"):
+        """``gemm`` picks the dense-projection path: ``tcgen05`` (the fused
+        LayerNorm-prologue and residual-epilogue row GEMMs of the library
+        wherever the shape is 256 x 256, cuBLAS elsewhere), ``tcgen05-res``
+        (only the residual-epilogue fusion), ``cublas`` (separate LayerNorm /
+        cuBLAS / residual kernels) or ``native`` (the CUDA-core fp32 GEMM,
+        the fp32 parity mode)."""
         if dtype not in (torch.float32, torch.bfloat16):
             raise ValueError("dtype must be torch.float32 or torch.bfloat16")
-        if gemm not in ("torch", "native"):
-            raise ValueError("gemm must be 'torch' or 'native'")
+        if gemm == "torch":
+            gemm = "cublas"
+        if gemm not in self.GEMM_MODES:
+            raise ValueError(f"gemm must be one of {self.GEMM_MODES}")
         self.cfg = cfg = model.cfg
         self.cd = cd = dtype
         self.gemm = gemm
@@ -470,7 +485,7 @@ class Engine:
                 "ln_cr_c": _LN(b.ln_cr_c), "ln_cr_w": _LN(b.ln_cr_w),
                 "cr_wq": _Lin(b.cr_wq.weight, b.cr_wq.bias, cd), "cr_kv": _cat_lin([b.cr_wk, b.cr_wv], cd),
                 "cr_wo": _Lin(b.cr_wo.weight, b.cr_wo.bias, cd), "cr_bias": _f32(b.cr_bias),
-                "cr_vclass": _f32(b.cr_vclass.weight),
+                "cr_vclass": b.cr_vclass.weight.detach().to(cd).contiguous(),
                 "ln_wr_w": _LN(b.ln_wr_w), "ln_wr_c": _LN(b.ln_wr_c),
                 "wr_wq": _Lin(b.wr_wq.weight, b.wr_wq.bias, cd), "wr_kv": _cat_lin([b.wr_wk, b.wr_wv], cd),
                 "wr_wo": _Lin(b.wr_wo.weight, b.wr_wo.bias, cd), "wr_bias": _f32(b.wr_bias),
@@ -481,14 +496,15 @@ class Engine:
                     "radius_wq": _Lin(b.radius_wq.weight, b.radius_wq.bias, cd),
                     "radius_kv": _cat_lin([b.radius_wk, b.radius_wv], cd),
                     "radius_wo": _Lin(b.radius_wo.weight, b.radius_wo.bias, cd),
-                    "radius_bias": _f32(b.radius_bias), "radius_vclass": _f32(b.radius_vclass.weight),
+                    "radius_bias": _f32(b.radius_bias),
+                    "radius_vclass": b.radius_vclass.weight.detach().to(cd).contiguous(),
                 })
             if cfg.cell_adjacency:
                 d.update({
                     "ln_adj_q": _LN(b.ln_adj_q), "ln_adj_k": _LN(b.ln_adj_k),
                     "adj_wq": _Lin(b.adj_wq.weight, b.adj_wq.bias, cd), "adj_kv": _cat_lin([b.adj_wk, b.adj_wv], cd),
                     "adj_wo": _Lin(b.adj_wo.weight, b.adj_wo.bias, cd), "adj_bias": _f32(b.adj_bias),
-                    "adj_vclass": _f32(b.adj_vclass.weight),
+                    "adj_vclass": b.adj_vclass.weight.detach().to(cd).contiguous(),
                 })
             if cfg.cell_structure:
                 d.update({"ln_c": _LN(b.ln_c), "mlp_c": _pair_lin(b.mlp_c, cd)})
@@ -520,6 +536,40 @@ class Engine:
     def ln(self, x: Tensor, p: _LN, out: Tensor | None = None, dtype=None) -> Tensor:
         return ops.layer_norm(x, p.g, p.b, out_dtype=dtype or self.cd, out=out)
 
+    def _fused(self, lin: _Lin, ln: bool = False) -> bool:
+        if lin.imgs is None:
+            return False
+        return self.gemm == "tcgen05" or (self.gemm == "tcgen05-res" and not ln)
+
+    def ln_linear(self, x: Tensor, p: _LN, lin: _Lin, relu: bool = False) -> Tensor:
+        """act(LN(x) @ W^T + b): one tcgen05 launch per 256 output columns
+        with the LayerNorm in the prologue (x fp32), else LN then GEMM."""
+        if self._fused(lin, ln=True) and x.dtype == torch.float32:
+            out = torch.empty(x.shape[0], lin.n, dtype=torch.bfloat16, device=x.device)
+            for j, img in enumerate(lin.imgs):
+                c = slice(j * ops.GEMM_N, (j + 1) * ops.GEMM_N)
+                ops.gemm_rows(x, img, bias=lin.b[c] if lin.b is not None else None, gamma=p.g, beta=p.b,
+                              relu=relu, out=out[:, c])
+            return out
+        return self.linear(self.ln(x, p), lin, relu=relu)
+
+    def linear_cd(self, a: Tensor, lin: _Lin, relu: bool = False) -> Tensor:
+        """act(a @ W^T + b) for compute-dtype rows a."""
+        if self.gemm == "tcgen05" and lin.imgs is not None and a.dtype == torch.bfloat16:
+            out = torch.empty(a.shape[0], lin.n, dtype=torch.bfloat16, device=a.device)
+            for j, img in enumerate(lin.imgs):
+                c = slice(j * ops.GEMM_N, (j + 1) * ops.GEMM_N)
+                ops.gemm_rows(a, img, bias=lin.b[c] if lin.b is not None else None, relu=relu, out=out[:, c])
+            return out
+        return self.linear(a, lin, relu=relu)
+
+    def linear_residual(self, a: Tensor, lin: _Lin, x: Tensor) -> None:
+        """x += a @ W^T + b with the residual add in the GEMM epilogue."""
+        if self._fused(lin) and lin.n == ops.GEMM_N and a.dtype == torch.bfloat16 and x.dtype == torch.float32:
+            ops.gemm_rows(a, lin.imgs[0], bias=lin.b, residual=x)
+            return
+        ops.residual_add(x, self.linear(a, lin))
+
     def pair_mlp_residual(self, x: Tensor, a_ln: _LN, agg_writer, mlp) -> None:
         """x += out(relu([ln(x) | agg] @ [Wa | Wb]^T + ba)) with ``agg_writer``
         filling the right half of the staging buffer."""
@@ -528,7 +578,7 @@ class Engine:
         self.ln(x, a_ln, out=buf[:, :h])
         agg_writer(buf[:, h:])
         hid = self.linear(buf, mlp[0], relu=True)
-        ops.residual_add(x, self.linear(hid, mlp[1]))
+        self.linear_residual(hid, mlp[1], x)
 
     # ---------------------------------------------------------------- trunk
     def trunk(self, b: Batch):
@@ -574,7 +624,7 @@ class Engine:
         cfg, cd, h = self.cfg, self.cd, self.h
         nb = len(self.blocks)
         # §5.1 windows <- stones (sum) + per-pattern class rows
-        x = self.linear(self.ln(s, blk["ln_ws_s"]), blk["u"])
+        x = self.ln_linear(s, blk["ln_ws_s"], blk["u"])
         ws = self.ws_table[:, i * h:(i + 1) * h]
         self.pair_mlp_residual(
             w, blk["ln_ws_w"],
@@ -585,12 +635,12 @@ class Engine:
             w, c = self._cell_stage(blk, s, w, c, T)
         else:
             # transient relay over the collated relay views (model.py:371-395)
-            xr = self.linear(self.ln(w, blk["ln_cp_in"]), blk["u_cp"])
+            xr = self.ln_linear(w, blk["ln_cp_in"], blk["u_cp"])
             agg = ops.cell_pass(xr, blk["e_cp"], b.relay_cell_ptr, b.relay_window, b.relay_class, b.relay_win_ptr,
                                 b.relay_wcell, b.relay_cls_ptr, b.relay_ccell)
             self.pair_mlp_residual(w, blk["ln_cp_w"], lambda out: out.copy_(agg), blk["mlp_cp"])
         # §5.2 stones <- windows (fp32 sum) + class rows
-        y = self.linear(self.ln(w, blk["ln_sw_w"]), blk["v"])
+        y = self.ln_linear(w, blk["ln_sw_w"], blk["v"])
         sw = sw_all[:, i * h:(i + 1) * h]
         self.pair_mlp_residual(
             s, blk["ln_sw_s"],
@@ -598,20 +648,19 @@ class Engine:
             blk["mlp_s"])
         # §5.3 attention over [latents; stones]
         tok = ops.tokens_gather(g, s, T.stone_off, T.tok_off, T.N_tok)
-        z = self.ln(tok, blk["ln_attn"])
-        qkv = self.linear(z, blk["qkv"])
+        qkv = self.ln_linear(tok, blk["ln_attn"], blk["qkv"])
         if update_stones:
             att = ops.stone_attention_ragged(qkv, T.tok_off, cfg.heads, T.max_t)
-            ops.tokens_scatter_add(g, s, T.stone_off, T.tok_off, self.linear(att, blk["wo"]), update_stones=True)
+            ops.tokens_scatter_add(g, s, T.stone_off, T.tok_off, self.linear_cd(att, blk["wo"]), update_stones=True)
         else:
             att = ops.stone_attention_ragged(qkv, T.tok_off, cfg.heads, T.max_t, max_queries=GLOBAL_ROWS,
                                              out_dtype=cd)
-            ops.residual_add(g, self.linear(att, blk["wo"]))
+            self.linear_residual(att, blk["wo"], g)
         # window-latent cycle
         w, g = self._latent_cycle(blk, w, g, T)
         # FFN (row-wise; the stone half is skipped in the last block)
         for x_ in ((s, g) if update_stones else (g,)):
-            hid = self.linear(self.ln(x_, blk["ln_ffn"]), blk["ffn0"], relu=True)
+            hid = self.ln_linear(x_, blk["ln_ffn"], blk["ffn0"], relu=True)
             ops.residual_add(x_, self.linear(hid, blk["ffn2"]))
         return s, w, g, c
 
@@ -619,51 +668,56 @@ class Engine:
         """model.py:397-490."""
         cfg, cd, h = self.cfg, self.cd, self.h
         zstate = self.ln(c, blk["ln_c"]) if cfg.cell_structure else None
-        q = self.linear(self.ln(c, blk["ln_cr_c"]), blk["cr_wq"])
-        kv = self.linear(self.ln(w, blk["ln_cr_w"]), blk["cr_kv"])
+        q = self.ln_linear(c, blk["ln_cr_c"], blk["cr_wq"])
+        kv = self.ln_linear(w, blk["ln_cr_w"], blk["cr_kv"])
         read = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["cr_bias"], blk["cr_vclass"], T.cell_ptr,
                                      T.dec_window, T.dec_class, out_dtype=cd)
-        reads = self.linear(read, blk["cr_wo"])
-        ops.residual_add(c, reads)
+        if cfg.cell_structure:
+            reads = self.linear_cd(read, blk["cr_wo"])
+            ops.residual_add(c, reads)
+        else:
+            self.linear_residual(read, blk["cr_wo"], c)
         if cfg.cell_nodes:
-            q = self.linear(self.ln(c, blk["ln_radius_c"]), blk["radius_wq"])
-            kv = self.linear(self.ln(s, blk["ln_radius_s"]), blk["radius_kv"])
+            q = self.ln_linear(c, blk["ln_radius_c"], blk["radius_wq"])
+            kv = self.ln_linear(s, blk["ln_radius_s"], blk["radius_kv"])
             read = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["radius_bias"], blk["radius_vclass"], T.r_ptr,
                                          T.r_src, T.r_cls, skip_ptr=T.skip, out_dtype=cd)
-            stone = self.linear(read, blk["radius_wo"])
-            ops.residual_add(c, stone)
             if cfg.cell_structure:
+                stone = self.linear_cd(read, blk["radius_wo"])
+                ops.residual_add(c, stone)
                 reads = (reads.float() + stone.float()).to(cd)
+            else:
+                self.linear_residual(read, blk["radius_wo"], c)
         if cfg.cell_structure:
             mlp = blk["mlp_c"]
             buf = torch.cat([zstate, reads], 1)
             ops.residual_add(c, self.linear(self.linear(buf, mlp[0], relu=True), mlp[1]))
         if cfg.cell_adjacency:
-            q = self.linear(self.ln(c, blk["ln_adj_q"]), blk["adj_wq"])
-            kv = self.linear(self.ln(c, blk["ln_adj_k"]), blk["adj_kv"])
+            q = self.ln_linear(c, blk["ln_adj_q"], blk["adj_wq"])
+            kv = self.ln_linear(c, blk["ln_adj_k"], blk["adj_kv"])
             read = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["adj_bias"], blk["adj_vclass"], T.a_ptr,
                                          T.a_src, T.a_cls, skip_ptr=T.skip, out_dtype=cd)
-            ops.residual_add(c, self.linear(read, blk["adj_wo"]))
-        q = self.linear(self.ln(w, blk["ln_wr_w"]), blk["wr_wq"])
-        kv = self.linear(self.ln(c, blk["ln_wr_c"]), blk["wr_kv"])
+            self.linear_residual(read, blk["adj_wo"], c)
+        q = self.ln_linear(w, blk["ln_wr_w"], blk["wr_wq"])
+        kv = self.ln_linear(c, blk["ln_wr_c"], blk["wr_kv"])
         back = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["wr_bias"], None, T.win_ptr, T.edge_wcell,
                                      T.edge_wclass, out_dtype=cd)
-        ops.residual_add(w, self.linear(back, blk["wr_wo"]))
+        self.linear_residual(back, blk["wr_wo"], w)
         return w, c
 
     def _latent_cycle(self, blk, w, g, T: _Tables):
         """model.py:492-541."""
         cfg, cd, h = self.cfg, self.cd, self.h
-        q = self.linear(self.ln(g, blk["ln_read_q"]), blk["wq_read"])
-        kv = self.linear(self.ln(w, blk["ln_read_w"]), blk["kv_read"])
+        q = self.ln_linear(g, blk["ln_read_q"], blk["wq_read"])
+        kv = self.ln_linear(w, blk["ln_read_w"], blk["kv_read"])
         read = ops.latent_read(q, kv[:, :h], kv[:, h:], cfg.heads, T.wl_off, T.wl_order, out_dtype=cd)
-        ops.residual_add(g, self.linear(read, blk["wo_read"]))
-        qkv = self.linear(self.ln(g, blk["ln_mix"]), blk["qkv_mix"])
-        ops.residual_add(g, self.linear(ops.latent_mix(qkv, cfg.heads, cd), blk["wo_mix"]))
-        kv = self.linear(self.ln(g, blk["ln_bcast_l"]), blk["kv_bcast"])
-        q = self.linear(self.ln(w, blk["ln_bcast_q"]), blk["wq_bcast"])
+        self.linear_residual(read, blk["wo_read"], g)
+        qkv = self.ln_linear(g, blk["ln_mix"], blk["qkv_mix"])
+        self.linear_residual(ops.latent_mix(qkv, cfg.heads, cd), blk["wo_mix"], g)
+        kv = self.ln_linear(g, blk["ln_bcast_l"], blk["kv_bcast"])
+        q = self.ln_linear(w, blk["ln_bcast_q"], blk["wq_bcast"])
         bc = ops.latent_broadcast(q, kv[:, :h], kv[:, h:], cfg.heads, T.window_pos, T.P, out_dtype=cd)
-        ops.residual_add(w, self.linear(bc, blk["wo_bcast"]))
+        self.linear_residual(bc, blk["wo_bcast"], w)
         return w, g
 
     # ---------------------------------------------------------------- heads
@@ -674,7 +728,7 @@ class Engine:
         if T is None or T.N_c != b.cell_pos.shape[0]:
             T = _Tables(cfg, b)
         n_c = T.N_c
-        pre = self.linear(w.to(cd), self.act_proj)
+        pre = self.linear_cd(w.to(cd), self.act_proj)
         acts_dtype = torch.float32 if cfg.action_tactical else cd
         buf = torch.empty(n_c, 2 * h, dtype=cd, device=w.device)
         acts = ops.row_encode(pre, self.act_table, T.dec_window, T.act_class, T.cell_ptr, n_c,

@@ -154,10 +154,12 @@ def segment_attention(q, k, v, bias, vcls, seg_ptr, src, cls, skip_ptr=None, out
     if stats:
         m = torch.empty(n_q, heads, dtype=torch.float32, device=q.device)
         l = torch.empty_like(m)
-    bias32 = bias.float().contiguous()
-    vcls32 = vcls.float().contiguous() if vcls is not None else None
+    bias32 = bias if (bias.dtype == torch.float32 and bias.is_contiguous()) else bias.float().contiguous()
+    if vcls is not None and not (vcls.dtype in (torch.float32, torch.bfloat16) and vcls.is_contiguous()):
+        vcls = vcls.float().contiguous()
     call("mb_segment_attention", ptr(q2), q2.stride(0), ptr(k2), ptr(v2), k2.stride(0), dtype_code(q2.dtype),
-         n_q, k2.shape[0], heads, hd, ptr(bias32), bias32.shape[1], ptr(vcls32), ptr(seg_ptr), ptr(src), ptr(cls),
+         n_q, k2.shape[0], heads, hd, ptr(bias32), bias32.shape[1], ptr(vcls),
+         dtype_code(vcls.dtype) if vcls is not None else 0, ptr(seg_ptr), ptr(src), ptr(cls),
          ptr(skip_ptr), ptr(out), dtype_code(out.dtype), out.stride(0), ptr(m), ptr(l), stream_of(q.device))
     return (out, m, l) if stats else out
 
@@ -590,3 +592,36 @@ def fused_attention(q, k, v, seq_lens):
          ptr(seq_lens.contiguous()), t, None, 0, -1, ptr(out), dtype_code(out.dtype), op, oa, ot,
          stream_of(q.device))
     return out
+
+
+# ============================================ tcgen05 fused row GEMM (sm_100a)
+
+GEMM_K = GEMM_N = 256
+
+
+def weight_image(w: torch.Tensor) -> torch.Tensor:
+    """The pre-swizzled bf16 image of a (256, 256) weight for ``gemm_rows``."""
+    _cuda(w)
+    w = w.detach().to(torch.bfloat16).contiguous()
+    if tuple(w.shape) != (GEMM_N, GEMM_K):
+        raise ValueError(f"gemm weight must be ({GEMM_N}, {GEMM_K}), got {tuple(w.shape)}")
+    img = torch.empty_like(w)
+    call("mb_gemm_weight_image", ptr(w), w.shape[0], w.shape[1], ptr(img), stream_of(w.device))
+    return img
+
+
+def gemm_rows(x, w_img, bias=None, gamma=None, beta=None, relu=False, out=None, residual=None, eps=1e-5):
+    """act(prologue(x) @ W^T + bias) on tcgen05: LayerNorm prologue when
+    ``gamma`` is given (x fp32), else x bf16. Writes ``out`` (bf16, allocated
+    when neither out nor residual is given) or adds into ``residual`` (fp32)."""
+    _rowmajor(x, "x")
+    if x.shape[1] != GEMM_K:
+        raise ValueError(f"gemm_rows takes rows of width {GEMM_K}")
+    m = x.shape[0]
+    if out is None and residual is None:
+        out = torch.empty(m, GEMM_N, dtype=torch.bfloat16, device=x.device)
+    b = bias.float().contiguous() if bias is not None else None
+    call("mb_gemm_rows", ptr(x), dtype_code(x.dtype), x.stride(0), m, ptr(gamma), ptr(beta), float(eps), ptr(w_img),
+         ptr(b), int(relu), ptr(out), out.stride(0) if out is not None else 0, ptr(residual),
+         residual.stride(0) if residual is not None else 0, stream_of(x.device))
+    return out if out is not None else residual

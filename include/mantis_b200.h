@@ -106,13 +106,14 @@ int mb_cell_pass(const void* x, int x_dtype, int64_t n_windows, const float* emb
 /* ------------------------------------------------------------ attention --
  * Typed segment attention: per query row and head, online softmax over its
  * CSR run of sources; score = q.k / sqrt(hd) + bias[head, cls]; value =
- * v[src] (+ vcls[cls] when vcls != NULL). Empty runs (or rows whose
+ * v[src] (+ vcls[cls] when vcls != NULL; vcls f32 or bf16, (n_cls, heads * head_dim)).
+ * Empty runs (or rows whose
  * skip_ptr run is non-empty) read zero with m = -inf, l = 0. m/l may be NULL.
  * Replaces mantisnet::cell_attention and mantisnet::cell_attention_plain
  * (cell_latents.py:834-940; kernel cell_latents.py:213-285). */
 int mb_segment_attention(const void* q, int64_t ldq, const void* k, const void* v, int64_t ldkv, int dtype,
                          int64_t n_q, int64_t n_src, int heads, int head_dim,
-                         const float* bias, int64_t n_cls, const float* vcls,
+                         const float* bias, int64_t n_cls, const void* vcls, int vcls_dtype,
                          const int64_t* seg_ptr, const int64_t* src, const int64_t* cls, const int64_t* skip_ptr,
                          void* out, int out_dtype, int64_t ldo, float* m, float* l, void* stream);
 
@@ -205,6 +206,19 @@ int mb_compose_q(const float* critic, int64_t ld_critic, const int64_t* offsets,
  * cuBLAS under autocast). */
 int mb_linear(const void* a, int a_dtype, int64_t lda, int64_t m, int64_t k, const void* w, int w_dtype,
               const float* bias, int64_t n, int relu, void* out, int out_dtype, int64_t ldo, void* stream);
+
+/* Fused row GEMM on tcgen05 tensor cores (sm_100a), K = N = 256:
+ *   out[r] = act(LN(x[r]) @ W^T + bias)            (gamma != NULL: x fp32, LayerNorm prologue)
+ *   out[r] = act(x[r] @ W^T + bias)                (gamma == NULL: x bf16)
+ * with either a bf16 output (out, ldo) or an in-place fp32 residual update
+ * residual[r] += result (exactly one of the two). W is passed as the image
+ * produced by mb_gemm_weight_image (256 x 256 bf16 -> 128 KB swizzled).
+ * Replaces the LayerNorm -> nn.Linear -> residual-add chains of the trunk
+ * (model.py:425-489, 506-540, 570-580, 609-619). */
+int mb_gemm_weight_image(const void* w, int64_t n, int64_t k, void* image, void* stream);
+int mb_gemm_rows(const void* x, int x_dtype, int64_t ldx, int64_t m, const float* gamma, const float* beta, float eps,
+                 const void* w_image, const float* bias, int relu, void* out, int64_t ldo, float* residual,
+                 int64_t ldr, void* stream);
 
 #ifdef __cplusplus
 }
