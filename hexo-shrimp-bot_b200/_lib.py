@@ -39,6 +39,7 @@ SIGNATURES = {
     "mb_window_latent_broadcast": "plpplilliippippp",
     "mb_latent_mix": "pppliliipip",
     "mb_layer_norm": "pilpllppfpilp",
+    "mb_add_ln": "plpilpllfpppilpppilpppilp",
     "mb_embed": "plpplpllpp",
     "mb_cell_init": "ppplppllpp",
     "mb_residual_add": "pilppilllp",

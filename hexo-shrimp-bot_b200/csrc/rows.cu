@@ -193,6 +193,90 @@ __global__ void __launch_bounds__(kWarps * 32) layer_norm_kernel(
   }
 }
 
+// ------------------------------------------- residual update + LayerNorms --
+// x[r] += y[r] (+ y_bias), then up to three LayerNorms of the updated row, each
+// with its own affine parameters, destination and dtype: one read and one
+// write of the residual row feed every consumer that normalises it next.
+struct LnOut {
+  const float* g;
+  const float* b;
+  void* out;
+  int dtype;
+  int64_t ld;
+};
+
+template <int VEC>
+__device__ __forceinline__ void ln_store(const LnOut& o, int64_t r, int64_t col, const float* v, float mean,
+                                         float rstd) {
+  float g[VEC], b[VEC], y[VEC];
+  load_vec<VEC>(o.g + col, g);
+  load_vec<VEC>(o.b + col, b);
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) y[i] = (v[i] - mean) * rstd * g[i] + b[i];
+  if (o.dtype == MB_BF16)
+    store_vec<VEC>(reinterpret_cast<__nv_bfloat16*>(o.out) + r * o.ld + col, y);
+  else
+    store_vec<VEC>(reinterpret_cast<float*>(o.out) + r * o.ld + col, y);
+}
+
+template <typename TY, int VEC>
+__global__ void __launch_bounds__(kWarps * 32) add_ln_kernel(float* __restrict__ x, int64_t ldx,
+                                                             const TY* __restrict__ y, int64_t ldy,
+                                                             const float* __restrict__ y_bias, int64_t n, int64_t h,
+                                                             float eps, int n_out, LnOut o0, LnOut o1, LnOut o2) {
+  const int64_t r = warp_row();
+  if (r >= n) return;
+  const int lane = threadIdx.x & 31;
+  const int chunks = (int)((h + 32 * VEC - 1) / (32 * VEC));
+  float v[kMaxChunks][VEC];
+  float sum = 0.f;
+#pragma unroll
+  for (int ch = 0; ch < kMaxChunks; ++ch) {
+    const int64_t col = ch * 32 * VEC + lane * VEC;
+    if (ch < chunks && col < h) {
+      load_vec<VEC>(x + r * ldx + col, v[ch]);
+      if (y) {
+        float a[VEC];
+        load_vec<VEC>(y + r * ldy + col, a);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) v[ch][i] += a[i];
+        if (y_bias) {
+          load_vec<VEC>(y_bias + col, a);
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) v[ch][i] += a[i];
+        }
+        store_vec<VEC>(x + r * ldx + col, v[ch]);
+      }
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) sum += v[ch][i];
+    }
+  }
+  if (n_out == 0) return;
+  const float mean = warp_sum(sum) / (float)h;
+  float sq = 0.f;
+#pragma unroll
+  for (int ch = 0; ch < kMaxChunks; ++ch) {
+    const int64_t col = ch * 32 * VEC + lane * VEC;
+    if (ch < chunks && col < h) {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        const float d = v[ch][i] - mean;
+        sq += d * d;
+      }
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(sq) / (float)h + eps);
+#pragma unroll
+  for (int ch = 0; ch < kMaxChunks; ++ch) {
+    const int64_t col = ch * 32 * VEC + lane * VEC;
+    if (ch < chunks && col < h) {
+      ln_store<VEC>(o0, r, col, v[ch], mean, rstd);
+      if (n_out > 1) ln_store<VEC>(o1, r, col, v[ch], mean, rstd);
+      if (n_out > 2) ln_store<VEC>(o2, r, col, v[ch], mean, rstd);
+    }
+  }
+}
+
 // ------------------------------------------------------------ misc rows --
 template <int VEC>
 __global__ void __launch_bounds__(kWarps * 32) embed_kernel(
@@ -470,6 +554,33 @@ int mb_layer_norm(const void* x, int x_dtype, int64_t ldx, const int64_t* in_row
     });
   });
   return launch_status("layer_norm");
+}
+
+int mb_add_ln(float* x, int64_t ldx, const void* y, int y_dtype, int64_t ldy, const float* y_bias, int64_t n,
+              int64_t h, float eps, const float* g0, const float* b0, void* o0, int o0_dtype, int64_t ld0,
+              const float* g1, const float* b1, void* o1, int o1_dtype, int64_t ld1, const float* g2,
+              const float* b2, void* o2, int o2_dtype, int64_t ld2, void* stream) {
+  if (n == 0) return MB_OK;
+  const int vec = row_vec(h);
+  MB_REQUIRE(x && vec > 0 && h <= 32 * vec * kMaxChunks, "add_ln: bad arguments (h=%lld)", (long long)h);
+  MB_REQUIRE(!y || valid_dtype(y_dtype), "add_ln: bad y dtype");
+  LnOut outs[3] = {{g0, b0, o0, o0_dtype, ld0}, {g1, b1, o1, o1_dtype, ld1}, {g2, b2, o2, o2_dtype, ld2}};
+  int n_out = 0;
+  for (int j = 0; j < 3; ++j) {
+    if (!outs[j].out) break;
+    MB_REQUIRE(outs[j].g && outs[j].b && valid_dtype(outs[j].dtype), "add_ln: output %d incomplete", j);
+    n_out = j + 1;
+  }
+  for (int j = n_out; j < 3; ++j) MB_REQUIRE(!outs[j].out, "add_ln: outputs must be given in order");
+  MB_REQUIRE(y || n_out > 0, "add_ln: nothing to do");
+  cudaStream_t s = as_stream(stream);
+  MB_DISPATCH_T(y ? y_dtype : MB_F32, TY, [&] {
+    MB_DISPATCH_VEC(vec, V, [&] {
+      add_ln_kernel<TY, V><<<row_grid(n), kWarps * 32, 0, s>>>(x, ldx, (const TY*)y, ldy, y_bias, n, h, eps, n_out,
+                                                               outs[0], outs[1], outs[2]);
+    });
+  });
+  return launch_status("add_ln");
 }
 
 int mb_embed(const float* ta, int64_t n_ta, const int64_t* ia, const float* tb, int64_t n_tb, const int64_t* ib,

@@ -581,7 +581,26 @@ class Engine:
         self.linear_residual(hid, mlp[1], x)
 
     # ---------------------------------------------------------------- trunk
+    def update(self, x: Tensor, y: Tensor | None, lns) -> list[Tensor]:
+        """x += y, then one LayerNorm per ``lns`` entry, in a single pass over
+        x. Entries are ``_LN`` (a new compute-dtype tensor), or ``(_LN, out)``
+        with ``out`` a preallocated destination (dtype and stride taken from
+        it). Returns the outputs in order."""
+        outs = []
+        for e in lns:
+            p, o = e if isinstance(e, tuple) else (e, None)
+            if o is None:
+                o = torch.empty(x.shape[0], x.shape[1], dtype=self.cd, device=x.device)
+            outs.append((p.g, p.b, o))
+        for j in range(0, max(len(outs), 1), 3):
+            ops.add_ln(x, y if j == 0 else None, outs=outs[j:j + 3])
+        return [o for _, _, o in outs]
+
+    # ---------------------------------------------------------------- trunk
     def trunk(self, b: Batch):
+        """model.py:898-985. Every update of the large residual streams (w per
+        window, c per cell) also emits the LayerNorms of the next stages that
+        read them, so a stream row is read and written once per update."""
         cfg, cd, h = self.cfg, self.cd, self.h
         T = _Tables(cfg, b)
         self.tables = T
@@ -607,44 +626,61 @@ class Engine:
                     c += add
         sw_all = ops.run_reduce(self.sw_tables, T.run_class, T.stone_ptr, T.N_s) if self.blocks else None
         nb = len(self.blocks)
-        for i, blk in enumerate(self.blocks):
-            s, w, g, c = self._block(i, blk, s, w, g, c, b, T, sw_all, update_stones=i + 1 < nb)
+        w_out = cells = None
+        if nb:
+            first = self.blocks[0]
+            buf_w = torch.empty(T.N_w, 2 * h, dtype=cd, device=dev)
+            self.update(w, None, [(first["ln_ws_w"], buf_w[:, :h])])
+            zc = self.update(c, None, [first["ln_cr_c"]])[0] if cfg.uses_cell_state else None
+            for i, blk in enumerate(self.blocks):
+                nxt = self.blocks[i + 1] if i + 1 < nb else None
+                s, w, g, c, buf_w, zc, w_out, cells = self._block(
+                    i, blk, nxt, s, w, g, c, b, T, sw_all, buf_w, zc, update_stones=i + 1 < nb)
+        else:
+            w_out = self.ln(w, self.ln_out, dtype=torch.float32)
+            if cfg.uses_cell_state:
+                cells = self.ln(c, self.ln_out, dtype=torch.float32)
         g_ln = self.ln(g, self.ln_out, dtype=torch.float32)
         global_rows = ops.latent_mean(g_ln, T.P)
-        cells = None
-        if cfg.uses_cell_state:
-            cells = self.ln(c, self.ln_out, dtype=torch.float32)
-            if not cfg.cell_nodes:
-                base = F.layer_norm(self.cell_base, (h,), self.ln_out.g, self.ln_out.b, 1e-5)
-                covered = (T.cell_ptr[1:] > T.cell_ptr[:-1])[:, None]
-                cells = torch.where(covered, cells, base)
-        return self.ln(w, self.ln_out, dtype=torch.float32), global_rows, cells
+        if cfg.uses_cell_state and not cfg.cell_nodes:
+            base = F.layer_norm(self.cell_base, (h,), self.ln_out.g, self.ln_out.b, 1e-5)
+            covered = (T.cell_ptr[1:] > T.cell_ptr[:-1])[:, None]
+            cells = torch.where(covered, cells, base)
+        return w_out, global_rows, cells
 
-    def _block(self, i, blk, s, w, g, c, b, T: _Tables, sw_all, update_stones: bool):
+    def _exit_lns(self, nxt, key):
+        """The LayerNorm a stream's last update of a block feeds: the next
+        block's entry norm, or the trunk's shared ln_out (fp32 output)."""
+        return nxt[key] if nxt is not None else None
+
+    def _block(self, i, blk, nxt, s, w, g, c, b, T: _Tables, sw_all, buf_w, zc, update_stones: bool):
+        """model.py:543-692."""
         cfg, cd, h = self.cfg, self.cd, self.h
-        nb = len(self.blocks)
-        # §5.1 windows <- stones (sum) + per-pattern class rows
+        # §5.1 windows <- stones (sum) + per-pattern class rows; buf_w's left
+        # half already holds LN_ws_w(w)
         x = self.ln_linear(s, blk["ln_ws_s"], blk["u"])
-        ws = self.ws_table[:, i * h:(i + 1) * h]
-        self.pair_mlp_residual(
-            w, blk["ln_ws_w"],
-            lambda out: ops.run_reduce(x, b.inc_stone, T.window_ptr, T.N_w, add=ws, add_idx=b.window_feat, out=out),
-            blk["mlp_w"])
+        ops.run_reduce(x, b.inc_stone, T.window_ptr, T.N_w, add=self.ws_table[:, i * h:(i + 1) * h],
+                       add_idx=b.window_feat, out=buf_w[:, h:])
+        y = self.linear(self.linear(buf_w, blk["mlp_w"][0], relu=True), blk["mlp_w"][1])
         # §5.1b
         if cfg.uses_cell_state:
-            w, c = self._cell_stage(blk, s, w, c, T)
+            zw_cr, zw_wr = self.update(w, y, [blk["ln_cr_w"], blk["ln_wr_w"]])
+            y, c, zc, cells = self._cell_stage(blk, nxt, s, c, T, zc, zw_cr, zw_wr)
         else:
-            # transient relay over the collated relay views (model.py:371-395)
-            xr = self.ln_linear(w, blk["ln_cp_in"], blk["u_cp"])
-            agg = ops.cell_pass(xr, blk["e_cp"], b.relay_cell_ptr, b.relay_window, b.relay_class, b.relay_win_ptr,
-                                b.relay_wcell, b.relay_cls_ptr, b.relay_ccell)
-            self.pair_mlp_residual(w, blk["ln_cp_w"], lambda out: out.copy_(agg), blk["mlp_cp"])
+            buf2 = torch.empty(T.N_w, 2 * h, dtype=cd, device=w.device)
+            zin, _ = self.update(w, y, [blk["ln_cp_in"], (blk["ln_cp_w"], buf2[:, :h])])
+            xr = self.linear(zin, blk["u_cp"])
+            buf2[:, h:].copy_(ops.cell_pass(xr, blk["e_cp"], b.relay_cell_ptr, b.relay_window, b.relay_class,
+                                            b.relay_win_ptr, b.relay_wcell, b.relay_cls_ptr, b.relay_ccell))
+            y = self.linear(self.linear(buf2, blk["mlp_cp"][0], relu=True), blk["mlp_cp"][1])
+            cells = None
+        zw_sw, zw_read, zw_bq = self.update(w, y, [blk["ln_sw_w"], blk["ln_read_w"], blk["ln_bcast_q"]])
         # §5.2 stones <- windows (fp32 sum) + class rows
-        y = self.ln_linear(w, blk["ln_sw_w"], blk["v"])
+        yv = self.linear(zw_sw, blk["v"])
         sw = sw_all[:, i * h:(i + 1) * h]
         self.pair_mlp_residual(
             s, blk["ln_sw_s"],
-            lambda out: ops.run_reduce(y, T.run_window, T.stone_ptr, T.N_s, add=sw, out=out),
+            lambda out: ops.run_reduce(yv, T.run_window, T.stone_ptr, T.N_s, add=sw, out=out),
             blk["mlp_s"])
         # §5.3 attention over [latents; stones]
         tok = ops.tokens_gather(g, s, T.stone_off, T.tok_off, T.N_tok)
@@ -656,69 +692,78 @@ class Engine:
             att = ops.stone_attention_ragged(qkv, T.tok_off, cfg.heads, T.max_t, max_queries=GLOBAL_ROWS,
                                              out_dtype=cd)
             self.linear_residual(att, blk["wo"], g)
-        # window-latent cycle
-        w, g = self._latent_cycle(blk, w, g, T)
-        # FFN (row-wise; the stone half is skipped in the last block)
-        for x_ in ((s, g) if update_stones else (g,)):
-            hid = self.ln_linear(x_, blk["ln_ffn"], blk["ffn0"], relu=True)
-            ops.residual_add(x_, self.linear(hid, blk["ffn2"]))
-        return s, w, g, c
-
-    def _cell_stage(self, blk, s, w, c, T: _Tables):
-        """model.py:397-490."""
-        cfg, cd, h = self.cfg, self.cd, self.h
-        zstate = self.ln(c, blk["ln_c"]) if cfg.cell_structure else None
-        q = self.ln_linear(c, blk["ln_cr_c"], blk["cr_wq"])
-        kv = self.ln_linear(w, blk["ln_cr_w"], blk["cr_kv"])
-        read = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["cr_bias"], blk["cr_vclass"], T.cell_ptr,
-                                     T.dec_window, T.dec_class, out_dtype=cd)
-        if cfg.cell_structure:
-            reads = self.linear_cd(read, blk["cr_wo"])
-            ops.residual_add(c, reads)
-        else:
-            self.linear_residual(read, blk["cr_wo"], c)
-        if cfg.cell_nodes:
-            q = self.ln_linear(c, blk["ln_radius_c"], blk["radius_wq"])
-            kv = self.ln_linear(s, blk["ln_radius_s"], blk["radius_kv"])
-            read = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["radius_bias"], blk["radius_vclass"], T.r_ptr,
-                                         T.r_src, T.r_cls, skip_ptr=T.skip, out_dtype=cd)
-            if cfg.cell_structure:
-                stone = self.linear_cd(read, blk["radius_wo"])
-                ops.residual_add(c, stone)
-                reads = (reads.float() + stone.float()).to(cd)
-            else:
-                self.linear_residual(read, blk["radius_wo"], c)
-        if cfg.cell_structure:
-            mlp = blk["mlp_c"]
-            buf = torch.cat([zstate, reads], 1)
-            ops.residual_add(c, self.linear(self.linear(buf, mlp[0], relu=True), mlp[1]))
-        if cfg.cell_adjacency:
-            q = self.ln_linear(c, blk["ln_adj_q"], blk["adj_wq"])
-            kv = self.ln_linear(c, blk["ln_adj_k"], blk["adj_kv"])
-            read = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["adj_bias"], blk["adj_vclass"], T.a_ptr,
-                                         T.a_src, T.a_cls, skip_ptr=T.skip, out_dtype=cd)
-            self.linear_residual(read, blk["adj_wo"], c)
-        q = self.ln_linear(w, blk["ln_wr_w"], blk["wr_wq"])
-        kv = self.ln_linear(c, blk["ln_wr_c"], blk["wr_kv"])
-        back = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["wr_bias"], None, T.win_ptr, T.edge_wcell,
-                                     T.edge_wclass, out_dtype=cd)
-        self.linear_residual(back, blk["wr_wo"], w)
-        return w, c
-
-    def _latent_cycle(self, blk, w, g, T: _Tables):
-        """model.py:492-541."""
-        cfg, cd, h = self.cfg, self.cd, self.h
+        # window-latent cycle (model.py:492-541)
         q = self.ln_linear(g, blk["ln_read_q"], blk["wq_read"])
-        kv = self.ln_linear(w, blk["ln_read_w"], blk["kv_read"])
+        kv = self.linear(zw_read, blk["kv_read"])
         read = ops.latent_read(q, kv[:, :h], kv[:, h:], cfg.heads, T.wl_off, T.wl_order, out_dtype=cd)
         self.linear_residual(read, blk["wo_read"], g)
         qkv = self.ln_linear(g, blk["ln_mix"], blk["qkv_mix"])
         self.linear_residual(ops.latent_mix(qkv, cfg.heads, cd), blk["wo_mix"], g)
         kv = self.ln_linear(g, blk["ln_bcast_l"], blk["kv_bcast"])
-        q = self.ln_linear(w, blk["ln_bcast_q"], blk["wq_bcast"])
+        q = self.linear(zw_bq, blk["wq_bcast"])
         bc = ops.latent_broadcast(q, kv[:, :h], kv[:, h:], cfg.heads, T.window_pos, T.P, out_dtype=cd)
-        self.linear_residual(bc, blk["wo_bcast"], w)
-        return w, g
+        y = self.linear(bc, blk["wo_bcast"])
+        w_out = None
+        if nxt is not None:
+            buf_w = torch.empty(T.N_w, 2 * h, dtype=cd, device=w.device)
+            self.update(w, y, [(nxt["ln_ws_w"], buf_w[:, :h])])
+        else:
+            w_out = torch.empty(T.N_w, h, dtype=torch.float32, device=w.device)
+            self.update(w, y, [(self.ln_out, w_out)])
+        # FFN (row-wise; the stone half is skipped in the last block)
+        for x_ in ((s, g) if update_stones else (g,)):
+            hid = self.ln_linear(x_, blk["ln_ffn"], blk["ffn0"], relu=True)
+            ops.residual_add(x_, self.linear(hid, blk["ffn2"]))
+        return s, w, g, c, buf_w, zc, w_out, cells
+
+    def _cell_stage(self, blk, nxt, s, c, T: _Tables, zc_cr, zw_cr, zw_wr):
+        """model.py:397-490. Returns the window update of the read-back (not
+        yet applied), the updated cells, the next block's LN_cr_c(c) and, after
+        the last block, ln_out(c) (fp32)."""
+        cfg, cd, h = self.cfg, self.cd, self.h
+        zstate = self.ln(c, blk["ln_c"]) if cfg.cell_structure else None
+        q = self.linear(zc_cr, blk["cr_wq"])
+        kv = self.linear(zw_cr, blk["cr_kv"])
+        read = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["cr_bias"], blk["cr_vclass"], T.cell_ptr,
+                                     T.dec_window, T.dec_class, out_dtype=cd)
+        reads = self.linear(read, blk["cr_wo"])
+        simple = not (cfg.cell_structure or cfg.cell_adjacency)
+        if cfg.cell_nodes:
+            (zc_rad,) = self.update(c, reads, [blk["ln_radius_c"]])
+            q = self.linear(zc_rad, blk["radius_wq"])
+            kv = self.ln_linear(s, blk["ln_radius_s"], blk["radius_kv"])
+            read = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["radius_bias"], blk["radius_vclass"], T.r_ptr,
+                                         T.r_src, T.r_cls, skip_ptr=T.skip, out_dtype=cd)
+            y = self.linear(read, blk["radius_wo"])
+            if cfg.cell_structure:
+                reads = (reads.float() + y.float()).to(cd)
+        else:
+            y = reads
+        exit_ln = (nxt["ln_cr_c"], None) if nxt is not None else (self.ln_out, torch.empty(
+            c.shape[0], h, dtype=torch.float32, device=c.device))
+        if simple:
+            zc_wr, zc_out = self.update(c, y, [blk["ln_wr_c"], exit_ln])
+        else:
+            self.update(c, y, [])
+            if cfg.cell_structure:
+                mlp = blk["mlp_c"]
+                buf = torch.cat([zstate, reads], 1)
+                ops.residual_add(c, self.linear(self.linear(buf, mlp[0], relu=True), mlp[1]))
+            if cfg.cell_adjacency:
+                q = self.ln_linear(c, blk["ln_adj_q"], blk["adj_wq"])
+                kv = self.ln_linear(c, blk["ln_adj_k"], blk["adj_kv"])
+                read = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["adj_bias"], blk["adj_vclass"], T.a_ptr,
+                                             T.a_src, T.a_cls, skip_ptr=T.skip, out_dtype=cd)
+                ops.residual_add(c, self.linear(read, blk["adj_wo"]))
+            zc_wr, zc_out = self.update(c, None, [blk["ln_wr_c"], exit_ln])
+        q = self.linear(zw_wr, blk["wr_wq"])
+        kv = self.linear(zc_wr, blk["wr_kv"])
+        back = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["wr_bias"], None, T.win_ptr, T.edge_wcell,
+                                     T.edge_wclass, out_dtype=cd)
+        y_w = self.linear(back, blk["wr_wo"])
+        if nxt is not None:
+            return y_w, c, zc_out, None
+        return y_w, c, None, zc_out
 
     # ---------------------------------------------------------------- heads
     def heads(self, w: Tensor, g: Tensor, cells, b: Batch):

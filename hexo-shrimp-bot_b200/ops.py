@@ -238,6 +238,28 @@ def layer_norm(x, gamma, beta, out_dtype=None, out=None, rows=None, eps=1e-5):
     return out
 
 
+def add_ln(x, y=None, y_bias=None, outs=(), eps=1e-5):
+    """x += y (+ y_bias) in place, then LN_j(x) into each of ``outs``: a list of
+    (gamma, beta, out tensor) with up to three entries (out views allowed)."""
+    _rowmajor(x, "x")
+    if len(outs) > 3:
+        raise ValueError("add_ln takes at most three LayerNorm outputs")
+    if y is not None:
+        _rowmajor(y, "y")
+    args = []
+    for j in range(3):
+        if j < len(outs):
+            g, b, o = outs[j]
+            _rowmajor(o, "out")
+            args += [ptr(g), ptr(b), ptr(o), dtype_code(o.dtype), o.stride(0)]
+        else:
+            args += [None, None, None, 0, 0]
+    call("mb_add_ln", ptr(x), x.stride(0), ptr(y), dtype_code(y.dtype) if y is not None else 0,
+         y.stride(0) if y is not None else 0, ptr(y_bias), x.shape[0], x.shape[1], float(eps), *args,
+         stream_of(x.device))
+    return [o for _, _, o in outs]
+
+
 def embed(ta, ia, tb=None, ib=None, n=None):
     n = n if n is not None else ia.shape[0]
     h = ta.shape[1]

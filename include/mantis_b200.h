@@ -161,6 +161,17 @@ int mb_layer_norm(const void* x, int x_dtype, int64_t ldx, const int64_t* in_row
                   const float* gamma, const float* beta, float eps, void* out, int out_dtype, int64_t ldo,
                   void* stream);
 
+/* Residual update fused with the LayerNorms that read it next:
+ *   x[r] += y[r] (+ y_bias)           (skipped when y == NULL)
+ *   o_j[r] = LN(x[r]; g_j, b_j)        for each given output j (up to 3, in order)
+ * x fp32 (in place), y f32/bf16, outputs f32/bf16 with their own strides.
+ * Replaces the residual-add + nn.LayerNorm pairs between the trunk's stages
+ * (model.py:436-452, 480-489, 539-541, 570-580, 681-692, 973-985). */
+int mb_add_ln(float* x, int64_t ldx, const void* y, int y_dtype, int64_t ldy, const float* y_bias, int64_t n,
+              int64_t h, float eps, const float* g0, const float* b0, void* o0, int o0_dtype, int64_t ld0,
+              const float* g1, const float* b1, void* o1, int o1_dtype, int64_t ld1, const float* g2,
+              const float* b2, void* o2, int o2_dtype, int64_t ld2, void* stream);
+
 /* out[i] = ta[ia[i]] + (tb ? tb[ib ? ib[i] : i] : 0): embedding lookups and
  * their sums (model.py:909-912, 929). fp32 tables and output. */
 int mb_embed(const float* ta, int64_t n_ta, const int64_t* ia, const float* tb, int64_t n_tb, const int64_t* ib,
