@@ -33,6 +33,7 @@ SIGNATURES = {
     "mb_run_reduce": "pillppllplplpilp",
     "mb_row_encode": "pilplppplpppilpip",
     "mb_cell_pass": "pilplplpppplppip",
+    "mb_cell_pass_noalloc": "pilplplpppplpip",
     "mb_segment_attention": "plpplilliiplpipppppilppp",
     "mb_stone_attention": "pppiliilllplplipilllp",
     "mb_window_latent_read": "plpplilliipppippp",

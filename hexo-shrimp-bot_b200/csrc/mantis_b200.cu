@@ -6,3 +6,4 @@
 #include "attention.cu"
 #include "gemm_simt.cu"
 #include "gemm_sm100.cu"
+#include "noalloc.cu"
