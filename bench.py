@@ -219,8 +219,7 @@ def run_ours(args, rank, world, local_rank):
 
     def step_device():
         for _ in range(n_chunks):
-            w, g, cells = eng.trunk(dev_batch)
-            policy, critic = eng.heads(w, g, cells, dev_batch)
+            policy, critic = eng.evaluate(dev_batch)
             ops.compose(critic, dev_batch.legal_offsets, 0.2)
 
     def barrier():
@@ -240,12 +239,15 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     calls0 = lib.call_count()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    eng.probe = {}
     with ClockSampler(local_rank) as clocks:
         start.record()
         for _ in range(args.steps):
             step_device()
         end.record()
         torch.cuda.synchronize()
+    probe, eng.probe = eng.probe, None
+    tables = eng.tables
     launches = (lib.call_count() - calls0) // max(args.steps, 1)
     ms = max_over_ranks(start.elapsed_time(end) / args.steps)
     positions_per_step = n_chunks * args.chunk
@@ -273,9 +275,9 @@ def run_ours(args, rank, world, local_rank):
     h2d = batch_bytes(host, fields) * n_chunks
     d2h = 3 * host.n_cells * 4 * n_chunks
 
-    # Roofline of the dominant native kernel: the radius read (typed segment
-    # attention cells <- stones), timed alone on this chunk's tables.
-    roof = radius_roofline(eng, dev_batch, cfg, args) if rank == 0 else None
+    # Roofline of the dominant native kernel, the radius read, from its
+    # launches inside the timed region.
+    roof = radius_roofline(probe, tables, cfg) if rank == 0 else None
 
     # p50 batch-64 latency (config-4 distribution: 40-150 stones), end to end
     p50 = None
@@ -327,40 +329,33 @@ def run_ours(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
-def radius_roofline(eng, b, cfg, args):
-    import torch
+def radius_read_bytes(T, cfg):
+    """Algorithmic HBM bytes of one radius read (cells <- stones): per cell its
+    bf16 query row in and output row out plus its run bound; per edge the int64
+    source and class; each stone's bf16 K and V rows once; the bf16 class value
+    rows and fp32 bias rows once."""
+    h, n_cls = cfg.h, 192
+    return (T.N_c * h * 2 * 2 + (T.N_c + 1) * 8 + int(T.r_src.numel()) * 16 + T.N_s * 2 * h * 2
+            + n_cls * h * 2 + cfg.heads * n_cls * 4)
 
-    mb = _pkg()
-    ops = mb.ops
-    T = mb.model._Tables(cfg, b)
-    h = cfg.h
-    blk = eng.blocks[0]
-    q = torch.randn(T.N_c, h, device=b.stone_own.device).to(torch.bfloat16)
-    kv = torch.randn(T.N_s, 2 * h, device=b.stone_own.device).to(torch.bfloat16)
-    out = torch.empty(T.N_c, h, dtype=torch.bfloat16, device=q.device)
 
-    def launch():
-        ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["radius_bias"], blk["radius_vclass"], T.r_ptr, T.r_src,
-                              T.r_cls, out=out, out_dtype=torch.bfloat16)
-
-    for _ in range(3):
-        launch()
-    torch.cuda.synchronize()
-    n = 20
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(n):
-        launch()
-    e1.record()
-    torch.cuda.synchronize()
-    sec = e0.elapsed_time(e1) / n / 1000.0
-    e_r = int(T.r_src.numel())
-    algo = T.N_c * h * 2 * 2 + T.N_s * 2 * h * 2 + e_r * 16 + (T.N_c + 1) * 8 + 192 * h * 4
+def radius_roofline(probe, T, cfg):
+    """The radius read's launches inside the timed region (CUDA events on the
+    launching stream around each launch, recorded by the engine's probe)."""
+    ev = probe.get("radius_read", [])
+    if not ev:
+        return None
+    ms = [s.elapsed_time(e) for s, e in ev]
+    sec = statistics.mean(ms) / 1000.0
+    algo = radius_read_bytes(T, cfg)
     pk, kind = peaks()
     achieved = algo / sec / 1e9
-    return {"kernel": "segment_attention (radius read, cells<-stones)", "bound": "hbm", "achieved": achieved,
-            "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": None,
-            "peak_kind": kind, "algorithmic_bytes": algo, "launch_ms": sec * 1000.0, "edges": e_r}
+    cell_ms = [s.elapsed_time(e) for s, e in probe.get("cell_read", [])]
+    return {"kernel": "segment_attention_grouped (radius read, cells<-stones)", "bound": "hbm",
+            "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+            "traffic": None, "peak_kind": kind, "algorithmic_bytes": algo, "launch_ms": sec * 1000.0,
+            "launches_timed": len(ms), "edges": int(T.r_src.numel()),
+            "cell_read_launch_ms": statistics.mean(cell_ms) if cell_ms else None}
 
 
 def main():

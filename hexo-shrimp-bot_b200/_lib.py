@@ -31,10 +31,11 @@ SIGNATURES = {
     "mb_radius_class": "pppplpp",
     "mb_div_i64": "pllpp",
     "mb_run_reduce": "pillppllplplpilp",
-    "mb_row_encode": "pilplppplpppilpip",
+    "mb_row_encode": "pilplppplpppilpilp",
     "mb_cell_pass": "pilplplpppplppip",
     "mb_cell_pass_noalloc": "pilplplpppplpip",
     "mb_segment_attention": "plpplilliiplpipppppilppp",
+    "mb_segment_attention_grouped": "plpplilliiplpippppppllpilp",
     "mb_stone_attention": "pppiliilllplplipilllp",
     "mb_window_latent_read": "plpplilliipppippp",
     "mb_window_latent_broadcast": "plpplilliippippp",

@@ -3,19 +3,23 @@
 //  K3  typed segment attention (cells<-windows, cells<-stones radius,
 //      windows<-cells, cell adjacency): one warp per query row covering every
 //      head; lane l holds VEC columns, lanes_per_head = head_dim / VEC lanes
-//      share one head. Edges are consumed two at a time so two gathered K/V
-//      rows are in flight per warp.
+//      share one head; two edges per iteration. The grouped form (radius
+//      read) stages each position's sources in shared memory and rescales
+//      once per chunk of eight edges.
+//  K4  window-latent read (a cluster of CTAs per position, merged through
+//      distributed shared memory), broadcast (warp per window) and the
+//      dense 4x4 latent mix.
 //  K1  stone attention over [4 latents; stones] per position: one thread per
 //      query row, K/V tiles staged in shared memory as fp32 and read by
 //      broadcast, online softmax in chunks of 8 keys.
-//  K4  window-latent read (block per position, warps split the window run,
-//      merged through shared memory), broadcast (warp per window) and the
-//      dense 4x4 latent mix.
 //
 // Scores use exp(x - running max); an empty run returns zero with l = 0.
 #include <math.h>
 
+#include <algorithm>
 #include <type_traits>
+
+#include <cooperative_groups.h>
 
 #include "common.cuh"
 
@@ -23,25 +27,99 @@ namespace mb {
 
 constexpr float kNegInf = -INFINITY;
 
+// ------------------------------------------------------- row loads
+// VEC elements of T as loaded from memory, unpacked to fp32 on use.
+template <typename T, int VEC> struct Raw;
+template <int VEC> struct Raw<float, VEC> { float w[VEC]; };
+template <int VEC> struct Raw<__nv_bfloat16, VEC> { uint32_t w[VEC >= 2 ? VEC / 2 : 1]; };
+
+template <bool SMEM, int VEC>
+__device__ __forceinline__ void raw_load(const float* p, Raw<float, VEC>& r) {
+  if constexpr (VEC % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < VEC / 4; ++i) {
+      const float4 f = SMEM ? reinterpret_cast<const float4*>(p)[i] : __ldg(reinterpret_cast<const float4*>(p) + i);
+      r.w[4 * i] = f.x; r.w[4 * i + 1] = f.y; r.w[4 * i + 2] = f.z; r.w[4 * i + 3] = f.w;
+    }
+  } else if constexpr (VEC == 2) {
+    const float2 f = SMEM ? *reinterpret_cast<const float2*>(p) : __ldg(reinterpret_cast<const float2*>(p));
+    r.w[0] = f.x; r.w[1] = f.y;
+  } else {
+    r.w[0] = SMEM ? *p : __ldg(p);
+  }
+}
+template <bool SMEM, int VEC>
+__device__ __forceinline__ void raw_load(const __nv_bfloat16* p, Raw<__nv_bfloat16, VEC>& r) {
+  if constexpr (VEC % 8 == 0) {
+#pragma unroll
+    for (int i = 0; i < VEC / 8; ++i) {
+      const uint4 u = SMEM ? reinterpret_cast<const uint4*>(p)[i] : __ldg(reinterpret_cast<const uint4*>(p) + i);
+      r.w[4 * i] = u.x; r.w[4 * i + 1] = u.y; r.w[4 * i + 2] = u.z; r.w[4 * i + 3] = u.w;
+    }
+  } else if constexpr (VEC == 4) {
+    const uint2 u = SMEM ? *reinterpret_cast<const uint2*>(p) : __ldg(reinterpret_cast<const uint2*>(p));
+    r.w[0] = u.x; r.w[1] = u.y;
+  } else if constexpr (VEC == 2) {
+    r.w[0] = SMEM ? *reinterpret_cast<const uint32_t*>(p) : __ldg(reinterpret_cast<const unsigned int*>(p));
+  } else {
+    const unsigned short b = SMEM ? *reinterpret_cast<const unsigned short*>(p)
+                                  : __ldg(reinterpret_cast<const unsigned short*>(p));
+    r.w[0] = (uint32_t)b;
+  }
+}
+template <int VEC>
+__device__ __forceinline__ void raw_unpack(const Raw<float, VEC>& r, float* out) {
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) out[i] = r.w[i];
+}
+template <int VEC>
+__device__ __forceinline__ void raw_unpack(const Raw<__nv_bfloat16, VEC>& r, float* out) {
+  if constexpr (VEC >= 2) {
+#pragma unroll
+    for (int i = 0; i < VEC / 2; ++i) {
+      out[2 * i] = __uint_as_float(r.w[i] << 16);
+      out[2 * i + 1] = __uint_as_float(r.w[i] & 0xffff0000u);
+    }
+  } else {
+    out[0] = __uint_as_float(r.w[0] << 16);
+  }
+}
+
+// Sum over aligned groups of LPH lanes; LPH == 0 reads the group from `lph`.
+template <int LPH>
+__device__ __forceinline__ float head_sum(float x, int lph) {
+  if constexpr (LPH > 0) {
+#pragma unroll
+    for (int o = LPH >> 1; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    return x;
+  } else {
+    return group_sum(x, lph);
+  }
+}
+
 // ------------------------------------------------------- segment attention
-// One warp per query row, blocks of 8 warps over consecutive rows, scheduled
-// in row order: the GPU works on a narrow band of positions at a time, so the
-// gathered source rows stay L2-resident. Two edges per iteration keep two
-// K/V row pairs in flight per lane at 80 registers (3 blocks per SM); wider
-// per-lane pipelines were measured slower at the bench's sizes because they
-// cost resident warps.
+// One warp per batch of kSegRows consecutive query rows (blocks of 8 warps,
+// scheduled in row order, so the GPU works on a narrow band of positions at a
+// time and the gathered source rows stay L2-resident). The batch's run bounds
+// and its first 32 edge indices are fetched by one coalesced load each and
+// broadcast by shuffle, so a row waits on one round trip (its K/V gathers,
+// issued together with its query load) instead of three (run bounds, edge
+// indices, gathers). Two edges per iteration keep two K/V row pairs in flight
+// per lane.
 constexpr int kSegWarps = 8;
+constexpr int kSegRows = 4;
 
 template <typename T, typename TO, typename TV, int VEC, bool HAS_VCLS>
-__global__ void __launch_bounds__(kSegWarps * 32) segment_attention_kernel(
+__global__ void __launch_bounds__(kSegWarps * 32, 3) segment_attention_kernel(
     const T* __restrict__ q, int64_t ldq, const T* __restrict__ k, const T* __restrict__ v, int64_t ldkv, int64_t n_q,
     int64_t n_src, int heads, int hd, const float* __restrict__ bias, int64_t n_cls, const TV* __restrict__ vcls,
     const int64_t* __restrict__ seg_ptr, const int64_t* __restrict__ src, const int64_t* __restrict__ cls,
     const int64_t* __restrict__ skip_ptr, TO* __restrict__ out, int64_t ldo, float* __restrict__ m_out,
     float* __restrict__ l_out, float scale) {
-  const int64_t row = (int64_t)blockIdx.x * kSegWarps + (threadIdx.x >> 5);
-  if (row >= n_q) return;
+  const int64_t row0 = ((int64_t)blockIdx.x * kSegWarps + (threadIdx.x >> 5)) * kSegRows;
+  if (row0 >= n_q) return;
   const int lane = threadIdx.x & 31;
+  const int nrows = (int)(n_q - row0 < kSegRows ? n_q - row0 : kSegRows);
   const int lph = hd / VEC;  // lanes per head
   const int head = lane / lph;
   const int H = heads * hd;
@@ -49,89 +127,316 @@ __global__ void __launch_bounds__(kSegWarps * 32) segment_attention_kernel(
   // Widths below one warp (H < 32, VEC == 1) leave the upper lanes idle; they
   // still join the shuffles with zero partial sums.
   const bool live = col < H;
-  float qv[VEC];
-#pragma unroll
-  for (int i = 0; i < VEC; ++i) qv[i] = 0.f;
-  if (live) load_vec<VEC>(q + row * ldq + col, qv);
-#pragma unroll
-  for (int i = 0; i < VEC; ++i) qv[i] *= scale;
-  int64_t beg = seg_ptr[row], end = seg_ptr[row + 1];
-  if (skip_ptr && skip_ptr[row + 1] > skip_ptr[row]) end = beg;
   const float* brow = bias + (int64_t)(live ? head : 0) * n_cls;
-  float m = kNegInf, l = 0.f, acc[VEC];
-#pragma unroll
-  for (int i = 0; i < VEC; ++i) acc[i] = 0.f;
-
-  auto consume = [&](float score, const float* vv) {
-    const float m_new = fmaxf(m, score);
-    const float corr = __expf(m - m_new);
-    const float p = __expf(score - m_new);
-    l = l * corr + p;
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) acc[i] = acc[i] * corr + p * vv[i];
-    m = m_new;
-  };
-  auto add_class_row = [&](int64_t c, float* vv) {
-    if constexpr (HAS_VCLS) {
-      if (live) {
-        float a[VEC];
-        load_vec<VEC>(vcls + c * H + col, a);
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) vv[i] += a[i];
-      }
-    }
-  };
-
-  int64_t e = beg;
-  for (; e + 1 < end; e += 2) {
-    const int64_t s0 = src[e], s1 = src[e + 1], c0 = cls[e], c1 = cls[e + 1];
-    if (s0 < 0 || s0 >= n_src || s1 < 0 || s1 >= n_src || c0 < 0 || c0 >= n_cls || c1 < 0 || c1 >= n_cls) {
-      report(ERR_INDEX);
-      continue;
-    }
-    float k0[VEC] = {}, k1[VEC] = {}, v0[VEC] = {}, v1[VEC] = {};
-    if (live) {
-      load_vec<VEC>(k + s0 * ldkv + col, k0);
-      load_vec<VEC>(k + s1 * ldkv + col, k1);
-      load_vec<VEC>(v + s0 * ldkv + col, v0);
-      load_vec<VEC>(v + s1 * ldkv + col, v1);
-    }
-    float d0 = 0.f, d1 = 0.f;
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) { d0 += qv[i] * k0[i]; d1 += qv[i] * k1[i]; }
-    d0 = group_sum(d0, lph) + __ldg(brow + c0);
-    d1 = group_sum(d1, lph) + __ldg(brow + c1);
-    add_class_row(c0, v0);
-    add_class_row(c1, v1);
-    consume(d0, v0);
-    consume(d1, v1);
+  // lane i holds the batch's run bound i and whether row i is skipped
+  const int64_t bound = lane <= nrows ? seg_ptr[row0 + lane] : 0;
+  int skipped = 0;
+  if (skip_ptr && lane < nrows) skipped = skip_ptr[row0 + lane + 1] > skip_ptr[row0 + lane];
+  const int64_t e0 = __shfl_sync(0xffffffffu, bound, 0), e1 = __shfl_sync(0xffffffffu, bound, nrows);
+  int64_t my_src = 0, my_cls = 0;  // the batch's edge e0 + lane
+  if (e0 + lane < e1) {
+    my_src = src[e0 + lane];
+    my_cls = cls[e0 + lane];
   }
-  if (e < end) {
-    const int64_t s0 = src[e], c0 = cls[e];
-    if (s0 < 0 || s0 >= n_src || c0 < 0 || c0 >= n_cls) {
-      report(ERR_INDEX);
+  auto fetch = [&](int64_t e, int64_t& s, int64_t& c) {
+    const int64_t i = e - e0;  // warp-uniform
+    if (i < 32) {
+      s = __shfl_sync(0xffffffffu, my_src, (int)i);
+      c = __shfl_sync(0xffffffffu, my_cls, (int)i);
     } else {
-      float k0[VEC] = {}, v0[VEC] = {};
+      s = src[e];
+      c = cls[e];
+    }
+  };
+
+  for (int r = 0; r < nrows; ++r) {
+    const int64_t row = row0 + r;
+    float qv[VEC];
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) qv[i] = 0.f;
+    if (live) load_vec<VEC>(q + row * ldq + col, qv);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) qv[i] *= scale;
+    const int64_t beg = __shfl_sync(0xffffffffu, bound, r);
+    int64_t end = __shfl_sync(0xffffffffu, bound, r + 1);
+    if (__shfl_sync(0xffffffffu, skipped, r)) end = beg;
+    float m = kNegInf, l = 0.f, acc[VEC];
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) acc[i] = 0.f;
+
+    auto consume = [&](float score, const float* vv) {
+      const float m_new = fmaxf(m, score);
+      const float corr = __expf(m - m_new);
+      const float p = __expf(score - m_new);
+      l = l * corr + p;
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) acc[i] = acc[i] * corr + p * vv[i];
+      m = m_new;
+    };
+    auto add_class_row = [&](int64_t c, float* vv) {
+      if constexpr (HAS_VCLS) {
+        if (live) {
+          float a[VEC];
+          load_vec<VEC>(vcls + c * H + col, a);
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) vv[i] += a[i];
+        }
+      }
+    };
+
+    int64_t e = beg;
+    for (; e + 1 < end; e += 2) {
+      int64_t s0, s1, c0, c1;
+      fetch(e, s0, c0);
+      fetch(e + 1, s1, c1);
+      if (s0 < 0 || s0 >= n_src || s1 < 0 || s1 >= n_src || c0 < 0 || c0 >= n_cls || c1 < 0 || c1 >= n_cls) {
+        report(ERR_INDEX);
+        continue;
+      }
+      float k0[VEC] = {}, k1[VEC] = {}, v0[VEC] = {}, v1[VEC] = {};
       if (live) {
         load_vec<VEC>(k + s0 * ldkv + col, k0);
+        load_vec<VEC>(k + s1 * ldkv + col, k1);
         load_vec<VEC>(v + s0 * ldkv + col, v0);
+        load_vec<VEC>(v + s1 * ldkv + col, v1);
       }
-      float d0 = 0.f;
+      float d0 = 0.f, d1 = 0.f;
 #pragma unroll
-      for (int i = 0; i < VEC; ++i) d0 += qv[i] * k0[i];
+      for (int i = 0; i < VEC; ++i) { d0 += qv[i] * k0[i]; d1 += qv[i] * k1[i]; }
       d0 = group_sum(d0, lph) + __ldg(brow + c0);
+      d1 = group_sum(d1, lph) + __ldg(brow + c1);
       add_class_row(c0, v0);
+      add_class_row(c1, v1);
       consume(d0, v0);
+      consume(d1, v1);
+    }
+    if (e < end) {
+      int64_t s0, c0;
+      fetch(e, s0, c0);
+      if (s0 < 0 || s0 >= n_src || c0 < 0 || c0 >= n_cls) {
+        report(ERR_INDEX);
+      } else {
+        float k0[VEC] = {}, v0[VEC] = {};
+        if (live) {
+          load_vec<VEC>(k + s0 * ldkv + col, k0);
+          load_vec<VEC>(v + s0 * ldkv + col, v0);
+        }
+        float d0 = 0.f;
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) d0 += qv[i] * k0[i];
+        d0 = group_sum(d0, lph) + __ldg(brow + c0);
+        add_class_row(c0, v0);
+        consume(d0, v0);
+      }
+    }
+    const float inv = l > 0.f ? 1.f / l : 1.f;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) acc[i] *= inv;
+    if (live) {
+      store_vec<VEC>(out + row * ldo + col, acc);
+      if (m_out && (lane % lph) == 0) {
+        m_out[row * heads + head] = m;
+        l_out[row * heads + head] = l;
+      }
     }
   }
-  const float inv = l > 0.f ? 1.f / l : 1.f;
+}
+
+// ---------------------------------------- grouped (source-staged) segment
+// When query rows and sources split into aligned groups (the radius read:
+// a position's cells attend only to that position's stones), one CTA takes
+// one group and one 64-column block (whole heads): it copies the group's K|V
+// columns, the class value rows and the bias rows into shared memory once,
+// so every gathered source row is a conflict-free shared-memory read instead
+// of an L2 round trip. Eight lanes hold one query row (8 bf16 columns each),
+// a warp carries four rows and a CTA 16 warps. Edges go in chunks of eight:
+// the row's lanes fetch the chunk's indices at once and broadcast them by
+// shuffle, a first pass scores every edge of the chunk, and a second pass
+// rescales the running state once and accumulates the value rows. Nothing
+// is held in registers across the passes but the scores and the packed
+// indices, so 32 warps fit on an SM to hide the shared-memory latency.
+constexpr int kGrpCols = 64;
+constexpr int kGrpWarps = 16;
+constexpr int kGrpChunk = 8;
+constexpr int kGrpClsBits = 11;  // packed edge: local source << 11 | class
+constexpr int kGrpKvRowBytes = 2 * kGrpCols * 2;  // K then V, bf16
+
+template <typename TV>
+__host__ __device__ constexpr int grp_vcls_bytes(int64_t n_cls) {
+  return (int)(((n_cls * kGrpCols * (int64_t)sizeof(TV)) + 15) / 16 * 16);
+}
+__host__ __device__ constexpr int grp_bias_bytes(int heads_in_block, int64_t n_cls) {
+  return (int)((heads_in_block * n_cls * 4 + 15) / 16 * 16);
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
+}
+
+// One chunk-by-chunk pass over the four rows a warp holds. Source r's K and V
+// columns are at kb + r * ld and vb + r * ld (offset by the lane's column).
+template <int LPH, bool KV_SMEM, bool HAS_VCLS, typename TV>
+__device__ __forceinline__ void grouped_rows(const float (&qv)[8], int64_t beg, int n, int nmax,
+                                             const int64_t* __restrict__ src, const int64_t* __restrict__ cls,
+                                             int64_t s0, int64_t ns, int64_t n_cls, const __nv_bfloat16* kb,
+                                             const __nv_bfloat16* vb, int64_t ld, const float* brow, const TV* vc,
+                                             int lph, float& m, float& l, float (&acc)[8]) {
+  const int lane = threadIdx.x & 31;
+  const int g0 = lane & ~7, li = lane & 7;
+  for (int j0 = 0; j0 < nmax; j0 += kGrpChunk) {
+    int mine = -1;
+    if (j0 + li < n) {
+      const int64_t s = src[beg + j0 + li] - s0, c = cls[beg + j0 + li];
+      if ((uint64_t)s < (uint64_t)ns && (uint64_t)c < (uint64_t)n_cls) mine = (int)(s << kGrpClsBits | c);
+      else report(ERR_INDEX);
+    }
+    const int steps = min(kGrpChunk, nmax - j0);
+    int pk[kGrpChunk];
+    float sc[kGrpChunk];
+    float cmax = kNegInf;
 #pragma unroll
-  for (int i = 0; i < VEC; ++i) acc[i] *= inv;
-  if (!live) return;
-  store_vec<VEC>(out + row * ldo + col, acc);
-  if (m_out && (lane % lph) == 0) {
-    m_out[row * heads + head] = m;
-    l_out[row * heads + head] = l;
+    for (int j = 0; j < kGrpChunk; ++j) {
+      pk[j] = -1;
+      sc[j] = kNegInf;
+      if (j < steps) {
+        pk[j] = __shfl_sync(0xffffffffu, mine, g0 + j);
+        float d = 0.f;
+        if (pk[j] >= 0) {
+          Raw<__nv_bfloat16, 8> kr;
+          raw_load<KV_SMEM, 8>(kb + (int64_t)(pk[j] >> kGrpClsBits) * ld, kr);
+          float kk[8];
+          raw_unpack<8>(kr, kk);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) d += qv[i] * kk[i];
+        }
+        d = head_sum<LPH>(d, lph);
+        if (pk[j] >= 0) {
+          sc[j] = d + brow[pk[j] & ((1 << kGrpClsBits) - 1)];
+          cmax = fmaxf(cmax, sc[j]);
+        }
+      }
+    }
+    if (cmax != kNegInf) {
+      const float m_new = fmaxf(m, cmax);
+      const float corr = __expf(m - m_new);
+      l *= corr;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] *= corr;
+#pragma unroll
+      for (int j = 0; j < kGrpChunk; ++j) {
+        if (j < steps && pk[j] >= 0) {
+          const float p = __expf(sc[j] - m_new);
+          l += p;
+          Raw<__nv_bfloat16, 8> vr;
+          raw_load<KV_SMEM, 8>(vb + (int64_t)(pk[j] >> kGrpClsBits) * ld, vr);
+          float vv[8];
+          raw_unpack<8>(vr, vv);
+          if constexpr (HAS_VCLS) {
+            Raw<TV, 8> cr;
+            raw_load<true, 8>(vc + (int64_t)(pk[j] & ((1 << kGrpClsBits) - 1)) * kGrpCols, cr);
+            float a[8];
+            raw_unpack<8>(cr, a);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) vv[i] += a[i];
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[i] += p * vv[i];
+        }
+      }
+      m = m_new;
+    }
+  }
+}
+
+template <typename TO, typename TV, int LPH, bool HAS_VCLS>
+__global__ void __launch_bounds__(kGrpWarps * 32, 2) segment_attention_grouped_kernel(
+    const __nv_bfloat16* __restrict__ q, int64_t ldq, const __nv_bfloat16* __restrict__ k,
+    const __nv_bfloat16* __restrict__ v, int64_t ldkv, int64_t n_q, int64_t n_src, int hd,
+    const float* __restrict__ bias, int64_t n_cls, const TV* __restrict__ vcls, int64_t ld_vcls,
+    const int64_t* __restrict__ seg_ptr, const int64_t* __restrict__ src, const int64_t* __restrict__ cls,
+    const int64_t* __restrict__ skip_ptr, const int64_t* __restrict__ q_off, const int64_t* __restrict__ s_off,
+    int stage_rows, TO* __restrict__ out, int64_t ldo, float scale) {
+  extern __shared__ __align__(16) unsigned char grp_smem[];
+  unsigned char* smem = grp_smem;
+  const int grp = blockIdx.x;
+  const int cb = blockIdx.y * kGrpCols;
+  const int nh = kGrpCols / hd;
+  const int64_t q0 = q_off[grp], q1 = q_off[grp + 1], s0 = s_off[grp], s1 = s_off[grp + 1];
+  if (q0 < 0 || q1 < q0 || q1 > n_q || s0 < 0 || s1 < s0 || s1 > n_src || s1 - s0 >= (int64_t(1) << 20)) {
+    if (threadIdx.x == 0) report(ERR_RUN_BOUND);
+    return;
+  }
+  if (q1 == q0) return;
+  const int64_t ns = s1 - s0;
+  const bool staged = ns <= stage_rows;
+
+  float* bias_s = reinterpret_cast<float*>(smem);
+  TV* vcls_s = reinterpret_cast<TV*>(smem + grp_bias_bytes(nh, n_cls));
+  __nv_bfloat16* kv_s = reinterpret_cast<__nv_bfloat16*>(smem + grp_bias_bytes(nh, n_cls) +
+                                                         (HAS_VCLS ? grp_vcls_bytes<TV>(n_cls) : 0));
+  const int head0 = cb / hd;
+  for (int64_t i = threadIdx.x; i < nh * n_cls; i += blockDim.x) bias_s[i] = bias[head0 * n_cls + i];
+  if constexpr (HAS_VCLS) {
+    constexpr int per_row = kGrpCols * (int)sizeof(TV) / 16;
+    for (int64_t i = threadIdx.x; i < n_cls * per_row; i += blockDim.x) {
+      const int64_t c = i / per_row, part = i % per_row;
+      cp_async16(reinterpret_cast<unsigned char*>(vcls_s + c * kGrpCols) + part * 16,
+                 reinterpret_cast<const unsigned char*>(vcls + c * ld_vcls + cb) + part * 16);
+    }
+  }
+  if (staged) {
+    constexpr int per_half = kGrpCols * 2 / 16;  // 16-byte pieces of the K (or V) columns
+    for (int64_t i = threadIdx.x; i < ns * 2 * per_half; i += blockDim.x) {
+      const int64_t r = i / (2 * per_half);
+      const int part = (int)(i % (2 * per_half));
+      const __nv_bfloat16* g = (part < per_half ? k : v) + (s0 + r) * ldkv + cb;
+      cp_async16(reinterpret_cast<unsigned char*>(kv_s) + r * kGrpKvRowBytes + part * 16,
+                 reinterpret_cast<const unsigned char*>(g) + (part % per_half) * 16);
+    }
+  }
+  cp_async_wait_all();
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = lane >> 3, sl = lane & 7;
+  const int col = sl * 8;
+  const int lph = hd / 8;
+  const float* brow = bias_s + (col / hd) * n_cls;
+  for (int64_t base = q0 + warp * 4; base < q1; base += kGrpWarps * 4) {
+    const int64_t row = base + sub;
+    const bool rv = row < q1;
+    float qv[8] = {};
+    int64_t beg = 0;
+    int n = 0;
+    if (rv) {
+      load_vec<8>(q + row * ldq + cb + col, qv);
+      beg = seg_ptr[row];
+      n = (int)(seg_ptr[row + 1] - beg);
+      if (skip_ptr && skip_ptr[row + 1] > skip_ptr[row]) n = 0;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qv[i] *= scale;
+    int nmax = n;
+    nmax = max(nmax, __shfl_xor_sync(0xffffffffu, nmax, 8));
+    nmax = max(nmax, __shfl_xor_sync(0xffffffffu, nmax, 16));
+    float m = kNegInf, l = 0.f, acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    if (staged)
+      grouped_rows<LPH, true, HAS_VCLS, TV>(qv, beg, n, nmax, src, cls, s0, ns, n_cls, kv_s + col,
+                                           kv_s + kGrpCols + col, kGrpKvRowBytes / 2, brow, vcls_s + col, lph, m, l,
+                                           acc);
+    else
+      grouped_rows<LPH, false, HAS_VCLS, TV>(qv, beg, n, nmax, src, cls, s0, ns, n_cls, k + s0 * ldkv + cb + col,
+                                            v + s0 * ldkv + cb + col, ldkv, brow, vcls_s + col, lph, m, l, acc);
+    const float inv = l > 0.f ? 1.f / l : 1.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] *= inv;
+    if (rv) store_vec<8>(out + row * ldo + cb + col, acc);
   }
 }
 
@@ -230,25 +535,39 @@ __global__ void __launch_bounds__(kStoneThreads) stone_attention_kernel(
 }
 
 // ------------------------------------------------------- window latents
+// Read: a position's 4 latent queries attend over its windows. The windows
+// of one position are split over a cluster of kReadSplit CTAs (8 warps each,
+// every warp a strided share of the split, two windows per step so four K/V
+// rows are in flight); each CTA merges its warps' partial softmax states in
+// shared memory, then the cluster's first CTA merges the kReadSplit CTA
+// states through distributed shared memory and writes the output.
 constexpr int kReadWarps = 8;
+constexpr int kReadSplit = 4;
 
 template <typename T, typename TO, int VEC>
-__global__ void __launch_bounds__(kReadWarps * 32) latent_read_kernel(
+__global__ void __cluster_dims__(1, kReadSplit, 1) __launch_bounds__(kReadWarps * 32) latent_read_kernel(
     const T* __restrict__ q, int64_t ldq, const T* __restrict__ k, const T* __restrict__ v, int64_t ldkv,
     int64_t n_windows, int heads, int hd, const int64_t* __restrict__ offsets, const int64_t* __restrict__ order,
     TO* __restrict__ out, float* __restrict__ m_out, float* __restrict__ l_out, float scale) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
   extern __shared__ float smem[];
   const int64_t p = blockIdx.x;
+  const int rank = (int)cluster.block_rank();
   const int H = heads * hd;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int lph = hd / VEC;
-  const int head = lane / lph;
   const int chunks = (H + 32 * VEC - 1) / (32 * VEC);  // column chunks per row
-  const int64_t beg = offsets[p], end = offsets[p + 1];
-  // shared layout: [warp][slot][H] acc, then [warp][slot][heads] m and l
+  const int64_t b0 = offsets[p], len = offsets[p + 1] - b0;
+  const int64_t beg = b0 + len * rank / kReadSplit, end = b0 + len * (rank + 1) / kReadSplit;
+  // shared layout: [warp][slot][H] acc, [warp][slot][heads] m and l, then the
+  // CTA's merged state: [slot][H] acc, [slot][heads] m and l
   float* s_acc = smem;
   float* s_m = s_acc + kReadWarps * 4 * H;
   float* s_l = s_m + kReadWarps * 4 * heads;
+  float* c_acc = s_l + kReadWarps * 4 * heads;
+  float* c_m = c_acc + 4 * H;
+  float* c_l = c_m + 4 * heads;
   for (int ch = 0; ch < chunks; ++ch) {
     const int col = ch * 32 * VEC + lane * VEC;
     const bool live = col < H;  // H < 32 leaves upper lanes idle
@@ -262,14 +581,10 @@ __global__ void __launch_bounds__(kReadWarps * 32) latent_read_kernel(
       m[s] = kNegInf;
       l[s] = 0.f;
     }
-    for (int64_t i = beg + warp; i < end; i += kReadWarps) {
-      const int64_t w = order[i];
-      if (w < 0 || w >= n_windows) { report(ERR_INDEX); continue; }
-      float kv[VEC] = {}, vv[VEC] = {};
-      if (live) {
-        load_vec<VEC>(k + w * ldkv + col, kv);
-        load_vec<VEC>(v + w * ldkv + col, vv);
-      }
+    auto consume = [&](const Raw<T, VEC>& kr, const Raw<T, VEC>& vr) {
+      float kv[VEC], vv[VEC];
+      raw_unpack<VEC>(kr, kv);
+      raw_unpack<VEC>(vr, vv);
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
         float d = 0.f;
@@ -283,6 +598,23 @@ __global__ void __launch_bounds__(kReadWarps * 32) latent_read_kernel(
         for (int u = 0; u < VEC; ++u) acc[s][u] = acc[s][u] * corr + pr * vv[u];
         m[s] = m_new;
       }
+    };
+    for (int64_t i = beg + warp; i < end; i += 2 * kReadWarps) {
+      const int64_t i1 = i + kReadWarps;
+      int64_t w0 = order[i], w1 = i1 < end ? order[i1] : -1;
+      const bool ok0 = w0 >= 0 && w0 < n_windows, ok1 = i1 < end && w1 >= 0 && w1 < n_windows;
+      if (!ok0 || (i1 < end && !ok1)) report(ERR_INDEX);
+      Raw<T, VEC> k0 = {}, v0 = {}, k1 = {}, v1 = {};
+      if (live && ok0) {
+        raw_load<false, VEC>(k + w0 * ldkv + col, k0);
+        raw_load<false, VEC>(v + w0 * ldkv + col, v0);
+      }
+      if (live && ok1) {
+        raw_load<false, VEC>(k + w1 * ldkv + col, k1);
+        raw_load<false, VEC>(v + w1 * ldkv + col, v1);
+      }
+      if (ok0) consume(k0, v0);
+      if (ok1) consume(k1, v1);
     }
     if (!live) continue;
 #pragma unroll
@@ -295,8 +627,8 @@ __global__ void __launch_bounds__(kReadWarps * 32) latent_read_kernel(
       }
     }
   }
-  (void)head;
   __syncthreads();
+  // this CTA's state: merge the warps (acc stays unnormalised)
   for (int idx = threadIdx.x; idx < 4 * H; idx += blockDim.x) {
     const int s = idx / H, col = idx % H, hh = col / hd;
     float mm = kNegInf;
@@ -311,14 +643,44 @@ __global__ void __launch_bounds__(kReadWarps * 32) latent_read_kernel(
         aa += f * s_acc[(w * 4 + s) * H + col];
       }
     }
-    out[(p * 4 + s) * H + col] = from_f<TO>(ll > 0.f ? aa / ll : 0.f);
-    if (m_out && (col % hd) == 0) {
-      m_out[(p * 4 + s) * heads + hh] = mm;
-      l_out[(p * 4 + s) * heads + hh] = ll;
+    c_acc[s * H + col] = aa;
+    if (col % hd == 0) {
+      c_m[s * heads + hh] = mm;
+      c_l[s * heads + hh] = ll;
     }
   }
+  cluster.sync();
+  if (rank == 0) {
+    for (int idx = threadIdx.x; idx < 4 * H; idx += blockDim.x) {
+      const int s = idx / H, col = idx % H, hh = col / hd;
+      float mr[kReadSplit], mm = kNegInf;
+#pragma unroll
+      for (int r = 0; r < kReadSplit; ++r) {
+        mr[r] = cluster.map_shared_rank(c_m, r)[s * heads + hh];
+        mm = fmaxf(mm, mr[r]);
+      }
+      float ll = 0.f, aa = 0.f;
+      if (mm != kNegInf) {
+#pragma unroll
+        for (int r = 0; r < kReadSplit; ++r) {
+          if (mr[r] == kNegInf) continue;
+          const float f = __expf(mr[r] - mm);
+          ll += f * cluster.map_shared_rank(c_l, r)[s * heads + hh];
+          aa += f * cluster.map_shared_rank(c_acc, r)[s * H + col];
+        }
+      }
+      out[(p * 4 + s) * H + col] = from_f<TO>(ll > 0.f ? aa / ll : 0.f);
+      if (m_out && (col % hd) == 0) {
+        m_out[(p * 4 + s) * heads + hh] = mm;
+        l_out[(p * 4 + s) * heads + hh] = ll;
+      }
+    }
+  }
+  cluster.sync();  // every CTA's shared state stays alive until the first CTA has read it
 }
 
+// Broadcast: warp per window; the window's query row and its position's four
+// latent K and V rows are all requested before the first is used.
 template <typename T, typename TO, int VEC>
 __global__ void __launch_bounds__(256) latent_broadcast_kernel(
     const T* __restrict__ q, int64_t ldq, const T* __restrict__ k, const T* __restrict__ v, int64_t ldkv,
@@ -334,12 +696,21 @@ __global__ void __launch_bounds__(256) latent_broadcast_kernel(
   for (int c0 = 0; c0 < H; c0 += 32 * VEC) {
     const int col = c0 + lane * VEC;
     const bool live = col < H;  // H < 32 leaves upper lanes idle
-    float qv[VEC] = {}, sc[4], mx = kNegInf;
-    if (live) load_vec<VEC>(q + w * ldq + col, qv);
+    Raw<T, VEC> qr = {}, kr[4] = {}, vr[4] = {};
+    if (live) {
+      raw_load<false, VEC>(q + w * ldq + col, qr);
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        raw_load<false, VEC>(k + (p * 4 + s) * ldkv + col, kr[s]);
+        raw_load<false, VEC>(v + (p * 4 + s) * ldkv + col, vr[s]);
+      }
+    }
+    float qv[VEC], sc[4], mx = kNegInf;
+    raw_unpack<VEC>(qr, qv);
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
-      float kv[VEC] = {};
-      if (live) load_vec<VEC>(k + (p * 4 + s) * ldkv + col, kv);
+      float kv[VEC];
+      raw_unpack<VEC>(kr[s], kv);
       float d = 0.f;
 #pragma unroll
       for (int u = 0; u < VEC; ++u) d += qv[u] * kv[u];
@@ -353,8 +724,8 @@ __global__ void __launch_bounds__(256) latent_broadcast_kernel(
     for (int s = 0; s < 4; ++s) {
       const float pr = __expf(sc[s] - mx);
       l += pr;
-      float vv[VEC] = {};
-      if (live) load_vec<VEC>(v + (p * 4 + s) * ldkv + col, vv);
+      float vv[VEC];
+      raw_unpack<VEC>(vr[s], vv);
 #pragma unroll
       for (int u = 0; u < VEC; ++u) acc[u] += pr * vv[u];
     }
@@ -433,7 +804,8 @@ int mb_segment_attention(const void* q, int64_t ldq, const void* k, const void* 
                          const int64_t* cls, const int64_t* skip_ptr, void* out, int out_dtype, int64_t ldo, float* m,
                          float* l, void* stream) {
   MB_REQUIRE(valid_dtype(dtype) && valid_dtype(out_dtype), "segment_attention: bad dtype");
-  MB_REQUIRE(heads > 0 && head_dim > 0 && n_q >= 0, "segment_attention: bad sizes");
+  MB_REQUIRE(heads > 0 && head_dim > 0 && n_q >= 0 && n_src >= 0 && n_src <= INT32_MAX,
+             "segment_attention: bad sizes");
   if (n_q == 0) return MB_OK;
   const int H = heads * head_dim;
   const int vec = attn_vec(heads, head_dim);
@@ -443,7 +815,7 @@ int mb_segment_attention(const void* q, int64_t ldq, const void* k, const void* 
   MB_REQUIRE(valid_dtype(vcls_dtype), "segment_attention: bad vcls dtype");
   const float scale = 1.f / sqrtf((float)head_dim);
   cudaStream_t s = as_stream(stream);
-  dim3 grid((unsigned)cdiv(n_q, kSegWarps));
+  dim3 grid((unsigned)cdiv(n_q, kSegWarps * kSegRows));
   MB_DISPATCH_T(dtype, T, [&] {
     MB_DISPATCH_T(out_dtype, TO, [&] {
       MB_DISPATCH_T(vcls_dtype, TV, [&] {
@@ -461,6 +833,63 @@ int mb_segment_attention(const void* q, int64_t ldq, const void* k, const void* 
     });
   });
   return launch_status("segment_attention");
+}
+
+int mb_segment_attention_grouped(const void* q, int64_t ldq, const void* k, const void* v, int64_t ldkv, int dtype,
+                                 int64_t n_q, int64_t n_src, int heads, int head_dim, const float* bias,
+                                 int64_t n_cls, const void* vcls, int vcls_dtype, const int64_t* seg_ptr,
+                                 const int64_t* src, const int64_t* cls, const int64_t* skip_ptr,
+                                 const int64_t* q_off, const int64_t* s_off, int64_t n_groups, int64_t stage_rows,
+                                 void* out, int out_dtype, int64_t ldo, void* stream) {
+  MB_REQUIRE(dtype == MB_BF16, "segment_attention_grouped: q/k/v must be bf16");
+  MB_REQUIRE(valid_dtype(out_dtype) && valid_dtype(vcls_dtype), "segment_attention_grouped: bad dtype");
+  MB_REQUIRE(heads > 0 && head_dim > 0 && n_q >= 0 && n_groups >= 0 && n_src >= 0 && n_src <= INT32_MAX,
+             "segment_attention_grouped: bad sizes");
+  const int64_t H = (int64_t)heads * head_dim;
+  MB_REQUIRE(H % kGrpCols == 0 && kGrpCols % head_dim == 0 && head_dim % 8 == 0,
+             "segment_attention_grouped: unsupported heads=%d head_dim=%d (needs head_dim in {8,16,32,64} and "
+             "width a multiple of %d)", heads, head_dim, kGrpCols);
+  MB_REQUIRE(n_cls > 0 && n_cls <= (1 << kGrpClsBits), "segment_attention_grouped: n_cls out of range");
+  MB_REQUIRE(stage_rows >= 1, "segment_attention_grouped: stage_rows must be >= 1");
+  MB_REQUIRE(q && k && v && out && bias && seg_ptr && src && cls && q_off && s_off,
+             "segment_attention_grouped: null pointer");
+  MB_REQUIRE(aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && ldq % 8 == 0 && ldkv % 8 == 0 &&
+                 ldo % 8 == 0 && aligned(out, 16) && (!vcls || aligned(vcls, 16)),
+             "segment_attention_grouped: q/k/v/out need 16-byte aligned rows");
+  if (n_q == 0 || n_groups == 0) return MB_OK;
+  const int nh = kGrpCols / head_dim;
+  const int fixed = grp_bias_bytes(nh, n_cls) +
+                    (vcls ? (vcls_dtype == MB_BF16 ? grp_vcls_bytes<__nv_bfloat16>(n_cls) : grp_vcls_bytes<float>(n_cls))
+                          : 0);
+  const int limit = 227 * 1024;
+  MB_REQUIRE(fixed + kGrpKvRowBytes <= limit, "segment_attention_grouped: %lld classes do not fit shared memory",
+             (long long)n_cls);
+  // Groups with more sources than fit read K/V from global memory instead.
+  const int64_t rows = std::min<int64_t>(stage_rows, (limit - fixed) / kGrpKvRowBytes);
+  const int smem = fixed + (int)rows * kGrpKvRowBytes;
+  const float scale = 1.f / sqrtf((float)head_dim);
+  cudaStream_t s = as_stream(stream);
+  dim3 grid((unsigned)n_groups, (unsigned)(H / kGrpCols));
+  int rc = MB_OK;
+  MB_DISPATCH_T(out_dtype, TO, [&] {
+    MB_DISPATCH_T(vcls_dtype, TV, [&] {
+      auto kern = head_dim == 32
+                      ? (vcls ? segment_attention_grouped_kernel<TO, TV, 4, true>
+                              : segment_attention_grouped_kernel<TO, TV, 4, false>)
+                      : (vcls ? segment_attention_grouped_kernel<TO, TV, 0, true>
+                              : segment_attention_grouped_kernel<TO, TV, 0, false>);
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+        rc = fail(MB_LAUNCH_FAILED, "segment_attention_grouped: %d bytes of shared memory refused", smem);
+        return;
+      }
+      kern<<<grid, kGrpWarps * 32, smem, s>>>((const __nv_bfloat16*)q, ldq, (const __nv_bfloat16*)k,
+                                             (const __nv_bfloat16*)v, ldkv, n_q, n_src, head_dim, bias, n_cls,
+                                             (const TV*)vcls, H, seg_ptr, src, cls, skip_ptr, q_off, s_off,
+                                             (int)rows, (TO*)out, ldo, scale);
+    });
+  });
+  if (rc != MB_OK) return rc;
+  return launch_status("segment_attention_grouped");
 }
 
 int mb_stone_attention(const void* q, const void* k, const void* v, int dtype, int64_t n_pos, int heads, int head_dim,
@@ -505,7 +934,7 @@ int mb_window_latent_read(const void* q, int64_t ldq, const void* k, const void*
   MB_REQUIRE(vec > 0, "window_latent_read: unsupported heads=%d head_dim=%d", heads, head_dim);
   MB_REQUIRE(q && out && offsets && (n_windows == 0 || (k && v && order)), "window_latent_read: null pointer");
   const int H = heads * head_dim;
-  const size_t smem = sizeof(float) * (size_t)kReadWarps * 4 * (H + 2 * heads);
+  const size_t smem = sizeof(float) * ((size_t)kReadWarps * 4 * (H + 2 * heads) + 4 * (H + 2 * heads));
   MB_REQUIRE(smem <= 200 * 1024, "window_latent_read: width too large");
   const float scale = 1.f / sqrtf((float)head_dim);
   cudaStream_t s = as_stream(stream);
@@ -514,9 +943,9 @@ int mb_window_latent_read(const void* q, int64_t ldq, const void* k, const void*
       MB_DISPATCH_VEC(vec, V, [&] {
         auto kern = latent_read_kernel<T, TO, V>;
         if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        kern<<<(unsigned)n_pos, kReadWarps * 32, smem, s>>>((const T*)q, ldq, (const T*)k, (const T*)v, ldkv,
-                                                            n_windows, heads, head_dim, offsets, order, (TO*)out, m,
-                                                            l, scale);
+        kern<<<dim3((unsigned)n_pos, kReadSplit), kReadWarps * 32, smem, s>>>(
+            (const T*)q, ldq, (const T*)k, (const T*)v, ldkv, n_windows, heads, head_dim, offsets, order, (TO*)out,
+            m, l, scale);
       });
     });
   });

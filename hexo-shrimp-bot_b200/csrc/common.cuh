@@ -166,6 +166,15 @@ inline int row_vec(int64_t width) { return width <= 0 ? 0 : (pick_vec(width) ? p
     }                                             \
   }()
 
+#define MB_DISPATCH_CH(ch, C, ...)                          \
+  [&] {                                                     \
+    switch (ch) {                                           \
+      case 1: { constexpr int C = 1; return __VA_ARGS__(); } \
+      case 2: { constexpr int C = 2; return __VA_ARGS__(); } \
+      default: { constexpr int C = 4; return __VA_ARGS__(); } \
+    }                                                       \
+  }()
+
 #define MB_DISPATCH_VEC(vec, V, ...)                        \
   [&] {                                                     \
     switch (vec) {                                          \

@@ -75,7 +75,7 @@ __global__ void __launch_bounds__(kWarps * 32) row_encode_kernel(
     const int64_t* __restrict__ edge_window, const int64_t* __restrict__ edge_class,
     const int64_t* __restrict__ cell_ptr, int64_t n_cells, const int64_t* __restrict__ empty_counts,
     const float* __restrict__ empty_base, const int64_t* __restrict__ empty_cls, int n_empty, int64_t h,
-    TO* __restrict__ out) {
+    TO* __restrict__ out, int64_t ld_out) {
   const int64_t c = warp_row();
   if (c >= n_cells) return;
   const int lane = threadIdx.x & 31;
@@ -106,7 +106,7 @@ __global__ void __launch_bounds__(kWarps * 32) row_encode_kernel(
         for (int i = 0; i < VEC; ++i) acc[i] += cnt * fmaxf(a[i] + b[i], 0.f);
       }
     }
-    store_vec<VEC>(out + c * h + col, acc);
+    store_vec<VEC>(out + c * ld_out + col, acc);
   }
 }
 
@@ -141,10 +141,18 @@ __global__ void __launch_bounds__(kWarps * 32) relay_cells_kernel(
 }
 
 // ----------------------------------------------------------- LayerNorm --
-// Warp per row; the row lives in registers (h <= 32 * VEC * kMaxChunks).
+// Warp per row; the row lives in registers as CH chunks of 32 * VEC columns
+// (h <= 32 * VEC * kMaxChunks). CH is a compile-time count so a 256-wide row
+// costs 8 registers, not 32: the kernels are HBM streams and need every
+// resident warp they can get to keep enough bytes in flight.
 constexpr int kMaxChunks = 4;
 
-template <typename TX, typename TO, int VEC>
+inline int row_chunks(int64_t h, int vec) {
+  const int64_t c = cdiv(h, 32 * (int64_t)vec);
+  return c <= 1 ? 1 : (c <= 2 ? 2 : 4);
+}
+
+template <typename TX, typename TO, int VEC, int CH>
 __global__ void __launch_bounds__(kWarps * 32) layer_norm_kernel(
     const TX* __restrict__ x, int64_t ldx, const int64_t* __restrict__ in_rows, int64_t n, int64_t h,
     const float* __restrict__ gamma, const float* __restrict__ beta, float eps, TO* __restrict__ out, int64_t ldo) {
@@ -153,10 +161,10 @@ __global__ void __launch_bounds__(kWarps * 32) layer_norm_kernel(
   const int lane = threadIdx.x & 31;
   const int64_t src = in_rows ? in_rows[r] : r;
   const int chunks = (int)((h + 32 * VEC - 1) / (32 * VEC));
-  float v[kMaxChunks][VEC];
+  float v[CH][VEC];
   float sum = 0.f;
 #pragma unroll
-  for (int ch = 0; ch < kMaxChunks; ++ch) {
+  for (int ch = 0; ch < CH; ++ch) {
     const int64_t col = ch * 32 * VEC + lane * VEC;
     const bool live = ch < chunks && col < h;  // ragged tail only when VEC == 1
     if (live) {
@@ -168,7 +176,7 @@ __global__ void __launch_bounds__(kWarps * 32) layer_norm_kernel(
   const float mean = warp_sum(sum) / (float)h;
   float sq = 0.f;
 #pragma unroll
-  for (int ch = 0; ch < kMaxChunks; ++ch) {
+  for (int ch = 0; ch < CH; ++ch) {
     const int64_t col = ch * 32 * VEC + lane * VEC;
     if (ch < chunks && col < h) {
 #pragma unroll
@@ -180,7 +188,7 @@ __global__ void __launch_bounds__(kWarps * 32) layer_norm_kernel(
   }
   const float rstd = rsqrtf(warp_sum(sq) / (float)h + eps);
 #pragma unroll
-  for (int ch = 0; ch < kMaxChunks; ++ch) {
+  for (int ch = 0; ch < CH; ++ch) {
     const int64_t col = ch * 32 * VEC + lane * VEC;
     if (ch < chunks && col < h) {
       float g[VEC], b[VEC], o[VEC];
@@ -219,7 +227,7 @@ __device__ __forceinline__ void ln_store(const LnOut& o, int64_t r, int64_t col,
     store_vec<VEC>(reinterpret_cast<float*>(o.out) + r * o.ld + col, y);
 }
 
-template <typename TY, int VEC>
+template <typename TY, int VEC, int CH>
 __global__ void __launch_bounds__(kWarps * 32) add_ln_kernel(float* __restrict__ x, int64_t ldx,
                                                              const TY* __restrict__ y, int64_t ldy,
                                                              const float* __restrict__ y_bias, int64_t n, int64_t h,
@@ -228,10 +236,10 @@ __global__ void __launch_bounds__(kWarps * 32) add_ln_kernel(float* __restrict__
   if (r >= n) return;
   const int lane = threadIdx.x & 31;
   const int chunks = (int)((h + 32 * VEC - 1) / (32 * VEC));
-  float v[kMaxChunks][VEC];
+  float v[CH][VEC];
   float sum = 0.f;
 #pragma unroll
-  for (int ch = 0; ch < kMaxChunks; ++ch) {
+  for (int ch = 0; ch < CH; ++ch) {
     const int64_t col = ch * 32 * VEC + lane * VEC;
     if (ch < chunks && col < h) {
       load_vec<VEC>(x + r * ldx + col, v[ch]);
@@ -255,7 +263,7 @@ __global__ void __launch_bounds__(kWarps * 32) add_ln_kernel(float* __restrict__
   const float mean = warp_sum(sum) / (float)h;
   float sq = 0.f;
 #pragma unroll
-  for (int ch = 0; ch < kMaxChunks; ++ch) {
+  for (int ch = 0; ch < CH; ++ch) {
     const int64_t col = ch * 32 * VEC + lane * VEC;
     if (ch < chunks && col < h) {
 #pragma unroll
@@ -267,7 +275,7 @@ __global__ void __launch_bounds__(kWarps * 32) add_ln_kernel(float* __restrict__
   }
   const float rstd = rsqrtf(warp_sum(sq) / (float)h + eps);
 #pragma unroll
-  for (int ch = 0; ch < kMaxChunks; ++ch) {
+  for (int ch = 0; ch < CH; ++ch) {
     const int64_t col = ch * 32 * VEC + lane * VEC;
     if (ch < chunks && col < h) {
       ln_store<VEC>(o0, r, col, v[ch], mean, rstd);
@@ -492,11 +500,13 @@ int mb_run_reduce(const void* values, int values_dtype, int64_t ld_values, int64
 int mb_row_encode(const void* pre, int pre_dtype, int64_t n_pre, const float* table, int64_t n_table,
                   const int64_t* edge_window, const int64_t* edge_class, const int64_t* cell_ptr, int64_t n_cells,
                   const int64_t* empty_counts, const float* empty_base, const int64_t* empty_cls, int n_empty,
-                  int64_t h, void* out, int out_dtype, void* stream) {
+                  int64_t h, void* out, int out_dtype, int64_t ld_out, void* stream) {
   MB_REQUIRE(valid_dtype(pre_dtype) && valid_dtype(out_dtype), "row_encode: bad dtype");
   if (n_cells == 0) return MB_OK;
   const int vec = row_vec(h);
   MB_REQUIRE(vec > 0, "row_encode: bad width %lld", (long long)h);
+  MB_REQUIRE(ld_out >= h && ld_out % vec == 0 && aligned(out, (size_t)vec * dtype_size(out_dtype)),
+             "row_encode: output rows must hold h aligned columns (ld_out=%lld)", (long long)ld_out);
   MB_REQUIRE(table && cell_ptr && out, "row_encode: null pointer");
   MB_REQUIRE(!empty_counts || (empty_base && empty_cls && n_empty > 0), "row_encode: empty rows incomplete");
   cudaStream_t s = as_stream(stream);
@@ -505,7 +515,7 @@ int mb_row_encode(const void* pre, int pre_dtype, int64_t n_pre, const float* ta
       MB_DISPATCH_VEC(vec, V, [&] {
         row_encode_kernel<TP, TO, V><<<row_grid(n_cells), kWarps * 32, 0, s>>>(
             (const TP*)pre, n_pre, table, n_table, edge_window, edge_class, cell_ptr, n_cells, empty_counts,
-            empty_base, empty_cls, n_empty, h, (TO*)out);
+            empty_base, empty_cls, n_empty, h, (TO*)out, ld_out);
       });
     });
   });
@@ -548,8 +558,10 @@ int mb_layer_norm(const void* x, int x_dtype, int64_t ldx, const int64_t* in_row
   MB_DISPATCH_T(x_dtype, TX, [&] {
     MB_DISPATCH_T(out_dtype, TO, [&] {
       MB_DISPATCH_VEC(vec, V, [&] {
-        layer_norm_kernel<TX, TO, V><<<row_grid(n), kWarps * 32, 0, s>>>((const TX*)x, ldx, in_rows, n, h, gamma,
-                                                                         beta, eps, (TO*)out, ldo);
+        MB_DISPATCH_CH(row_chunks(h, vec), C, [&] {
+          layer_norm_kernel<TX, TO, V, C><<<row_grid(n), kWarps * 32, 0, s>>>((const TX*)x, ldx, in_rows, n, h,
+                                                                              gamma, beta, eps, (TO*)out, ldo);
+        });
       });
     });
   });
@@ -576,8 +588,10 @@ int mb_add_ln(float* x, int64_t ldx, const void* y, int y_dtype, int64_t ldy, co
   cudaStream_t s = as_stream(stream);
   MB_DISPATCH_T(y ? y_dtype : MB_F32, TY, [&] {
     MB_DISPATCH_VEC(vec, V, [&] {
-      add_ln_kernel<TY, V><<<row_grid(n), kWarps * 32, 0, s>>>(x, ldx, (const TY*)y, ldy, y_bias, n, h, eps, n_out,
-                                                               outs[0], outs[1], outs[2]);
+      MB_DISPATCH_CH(row_chunks(h, vec), C, [&] {
+        add_ln_kernel<TY, V, C><<<row_grid(n), kWarps * 32, 0, s>>>(x, ldx, (const TY*)y, ldy, y_bias, n, h, eps,
+                                                                    n_out, outs[0], outs[1], outs[2]);
+      });
     });
   });
   return launch_status("add_ln");

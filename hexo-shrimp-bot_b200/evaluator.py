@@ -85,8 +85,7 @@ def network_evaluate(model, cfg):
         with _gpu_lock, torch.no_grad():
             b = to_device(batch, device, fields)
             eng = model.engine(dtype, gemm=gemm)
-            w, g, cells = eng.trunk(b)
-            policy, critic = eng.heads(w, g, cells, b)
+            policy, critic = eng.evaluate(b)
             q_score, q_values = ops.compose(critic, b.legal_offsets, cfg.mass_floor)
             out = torch.cat([policy.float(), q_score, q_values]).to("cpu")
             check_device_error(device)

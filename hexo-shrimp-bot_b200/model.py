@@ -18,6 +18,7 @@ stage in fp32 (the parity mode).
 
 from __future__ import annotations
 
+import contextlib
 import math
 from dataclasses import dataclass
 
@@ -380,6 +381,7 @@ class _Tables:
             self.r_src = ops.gather_i64(b.radius_src, rorder)
             self.r_cls = ops.radius_class(b.radius_orbit, b.radius_own, b.radius_on_axis, rorder)
             self.r_ptr = ops.csr(r_sorted, self.N_c)
+            self.cell_off = ops.csr(b.cell_pos, self.P)  # cells are laid out position by position
             self.skip = self.cell_ptr if cfg.cell_node_scope == "uncovered" else None
         if cfg.cell_adjacency:
             a_sorted, aorder = ops.argsort(b.adjacency_dst, self.N_c)
@@ -410,6 +412,9 @@ class Engine:
         self.cd = cd = dtype
         self.gemm = gemm
         self.stamp = None
+        # Optional launch timing: when a dict, the named stages of each forward
+        # append a (start, end) CUDA event pair recorded on the launching stream.
+        self.probe = None
         h = cfg.h
         m = model
         dev = m.latent_base.device
@@ -533,6 +538,18 @@ class Engine:
             y.relu_()
         return y
 
+    @contextlib.contextmanager
+    def timed(self, name: str):
+        """Bracket the launches of one stage with CUDA events when probing."""
+        if self.probe is None:
+            yield
+            return
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        yield
+        end.record()
+        self.probe.setdefault(name, []).append((start, end))
+
     def ln(self, x: Tensor, p: _LN, out: Tensor | None = None, dtype=None) -> Tensor:
         return ops.layer_norm(x, p.g, p.b, out_dtype=dtype or self.cd, out=out)
 
@@ -597,14 +614,30 @@ class Engine:
         return [o for _, _, o in outs]
 
     # ---------------------------------------------------------------- trunk
-    def trunk(self, b: Batch):
+    def trunk(self, b: Batch, for_heads: bool = False):
         """model.py:898-985. Every update of the large residual streams (w per
         window, c per cell) also emits the LayerNorms of the next stages that
-        read them, so a stream row is read and written once per update."""
+        read them, so a stream row is read and written once per update.
+
+        Returns ln_out(w) and cells fp32, as the reference does. With
+        ``for_heads`` (the evaluate path, whose only readers are the heads'
+        compute-dtype GEMMs) the final LayerNorms write compute-dtype rows
+        instead, cells straight into the left half of the decoder's input
+        buffer; the values are the same rows rounded where the reference's
+        autocast GEMMs round them."""
         cfg, cd, h = self.cfg, self.cd, self.h
         T = _Tables(cfg, b)
         self.tables = T
         dev = b.stone_own.device
+        direct = for_heads and cfg.uses_cell_state and cfg.cell_nodes
+        self._exit_w = torch.empty(T.N_w, h, dtype=cd if direct else torch.float32, device=dev)
+        self._head_buf = self._exit_c = None
+        if cfg.uses_cell_state:
+            if direct:
+                self._head_buf = torch.empty(T.N_c, 2 * h, dtype=cd, device=dev)
+                self._exit_c = self._head_buf[:, :h]
+            else:
+                self._exit_c = torch.empty(T.N_c, h, dtype=torch.float32, device=dev)
         s = ops.embed(self.stone_table, b.stone_own)
         w = ops.embed(self.window_table, b.window_feat)
         slot = torch.arange(T.P * GLOBAL_ROWS, device=dev) % GLOBAL_ROWS
@@ -708,7 +741,7 @@ class Engine:
             buf_w = torch.empty(T.N_w, 2 * h, dtype=cd, device=w.device)
             self.update(w, y, [(nxt["ln_ws_w"], buf_w[:, :h])])
         else:
-            w_out = torch.empty(T.N_w, h, dtype=torch.float32, device=w.device)
+            w_out = self._exit_w
             self.update(w, y, [(self.ln_out, w_out)])
         # FFN (row-wise; the stone half is skipped in the last block)
         for x_ in ((s, g) if update_stones else (g,)):
@@ -724,23 +757,30 @@ class Engine:
         zstate = self.ln(c, blk["ln_c"]) if cfg.cell_structure else None
         q = self.linear(zc_cr, blk["cr_wq"])
         kv = self.linear(zw_cr, blk["cr_kv"])
-        read = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["cr_bias"], blk["cr_vclass"], T.cell_ptr,
-                                     T.dec_window, T.dec_class, out_dtype=cd)
+        with self.timed("cell_read"):
+            read = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["cr_bias"], blk["cr_vclass"], T.cell_ptr,
+                                         T.dec_window, T.dec_class, out_dtype=cd)
         reads = self.linear(read, blk["cr_wo"])
         simple = not (cfg.cell_structure or cfg.cell_adjacency)
         if cfg.cell_nodes:
             (zc_rad,) = self.update(c, reads, [blk["ln_radius_c"]])
             q = self.linear(zc_rad, blk["radius_wq"])
             kv = self.ln_linear(s, blk["ln_radius_s"], blk["radius_kv"])
-            read = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["radius_bias"], blk["radius_vclass"], T.r_ptr,
-                                         T.r_src, T.r_cls, skip_ptr=T.skip, out_dtype=cd)
+            with self.timed("radius_read"):
+                if ops.grouped_supported(cfg.heads, h, cd):
+                    # block-diagonal: position p's cells read only position p's stones
+                    read = ops.segment_attention_grouped(
+                        q, kv[:, :h], kv[:, h:], blk["radius_bias"], blk["radius_vclass"], T.r_ptr, T.r_src,
+                        T.r_cls, T.cell_off, T.stone_off, T.max_t - GLOBAL_ROWS, skip_ptr=T.skip, out_dtype=cd)
+                else:
+                    read = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["radius_bias"], blk["radius_vclass"],
+                                                 T.r_ptr, T.r_src, T.r_cls, skip_ptr=T.skip, out_dtype=cd)
             y = self.linear(read, blk["radius_wo"])
             if cfg.cell_structure:
                 reads = (reads.float() + y.float()).to(cd)
         else:
             y = reads
-        exit_ln = (nxt["ln_cr_c"], None) if nxt is not None else (self.ln_out, torch.empty(
-            c.shape[0], h, dtype=torch.float32, device=c.device))
+        exit_ln = (nxt["ln_cr_c"], None) if nxt is not None else (self.ln_out, self._exit_c)
         if simple:
             zc_wr, zc_out = self.update(c, y, [blk["ln_wr_c"], exit_ln])
         else:
@@ -774,19 +814,27 @@ class Engine:
             T = _Tables(cfg, b)
         n_c = T.N_c
         pre = self.linear_cd(w.to(cd), self.act_proj)
-        acts_dtype = torch.float32 if cfg.action_tactical else cd
-        buf = torch.empty(n_c, 2 * h, dtype=cd, device=w.device)
-        acts = ops.row_encode(pre, self.act_table, T.dec_window, T.act_class, T.cell_ptr, n_c,
-                              empty_counts=b.act_empty.contiguous(), empty_base=self.act_empty_base,
-                              empty_cls=self.act_empty_classes, out_dtype=acts_dtype)
+        # decoder input [cells | action rows]; the evaluate path's trunk has
+        # already written cells into the left half of its buffer
+        head_buf = getattr(self, "_head_buf", None)
+        in_place = (cfg.uses_cell_state and head_buf is not None and cells is not None
+                    and cells.data_ptr() == head_buf.data_ptr() and head_buf.shape == (n_c, 2 * h))
+        buf = head_buf if in_place else torch.empty(n_c, 2 * h, dtype=cd, device=w.device)
+        enc = dict(empty_counts=b.act_empty.contiguous(), empty_base=self.act_empty_base,
+                   empty_cls=self.act_empty_classes)
         if cfg.action_tactical:
+            acts = ops.row_encode(pre, self.act_table, T.dec_window, T.act_class, T.cell_ptr, n_c,
+                                  out_dtype=torch.float32, **enc)
             t = self.linear(self.linear(b.act_tactical.to(cd), self.tactical_a, relu=True), self.tactical_out)
             ops.residual_add(acts, t)
-        buf[:, h:].copy_(acts)
-        if cfg.uses_cell_state:
-            buf[:, :h].copy_(cells)
+            buf[:, h:].copy_(acts)
         else:
-            ops.run_reduce(w, T.dec_window, T.cell_ptr, n_c, out=buf[:, :h])
+            ops.row_encode(pre, self.act_table, T.dec_window, T.act_class, T.cell_ptr, n_c, out=buf[:, h:], **enc)
+        if not in_place:
+            if cfg.uses_cell_state:
+                buf[:, :h].copy_(cells)
+            else:
+                ops.run_reduce(w, T.dec_window, T.cell_ptr, n_c, out=buf[:, :h])
         base = self.linear(buf, self.dec_pq)  # (N_c, 2H): [p-head | q-head]
         extra = ops.run_reduce(self.e_pq, T.dec_class, T.cell_ptr, n_c)
         ops.residual_add(base, extra)
@@ -794,10 +842,15 @@ class Engine:
         ph = cfg.policy_hidden
         outs = []
         for j, (lin_a, out_lin) in enumerate(((self.p_lin_a, self.p_out), (self.q_lin_a, self.q_out))):
-            pre_j = self.linear(base[:, j * h:(j + 1) * h].contiguous(), lin_a)
+            pre_j = self.linear(base[:, j * h:(j + 1) * h], lin_a)
             ops.add_gather(pre_j, gh[:, j * ph:(j + 1) * ph].contiguous(), b.cell_pos, relu=True)
             outs.append(self.linear(pre_j, out_lin))
         return outs[0].float().reshape(-1), outs[1].float()
+
+    def evaluate(self, b: Batch):
+        """trunk + heads for the evaluator closure: (policy (N,), critic (N, 3))."""
+        w, g, cells = self.trunk(b, for_heads=True)
+        return self.heads(w, g, cells, b)
 
     def value_head(self, w: Tensor, g: Tensor, b: Batch):
         """model.py:1160-1183 (full forward only; KLENT skips it)."""

@@ -119,15 +119,19 @@ def run_reduce(values, gather, ptr_, n_dest, add=None, add_idx=None, out=None, o
 
 
 def row_encode(pre, table, edge_window, edge_class, cell_ptr, n_cells, empty_counts=None, empty_base=None,
-               empty_cls=None, out_dtype=torch.float32):
+               empty_cls=None, out_dtype=torch.float32, out=None):
+    """Action-row encoder (K5); ``out`` may be a row-strided column view."""
     _cuda(pre, table, edge_window, edge_class, cell_ptr)
     h = pre.shape[1]
-    out = torch.empty(n_cells, h, dtype=out_dtype, device=pre.device)
+    if out is None:
+        out = torch.empty(n_cells, h, dtype=out_dtype, device=pre.device)
+    elif out.shape != (n_cells, h) or out.stride(1) != 1:
+        raise ValueError("row_encode out must be (n_cells, h) with unit column stride")
     n_empty = empty_cls.numel() if empty_cls is not None else 0
     call("mb_row_encode", ptr(pre), dtype_code(pre.dtype), pre.shape[0], ptr(table), table.shape[0],
          ptr(edge_window), ptr(edge_class), ptr(cell_ptr), n_cells,
          ptr(empty_counts), ptr(empty_base), ptr(empty_cls), n_empty, h, ptr(out), dtype_code(out.dtype),
-         stream_of(pre.device))
+         out.stride(0), stream_of(pre.device))
     return out
 
 
@@ -162,6 +166,41 @@ def segment_attention(q, k, v, bias, vcls, seg_ptr, src, cls, skip_ptr=None, out
          dtype_code(vcls.dtype) if vcls is not None else 0, ptr(seg_ptr), ptr(src), ptr(cls),
          ptr(skip_ptr), ptr(out), dtype_code(out.dtype), out.stride(0), ptr(m), ptr(l), stream_of(q.device))
     return (out, m, l) if stats else out
+
+
+def segment_attention_grouped(q, k, v, bias, vcls, seg_ptr, src, cls, q_off, s_off, stage_rows, skip_ptr=None,
+                              out=None, out_dtype=torch.bfloat16):
+    """Segment attention over a block-diagonal edge set (the radius read:
+    group g = position g, its cells [q_off[g], q_off[g+1]) attend only to its
+    stones [s_off[g], s_off[g+1])). Same result as ``segment_attention`` up
+    to float rounding; each group's K/V columns are staged in shared memory
+    (up to ``stage_rows`` sources per group). bf16 q/k/v only."""
+    _cuda(q, k, v, bias, seg_ptr, q_off, s_off)
+    heads = bias.shape[0]
+    for t, n in ((q, "q"), (k, "k"), (v, "v")):
+        _rowmajor(t, n)
+    if k.stride(0) != v.stride(0):
+        raise ValueError("k and v must share a row stride")
+    if not (q.dtype == k.dtype == v.dtype == torch.bfloat16):
+        raise ValueError("segment_attention_grouped needs bf16 q, k and v")
+    n_q, width = q.shape
+    if out is None:
+        out = torch.empty(n_q, width, dtype=out_dtype, device=q.device)
+    bias32 = bias if (bias.dtype == torch.float32 and bias.is_contiguous()) else bias.float().contiguous()
+    if vcls is not None and not (vcls.dtype in (torch.float32, torch.bfloat16) and vcls.is_contiguous()):
+        vcls = vcls.float().contiguous()
+    call("mb_segment_attention_grouped", ptr(q), q.stride(0), ptr(k), ptr(v), k.stride(0), dtype_code(q.dtype),
+         n_q, k.shape[0], heads, width // heads, ptr(bias32), bias32.shape[1], ptr(vcls),
+         dtype_code(vcls.dtype) if vcls is not None else 0, ptr(seg_ptr), ptr(src), ptr(cls), ptr(skip_ptr),
+         ptr(q_off), ptr(s_off), q_off.shape[0] - 1, max(int(stage_rows), 1), ptr(out), dtype_code(out.dtype),
+         out.stride(0), stream_of(q.device))
+    return out
+
+
+def grouped_supported(heads: int, width: int, dtype) -> bool:
+    """Whether ``segment_attention_grouped`` takes this shape."""
+    hd = width // heads
+    return dtype == torch.bfloat16 and width % 64 == 0 and hd % 8 == 0 and 64 % hd == 0
 
 
 def stone_attention_ragged(qkv, tok_off, heads, max_tokens, max_queries=-1, out=None, out_dtype=None):

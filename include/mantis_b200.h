@@ -89,11 +89,12 @@ int mb_run_reduce(const void* values, int values_dtype, int64_t ld_values, int64
  *   + sum_o empty_counts[c, o] * relu(empty_base + table[empty_cls[o]]),
  * fp32 accumulation, run ptr over cells. Replaces mantisnet::action_row_encode
  * (row_encoder.py:368-380, 416-447) fused with the EMPTY-row term
- * (model.py:1049-1057). empty_counts may be NULL. */
+ * (model.py:1049-1057). empty_counts may be NULL. Output row c starts at
+ * out + c * ld_out (ld_out >= h, a multiple of the vector width). */
 int mb_row_encode(const void* pre, int pre_dtype, int64_t n_pre, const float* table, int64_t n_table,
                   const int64_t* edge_window, const int64_t* edge_class, const int64_t* cell_ptr, int64_t n_cells,
                   const int64_t* empty_counts, const float* empty_base, const int64_t* empty_cls, int n_empty,
-                  int64_t h, void* out, int out_dtype, void* stream);
+                  int64_t h, void* out, int out_dtype, int64_t ld_out, void* stream);
 
 /* Relay cell pass (default config, §5.1b): pre[c] = sum x[w] + emb[cls];
  * val = relu(pre); out[w] = sum val over the window's cells. `scratch` holds
@@ -129,6 +130,26 @@ int mb_segment_attention(const void* q, int64_t ldq, const void* k, const void* 
                          const float* bias, int64_t n_cls, const void* vcls, int vcls_dtype,
                          const int64_t* seg_ptr, const int64_t* src, const int64_t* cls, const int64_t* skip_ptr,
                          void* out, int out_dtype, int64_t ldo, float* m, float* l, void* stream);
+
+/* The segment attention above for block-diagonal edge sets, with the same
+ * result up to float rounding (m/l not produced): query rows and sources split into
+ * n_groups groups (group g: rows [q_off[g], q_off[g+1]), sources
+ * [s_off[g], s_off[g+1])) and every edge of a group-g row names a group-g
+ * source; an edge outside its group is reported as an index error and
+ * skipped. Each group's K/V columns are staged in shared memory once (groups
+ * of more than stage_rows sources, or more than fit, read K/V from global
+ * memory). q/k/v bf16 with 16-byte aligned rows; head_dim in {8, 16, 32, 64}
+ * and heads * head_dim a multiple of 64; n_cls <= 2048 and the bias and
+ * class value rows of one 64-column block must fit in shared memory. Replaces the radius
+ * read mantisnet::cell_attention(q cells, k/v stones, radius tables)
+ * (model.py:439-451, tables model.py:864-875; kernel cell_latents.py:213-285). */
+int mb_segment_attention_grouped(const void* q, int64_t ldq, const void* k, const void* v, int64_t ldkv, int dtype,
+                                 int64_t n_q, int64_t n_src, int heads, int head_dim,
+                                 const float* bias, int64_t n_cls, const void* vcls, int vcls_dtype,
+                                 const int64_t* seg_ptr, const int64_t* src, const int64_t* cls,
+                                 const int64_t* skip_ptr, const int64_t* q_off, const int64_t* s_off,
+                                 int64_t n_groups, int64_t stage_rows, void* out, int out_dtype, int64_t ldo,
+                                 void* stream);
 
 /* Block-diagonal stone attention over [4 latents; stones] per position.
  * Padded mode (tok_off == NULL): q/k/v/out element (p, a, t, d) at

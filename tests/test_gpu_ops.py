@@ -113,6 +113,86 @@ def test_segment_attention_bad_index_is_reported_not_faulted():
     mb._lib.check_device_error()  # cleared
 
 
+def _grouped_case(heads, hd, seed, big=400):
+    """Block-diagonal edges: group g's rows name only group g's sources
+    (empty groups, empty runs and one group larger than a small stage)."""
+    g = torch.Generator().manual_seed(seed)
+    n_src_g = [5, 0, 37, big, 1, 60, 12]
+    n_q_g = [40, 9, 0, 130, 7, 55, 33]
+    q_off = torch.tensor([0] + n_q_g).cumsum(0)
+    s_off = torch.tensor([0] + n_src_g).cumsum(0)
+    runs, src = [], []
+    for gi, (nq, ns) in enumerate(zip(n_q_g, n_src_g)):
+        r = torch.randint(0, 25, (nq,), generator=g) if ns else torch.zeros(nq, dtype=torch.long)
+        runs.append(r)
+        src.append(s_off[gi] + torch.randint(0, max(ns, 1), (int(r.sum()),), generator=g))
+    runs, src = torch.cat(runs), torch.cat(src)
+    n_q, n_src, n_cls = int(q_off[-1]), int(s_off[-1]), 192
+    cls = torch.randint(0, n_cls, (src.numel(),), generator=g)
+    seg_ptr = torch.cat([torch.zeros(1, dtype=torch.long), runs.cumsum(0)])
+    kv = torch.randn(n_src, 2 * heads * hd, generator=g).to(torch.bfloat16)
+    q = torch.randn(n_q, heads * hd, generator=g).to(torch.bfloat16)
+    bias = torch.randn(heads, n_cls, generator=g)
+    vcls = torch.randn(n_cls, heads * hd, generator=g)
+    return q, kv, bias, vcls, seg_ptr, src, cls, q_off, s_off, runs
+
+
+@pytest.mark.parametrize("heads,hd", [(8, 32), (4, 16), (2, 32), (4, 64), (8, 8)])
+@pytest.mark.parametrize("vdt", [None, torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("odt", [torch.float32, torch.bfloat16])
+def test_segment_attention_grouped_matches_generic(heads, hd, vdt, odt):
+    q, kv, bias, vcls, seg_ptr, src, cls, q_off, s_off, runs = (
+        x.to(DEV) for x in _grouped_case(heads, hd, heads * 1000 + hd))
+    h = heads * hd
+    vc = None if vdt is None else vcls.to(vdt)
+
+    def same(got, want, msg=""):
+        # The grouped kernel rescales its softmax state once per chunk of
+        # edges, the generic one once per edge: equal up to float rounding
+        # (bf16 outputs: one bf16 step).
+        if odt == torch.float32:
+            torch.testing.assert_close(got, want, rtol=1e-5, atol=1e-5, msg=msg)
+        else:
+            torch.testing.assert_close(got.float(), want.float(), rtol=8e-3, atol=8e-3, msg=msg)
+
+    want = ops.segment_attention(q, kv[:, :h], kv[:, h:], bias, vc, seg_ptr, src, cls, out_dtype=odt)
+    for stage in (1024, 64, 1):  # all staged; the 400-source group from global memory; every group from global
+        got = ops.segment_attention_grouped(q, kv[:, :h], kv[:, h:], bias, vc, seg_ptr, src, cls, q_off, s_off,
+                                            stage, out_dtype=odt)
+        torch.cuda.synchronize()
+        same(got, want, f"stage_rows={stage}")
+    skip = torch.cat([torch.zeros(1, dtype=torch.long, device=DEV),
+                      (torch.arange(q.shape[0], device=DEV) % 3 == 0).long().cumsum(0)])
+    want = ops.segment_attention(q, kv[:, :h], kv[:, h:], bias, vc, seg_ptr, src, cls, skip_ptr=skip, out_dtype=odt)
+    got = ops.segment_attention_grouped(q, kv[:, :h], kv[:, h:], bias, vc, seg_ptr, src, cls, q_off, s_off, 1024,
+                                        skip_ptr=skip, out_dtype=odt)
+    same(got, want, "skip")
+    mb._lib.check_device_error()
+
+
+def test_segment_attention_grouped_against_oracle():
+    q, kv, bias, vcls, seg_ptr, src, cls, q_off, s_off, runs = _grouped_case(8, 32, 7)
+    qid = torch.repeat_interleave(torch.arange(q.shape[0]), runs)
+    got = ops.segment_attention_grouped(q.to(DEV), kv[:, :256].to(DEV), kv[:, 256:].to(DEV), bias.to(DEV),
+                                        vcls.to(DEV), seg_ptr.to(DEV), src.to(DEV), cls.to(DEV), q_off.to(DEV),
+                                        s_off.to(DEV), 1024, out_dtype=torch.float32)
+    want = O.segment_attention(q.float().view(-1, 8, 32), kv[:, :256].float().view(-1, 8, 32),
+                               kv[:, 256:].float().view(-1, 8, 32), bias, vcls, src, cls, qid)
+    torch.testing.assert_close(got.view(-1, 8, 32).cpu(), want, rtol=1e-5, atol=2e-5)
+
+
+def test_segment_attention_grouped_cross_group_edge_is_reported():
+    q, kv, bias, vcls, seg_ptr, src, cls, q_off, s_off, runs = _grouped_case(8, 32, 3)
+    src = src.clone()
+    src[0] = int(s_off[3])  # a row of group 0 naming a source of group 3
+    mb._lib.check_device_error()  # clear
+    ops.segment_attention_grouped(q.to(DEV), kv[:, :256].to(DEV), kv[:, 256:].to(DEV), bias.to(DEV), None,
+                                  seg_ptr.to(DEV), src.to(DEV), cls.to(DEV), q_off.to(DEV), s_off.to(DEV), 1024)
+    with pytest.raises(ValueError, match="out of range"):
+        mb._lib.check_device_error()
+    mb._lib.check_device_error()  # cleared
+
+
 def test_window_latents_match_reference_fixture():
     t = _fx()
     pos = t["win.pos"].to(DEV)

@@ -56,5 +56,11 @@ def test_host_side_validation_without_gpu():
     with pytest.raises(ValueError, match="head_dim"):
         _lib.call("mb_stone_attention", None, None, None, 0, 1, 1, 24, 0, 0, 0, None, 0, None, 0, -1, None, 0, 0, 0,
                   0, None)
+    with pytest.raises(ValueError, match="must be bf16"):
+        _lib.call("mb_segment_attention_grouped", None, 256, None, None, 512, 0, 1, 1, 8, 32, None, 192, None, 0,
+                  None, None, None, None, None, None, 1, 300, None, 1, 256, None)
+    with pytest.raises(ValueError, match="unsupported heads"):
+        _lib.call("mb_segment_attention_grouped", None, 256, None, None, 512, 1, 1, 1, 2, 128, None, 192, None, 0,
+                  None, None, None, None, None, None, 1, 300, None, 1, 256, None)
     with pytest.raises(ValueError, match="key_bits"):
         _lib.call("mb_argsort_workspace", 1000, 0, ctypes.byref(ctypes.c_int64(0)))
