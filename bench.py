@@ -339,6 +339,13 @@ def radius_read_bytes(T, cfg):
             + n_cls * h * 2 + cfg.heads * n_cls * 4)
 
 
+# DRAM bytes per cell of one radius read, from an ncu capture of the same
+# kernel (dram__bytes_read.sum + dram__bytes_write.sum = 486.8 MB over 438,658
+# cells; profiles/segment_attention_radius_and_incidence_reads_64pos.md), scaled
+# to the timed launch by its cell count.
+RADIUS_DRAM_BYTES_PER_CELL = 486_827_264 / 438_658
+
+
 def radius_roofline(probe, T, cfg):
     """The radius read's launches inside the timed region (CUDA events on the
     launching stream around each launch, recorded by the engine's probe)."""
@@ -353,7 +360,8 @@ def radius_roofline(probe, T, cfg):
     cell_ms = [s.elapsed_time(e) for s, e in probe.get("cell_read", [])]
     return {"kernel": "segment_attention_grouped (radius read, cells<-stones)", "bound": "hbm",
             "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
-            "traffic": None, "peak_kind": kind, "algorithmic_bytes": algo, "launch_ms": sec * 1000.0,
+            "traffic": RADIUS_DRAM_BYTES_PER_CELL * T.N_c, "traffic_source": "ncu capture at 64 positions, scaled by cells",
+            "peak_kind": kind, "algorithmic_bytes": algo, "launch_ms": sec * 1000.0,
             "launches_timed": len(ms), "edges": int(T.r_src.numel()),
             "cell_read_launch_ms": statistics.mean(cell_ms) if cell_ms else None}
 

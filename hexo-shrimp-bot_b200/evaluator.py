@@ -16,11 +16,13 @@ from __future__ import annotations
 import threading
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from . import ops
 from ._lib import check_device_error
 from .builder import Batch
+from .vocab import GLOBAL_ROWS
 from .config import MantisConfig
 
 _gpu_lock = threading.Lock()
@@ -64,12 +66,97 @@ def to_device(batch: Batch, device, fields) -> Batch:
     return Batch(**moved)
 
 
+# ------------------------------------------------------------ sub-batches
+# Positions are independent, so a batch can be evaluated as consecutive runs
+# of positions, each a self-contained batch whose index fields are rebased to
+# its own first stone, window, cell and position. Every per-position block of
+# the collated arrays is contiguous and in position order (the builder
+# concatenates positions; edge arrays are sorted by their destination), so a
+# run is a set of host slices, found by binary search, plus four bases.
+#
+# field: (row space, value space) -- the row space names the offsets that cut
+# the field; the value space, the base its values are rebased by (None: none).
+_SPLIT_FIELDS = {
+    "stone_own": ("stone", None), "window_feat": ("window", None), "moves_idx": ("pos", None),
+    "inc_stone": ("inc", "stone"), "inc_window": ("inc", "window"), "inc_class": ("inc", None),
+    "attn_valid": ("pos", None), "window_slot": ("window", "slot"), "value_valid": ("pos", None),
+    "legal_offsets": ("pos+1", "cell"), "cell_pos": ("cell", "pos"), "cell_nearest": ("cell", None),
+    "radius_src": ("radius", "stone"), "radius_dst": ("radius", "cell"), "radius_orbit": ("radius", None),
+    "radius_own": ("radius", None), "radius_on_axis": ("radius", None),
+    "dec_cell": ("dec", "cell"), "dec_window": ("dec", "window"), "dec_class": ("dec", None),
+    "act_class": ("dec", None), "act_empty": ("cell", None), "act_tactical": ("cell", None),
+}
+
+
+def split_points(batch: Batch, n_parts: int) -> list[int]:
+    """Position boundaries of up to ``n_parts`` runs with about equal cells."""
+    cells = batch.legal_offsets.numpy()
+    p = batch.n_pos
+    cuts = [0]
+    for k in range(1, n_parts):
+        c = int(np.searchsorted(cells, cells[-1] * k / n_parts))
+        if cuts[-1] < c < p:
+            cuts.append(c)
+    cuts.append(p)
+    return cuts
+
+
+def _offsets(batch: Batch, fields) -> dict[str, np.ndarray]:
+    """Per-position start offsets (length n_pos + 1) of every row space."""
+    p = batch.n_pos
+    stones = batch.attn_valid.sum(1).numpy() - GLOBAL_ROWS
+    off = {"pos": np.arange(p + 1), "stone": np.concatenate([[0], np.cumsum(stones)])}
+    off["window"] = np.searchsorted(batch.window_slot.numpy(), np.arange(p + 1) * batch.max_w)
+    off["cell"] = batch.legal_offsets.numpy()
+    keys = {"inc": ("inc_window", "window"), "radius": ("radius_dst", "cell"), "dec": ("dec_cell", "cell")}
+    for space, (key, by) in keys.items():
+        if key in fields:
+            off[space] = np.searchsorted(getattr(batch, key).numpy(), off[by])
+    return off
+
+
+def split_supported(fields) -> bool:
+    return all(f in _SPLIT_FIELDS for f in fields)
+
+
+def part_to_device(batch: Batch, fields, off, p0: int, p1: int, device) -> Batch:
+    """Copy positions [p0, p1) of ``batch`` to ``device`` as a batch of their
+    own (host slices copied on the current stream, indices rebased there)."""
+    base = {"stone": int(off["stone"][p0]), "window": int(off["window"][p0]), "cell": int(off["cell"][p0]),
+            "pos": p0, "slot": p0 * batch.max_w}
+    moved = {}
+    for k, v in vars(batch).items():
+        if not isinstance(v, torch.Tensor):
+            moved[k] = v
+            continue
+        if k not in fields:
+            moved[k] = torch.empty((0,) + tuple(v.shape[1:]), dtype=v.dtype, device=device)
+            continue
+        rows, by = _SPLIT_FIELDS[k]
+        if rows == "pos+1":
+            a, z = p0, p1 + 1
+        else:
+            o = off[rows]
+            a, z = int(o[p0]), int(o[p1])
+        t = v[a:z].to(device, non_blocking=True, copy=True)
+        if by is not None and base[by]:
+            t.sub_(base[by])
+        moved[k] = t
+    moved["n_pos"] = p1 - p0
+    moved["n_cells"] = int(off["cell"][p1] - off["cell"][p0])
+    return Batch(**moved)
+
+
 @dataclass
 class EvaluatorConfig:
     device: str = "cuda"
     autocast: bool = True
     mass_floor: float = 0.2
     gemm: str = "cublas"
+    # Batches of at least 2 * part_positions positions are evaluated as runs
+    # of about part_positions positions whose host-to-device copies overlap
+    # the previous run's compute; 0 turns this off.
+    part_positions: int = 256
 
 
 def network_evaluate(model, cfg):
@@ -81,13 +168,50 @@ def network_evaluate(model, cfg):
     if device.type != "cuda":
         raise RuntimeError("the B200 evaluator runs on CUDA devices only")
 
-    def evaluate(batch: Batch):
-        with _gpu_lock, torch.no_grad():
-            b = to_device(batch, device, fields)
-            eng = model.engine(dtype, gemm=gemm)
+    part = int(getattr(cfg, "part_positions", 256) or 0)
+    pipelined = part > 0 and split_supported(fields)
+
+    def run_parts(batch: Batch, eng):
+        """Copy run k + 1 on a side stream while run k computes."""
+        cuts = split_points(batch, max(1, batch.n_pos // part))
+        off = _offsets(batch, fields)
+        compute = torch.cuda.current_stream(device)
+        copy = torch.cuda.Stream(device)
+
+        def issue(k):
+            copy.wait_stream(compute)  # buffers the allocator hands out may still be read by compute
+            with torch.cuda.stream(copy):
+                b = part_to_device(batch, fields, off, cuts[k], cuts[k + 1], device)
+                done = torch.cuda.Event()
+                done.record(copy)
+            return b, done
+
+        outs = []
+        nxt = issue(0)
+        for k in range(len(cuts) - 1):
+            b, done = nxt
+            compute.wait_event(done)
+            for t in vars(b).values():
+                if isinstance(t, torch.Tensor):
+                    t.record_stream(compute)
+            if k + 2 < len(cuts):
+                nxt = issue(k + 1)
             policy, critic = eng.evaluate(b)
             q_score, q_values = ops.compose(critic, b.legal_offsets, cfg.mass_floor)
-            out = torch.cat([policy.float(), q_score, q_values]).to("cpu")
+            outs.append((policy.float(), q_score, q_values))
+        return [torch.cat(x) for x in zip(*outs)]
+
+    def evaluate(batch: Batch):
+        with _gpu_lock, torch.no_grad():
+            eng = model.engine(dtype, gemm=gemm)
+            if pipelined and batch.n_pos >= 2 * part:
+                policy, q_score, q_values = run_parts(batch, eng)
+            else:
+                b = to_device(batch, device, fields)
+                policy, critic = eng.evaluate(b)
+                q_score, q_values = ops.compose(critic, b.legal_offsets, cfg.mass_floor)
+                policy = policy.float()
+            out = torch.cat([policy, q_score, q_values]).to("cpu")
             check_device_error(device)
             n = policy.shape[0]
             return out[:n], out[n:2 * n], out[2 * n:]

@@ -1,0 +1,62 @@
+"""Sub-batch split of the evaluator (host logic, CPU): every run of positions
+is a self-contained batch whose index fields point into its own stones,
+windows, cells and positions, and the runs put back together give the parent
+batch (the order the pipelined evaluator concatenates its outputs in)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from golden_io import mb
+
+E = mb.evaluator
+INDEX_RANGE = {  # field -> attribute counting the rows its values index
+    "inc_stone": "stone_own", "inc_window": "window_feat", "radius_src": "stone_own", "radius_dst": "cell_pos",
+    "dec_cell": "cell_pos", "dec_window": "window_feat",
+}
+
+
+@pytest.fixture(scope="module")
+def batch():
+    specs = mb.engine.random_positions(9, 20, 120, seed=11)
+    return mb.collate([mb.from_spec(s) for s in specs])
+
+
+@pytest.mark.parametrize("n_parts", [1, 2, 3, 5])
+def test_runs_reassemble_the_batch(batch, n_parts):
+    cfg = mb.MantisConfig(h=32, blocks=1, heads=2, cell_latents=True, cell_nodes=True)
+    fields = E.needed_fields(cfg)
+    assert E.split_supported(fields)
+    cuts = E.split_points(batch, n_parts)
+    assert cuts[0] == 0 and cuts[-1] == batch.n_pos and all(a < b for a, b in zip(cuts, cuts[1:]))
+    off = E._offsets(batch, fields)
+    parts = [E.part_to_device(batch, fields, off, a, b, "cpu") for a, b in zip(cuts, cuts[1:])]
+    for part, p0 in zip(parts, cuts):
+        for f, rows in INDEX_RANGE.items():
+            v = getattr(part, f)
+            assert v.numel() == 0 or (int(v.min()) >= 0 and int(v.max()) < getattr(part, rows).shape[0]), f
+        assert int(part.legal_offsets[0]) == 0 and int(part.legal_offsets[-1]) == part.cell_pos.shape[0]
+        assert part.n_cells == part.cell_pos.shape[0] and part.n_pos == part.moves_idx.shape[0]
+        assert torch.all(part.cell_pos < part.n_pos)
+    base = {"stone": off["stone"], "window": off["window"], "cell": off["cell"], "pos": off["pos"],
+            "slot": off["pos"] * batch.max_w}
+    for f in fields:
+        rows, by = E._SPLIT_FIELDS[f]
+        pieces = []
+        for part, p0 in zip(parts, cuts):
+            t = getattr(part, f).clone()
+            if rows == "pos+1" and pieces:
+                t = t[1:]
+            if by is not None:
+                t += int(base[by][p0])
+            pieces.append(t)
+        assert torch.equal(torch.cat(pieces), getattr(batch, f)), f
+    # the source batch is untouched by the in-place rebasing
+    assert int(batch.radius_src.max()) == int(off["stone"][-1]) - 1 or batch.radius_src.numel() == 0
+
+
+def test_unsupported_fields_fall_back():
+    cfg = mb.MantisConfig(h=32, blocks=1, heads=2)  # relay path: its tables are not split
+    assert not E.split_supported(E.needed_fields(cfg))

@@ -120,3 +120,25 @@ def test_bf16_contract_at_bench_architecture(blocks):
     assert (out.policy_logits.cpu() - ref["policy_logits"]).abs().max() <= 2e-2
     assert (out.q_values.cpu() - ref["q_values"]).abs().max() <= 1e-2
     assert (out.value.cpu() - ref["value"]).abs().max() <= 1e-2
+
+
+@pytest.mark.parametrize("autocast", [False, True])
+def test_pipelined_evaluator_equals_one_shot(autocast):
+    """Runs of positions copied on a side stream while the previous run
+    computes give the one-shot evaluation's outputs exactly (positions are
+    independent and every kernel works per row)."""
+    cfg = mb.MantisConfig(h=64, blocks=2, heads=4, cell_latents=True, cell_nodes=True)
+    torch.manual_seed(5)
+    net = mb.MantisNet(cfg)
+    with torch.no_grad():
+        for head in (net.mlp_p, net.mlp_q):
+            head.out.weight.normal_(std=0.05)
+    net = net.to(DEV).eval()
+    specs = mb.engine.random_positions(11, 20, 160, seed=21)
+    batch = mb.collate([mb.from_spec(s) for s in specs]).pin_memory()
+    one = mb.network_evaluate(net, mb.evaluator.EvaluatorConfig(device=DEV, autocast=autocast, part_positions=0))
+    runs = mb.network_evaluate(net, mb.evaluator.EvaluatorConfig(device=DEV, autocast=autocast, part_positions=3))
+    want = one(batch)
+    got = runs(batch)
+    for a, b in zip(got, want):
+        assert torch.equal(a, b)
