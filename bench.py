@@ -366,6 +366,77 @@ def radius_roofline(probe, T, cfg):
             "cell_read_launch_ms": statistics.mean(cell_ms) if cell_ms else None}
 
 
+def _time_launches(fn, steps, warmup):
+    """Mean CUDA-event time of ``fn`` over ``steps`` launches after ``warmup``."""
+    import torch
+
+    for _ in range(max(warmup, 3)):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_op(args):
+    """One JSON line for an isolated-op workload on one GPU (inputs resident;
+    both inputs are larger than L2): ``hex`` = the fused hex message pass over
+    4096 x 256 cell tokens, ``axial`` = the axial-bias attention over 4096
+    positions x 8 heads x 256 tokens. Not the headline metric."""
+    import numpy as np
+    import torch
+
+    mb = _pkg()
+    ops = mb.ops
+    dev = torch.device("cuda", 0)
+    pk, kind = peaks()
+    g = torch.Generator(device=dev).manual_seed(0)
+    p = args.positions
+    if args.op == "hex":
+        nbr, _ = mb.hexgraph.message_graph(p, 256, 40, 200, seed=1)
+        n = nbr.shape[0]
+        x = torch.randn(n, 256, device=dev, generator=g).to(torch.bfloat16)
+        w = (torch.randn(256, 256, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        b = torch.randn(256, device=dev, generator=g) * 0.02
+        nb = torch.from_numpy(nbr).to(dev)
+        img = ops.weight_image(w)
+        out = torch.empty_like(x)
+        ms = _time_launches(lambda: ops.hex_message_pass(x, nb, img, b, out=out), args.steps, args.warmup)
+        algo = 2 * n * 256 * 2 + n * 6 * 4 + 256 * 256 * 2 + 256 * 4
+        flops = 2 * n * 256 * 256
+        line = {"metric": "hex message-pass nodes/s (config 3)", "value": n / (ms / 1000.0), "unit": "nodes/s",
+                "ms_per_step": ms, "config": {"workload": f"config 3: {p} x 256 cell tokens, F=256, bf16", "nodes": n},
+                "roofline": {"kernel": "rowgemm_kernel<HEXMEAN, ADD_X>", "bound": "hbm",
+                             "achieved": algo / ms / 1e6, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                             "frac": algo / ms / 1e6 / pk["hbm_gbs"], "peak_kind": kind, "algorithmic_bytes": algo,
+                             "tflops": flops / ms / 1e9}}
+    else:
+        coords, valid = mb.hexgraph.attention_layout(p, 256, seed=2)
+        q, k, v = (torch.randn(p, 8, 256, 32, device=dev, generator=g).to(torch.bfloat16) for _ in range(3))
+        c = torch.from_numpy(coords).to(dev)
+        vl = torch.from_numpy(valid).to(dev)
+        bias = torch.randn(33, 33, 8, device=dev, generator=g) * 0.02
+        out = torch.empty_like(q)
+        ms = _time_launches(lambda: ops.axial_attention(q, k, v, c, vl, bias, out=out), args.steps, args.warmup)
+        lv = valid.astype(np.float64)
+        flops = float((8 * 4 * 32 * lv ** 2).sum())
+        algo = float(((3 * lv + 256) * 8 * 32 * 2 + 256 * 8 + 4).sum() + 33 * 33 * 8 * 4)
+        line = {"metric": "axial-bias attention positions/s (config 2)", "value": p / (ms / 1000.0),
+                "unit": "positions/s", "ms_per_step": ms,
+                "config": {"workload": f"config 2: {p} positions x 8 heads x 256 tokens, d=32, bf16"},
+                "roofline": {"kernel": "axial_attention_kernel", "bound": "hbm", "achieved": algo / ms / 1e6,
+                             "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": algo / ms / 1e6 / pk["hbm_gbs"],
+                             "peak_kind": kind, "algorithmic_bytes": algo, "algorithmic_flops": flops,
+                             "tflops": flops / ms / 1e9, "tensor_frac": flops / ms / 1e9 / pk["bf16_tflops"]}}
+    line.update({"n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "bf16",
+                 "data": "synthetic", "gpu_launches": 1})
+    print(json.dumps(line))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -381,7 +452,12 @@ def main():
     ap.add_argument("--ref-sample", type=int, default=4)
     ap.add_argument("--latency", type=int, default=1)
     ap.add_argument("--gemm", default="cublas", help="dense projection path (see model.Engine)")
+    ap.add_argument("--op", default=None, choices=["hex", "axial"],
+                    help="time one isolated-op workload instead of the evaluator (config 3 / config 2)")
     args = ap.parse_args()
+    if args.op:
+        run_op(args)
+        return
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))

@@ -17,7 +17,8 @@ __all__ = [
 ]
 
 
-_SUBMODULES = ("_lib", "ops", "model", "evaluator", "vocab", "engine", "builder", "config", "build", "sharding")
+_SUBMODULES = ("_lib", "ops", "model", "evaluator", "vocab", "engine", "builder", "config", "build", "sharding",
+               "hexgraph")
 
 
 def __getattr__(name):

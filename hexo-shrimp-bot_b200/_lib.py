@@ -36,6 +36,8 @@ SIGNATURES = {
     "mb_cell_pass_noalloc": "pilplplpppplpip",
     "mb_segment_attention": "plpplilliiplpipppppilppp",
     "mb_segment_attention_grouped": "plpplilliiplpippppppllpilp",
+    "mb_hex_message_pass": "pllpppplp",
+    "mb_axial_attention": "pppliillllpppplllp",
     "mb_stone_attention": "pppiliilllplplipilllp",
     "mb_window_latent_read": "plpplilliipppippp",
     "mb_window_latent_broadcast": "plpplilliippippp",

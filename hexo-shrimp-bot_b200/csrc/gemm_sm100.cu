@@ -2,10 +2,15 @@
 //
 //     out = epilogue( prologue(x) @ W^T + bias )
 //
-//   prologue: LN  - fp32 rows -> LayerNorm (fp32 statistics) -> bf16
-//             COPY - bf16 rows used as they are
+//   prologue: LN      - fp32 rows -> LayerNorm (fp32 statistics) -> bf16
+//             COPY    - bf16 rows used as they are
+//             HEXMEAN - mean of the bf16 rows of a node's present hex
+//                       neighbours (six-slot int32 table, -1 = absent; fp32
+//                       sum, zero when none is present) -> bf16
 //   epilogue: STORE    - bf16 rows (optionally ReLU)
 //             RESIDUAL - x_res[row] += result (fp32, in place)
+//             ADD_X    - out[row] = x[row] + result (bf16), the fused
+//                        message-passing update y = x + W mean(x[nbr]) + b
 //
 // K = 256 (one model width), N = 256 output columns per launch, M any.
 // The op is HBM-bound (about 1.5-2.5 KB of row traffic per 131 kFLOP), so the
@@ -59,8 +64,9 @@ constexpr int EPI_WARP_FLOATS = 32 * EPI_PITCH;
 constexpr int BAR_BYTES = 256;
 constexpr long long kWaitCycles = 4000000000LL;   // ~2 s at 1.9 GHz
 
-enum Prologue { PRO_LN = 0, PRO_COPY = 1 };
-enum Epilogue { EPI_STORE = 0, EPI_RESIDUAL = 1 };
+enum Prologue { PRO_LN = 0, PRO_COPY = 1, PRO_HEXMEAN = 2 };
+enum Epilogue { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_ADD_X = 2 };
+constexpr int HEX_SLOTS = 6;
 
 constexpr uint32_t ERR_TIMEOUT = 4;
 
@@ -163,6 +169,7 @@ struct Params {
   int64_t ldo;
   float* res;           // EPI_RESIDUAL
   int64_t ldr;
+  const int32_t* nbr;   // PRO_HEXMEAN: (m, 6) neighbour rows of x, -1 = absent
 };
 
 // Shared-memory plan of one variant (all region offsets 1024-byte aligned).
@@ -389,27 +396,77 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
         const uint32_t ab = t % L::A_BUFS, aph = (t / L::A_BUFS) & 1;
         uint8_t* abuf = a_smem + ab * A_BYTES;
         bool ok = true;
-        for (int r0 = 0; r0 * L::PRODUCERS + pw < BM; r0 += RB) {
-          float v[RB][8];
+        constexpr int NRB = PRO == PRO_HEXMEAN ? 3 : RB;  // rows in flight (6 gathers each for HEXMEAN)
+        for (int r0 = 0; r0 * L::PRODUCERS + pw < BM; r0 += NRB) {
+          float v[NRB][8];
 #pragma unroll
-          for (int u = 0; u < RB; ++u) {
+          for (int u = 0; u < NRB; ++u) {
             const int r = (r0 + u) * L::PRODUCERS + pw;
             const int64_t row = tile * BM + r;
             if (r < BM && row < p.m) {
-              if constexpr (PRO == PRO_LN)
+              if constexpr (PRO == PRO_LN) {
                 load_vec<8>(reinterpret_cast<const float*>(p.x) + row * p.ldx + lane * 8, v[u]);
-              else
+              } else if constexpr (PRO == PRO_HEXMEAN) {
+                // gathered below, all rows' neighbour loads in flight together
+              } else {
                 load_vec<8>(reinterpret_cast<const __nv_bfloat16*>(p.x) + row * p.ldx + lane * 8, v[u]);
+              }
             } else {
 #pragma unroll
               for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
+            }
+          }
+          if constexpr (PRO == PRO_HEXMEAN) {
+            // lanes 0-5 fetch a row's six slots; every lane then gathers its
+            // 16-byte column chunk of each present neighbour row, all NRB rows'
+            // gathers issued before the first is summed
+            const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(p.x);
+            int my[NRB];
+#pragma unroll
+            for (int u = 0; u < NRB; ++u) {
+              const int64_t row = tile * BM + (r0 + u) * L::PRODUCERS + pw;
+              const bool live = (r0 + u) * L::PRODUCERS + pw < BM && row < p.m;
+              my[u] = (live && lane < HEX_SLOTS) ? __ldg(p.nbr + row * HEX_SLOTS + lane) : -1;
+            }
+            uint4 raw[NRB][HEX_SLOTS];
+            int present[NRB];
+#pragma unroll
+            for (int u = 0; u < NRB; ++u) {
+              present[u] = 0;
+#pragma unroll
+              for (int j = 0; j < HEX_SLOTS; ++j) {
+                const int nb = __shfl_sync(0xffffffffu, my[u], j);
+                raw[u][j] = make_uint4(0, 0, 0, 0);
+                if (nb >= p.m) report(ERR_INDEX);
+                if (nb >= 0 && nb < p.m) {
+                  raw[u][j] = __ldg(reinterpret_cast<const uint4*>(xb + (int64_t)nb * p.ldx) + lane);
+                  ++present[u];
+                }
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < NRB; ++u) {
+              float acc[8] = {};
+#pragma unroll
+              for (int j = 0; j < HEX_SLOTS; ++j) {
+                const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&raw[u][j]);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const float2 f = __bfloat1622float2(hh[i]);
+                  acc[2 * i] += f.x;
+                  acc[2 * i + 1] += f.y;
+                }
+              }
+              const float inv = present[u] ? 1.f / (float)present[u] : 0.f;
+#pragma unroll
+              for (int i = 0; i < 8; ++i) v[u][i] = acc[i] * inv;
             }
           }
           // the first batch is fetched before waiting for the buffer to drain
           if (r0 == 0 && !mbar_wait(smem_u32(&a_empty[ab]), aph ^ 1, abort)) { ok = false; break; }
           if constexpr (PRO == PRO_LN) layer_norm(v);
 #pragma unroll
-          for (int u = 0; u < RB; ++u) {
+          for (int u = 0; u < NRB; ++u) {
             const int r = (r0 + u) * L::PRODUCERS + pw;
             if (r < BM) put(abuf, r, v[u]);
           }
@@ -445,8 +502,18 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i], 0.f);
         }
-        if constexpr (EPI == EPI_STORE) {
+        if constexpr (EPI == EPI_STORE || EPI == EPI_ADD_X) {
           if (row < p.m) {
+            if constexpr (EPI == EPI_ADD_X) {
+              const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(p.x) + row * p.ldx + c0;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                float a[8];
+                load_vec<8>(xr + 8 * i, a);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[8 * i + j] += a[j];
+              }
+            }
             __nv_bfloat16* o = p.out + row * p.ldo + c0;
 #pragma unroll
             for (int i = 0; i < 4; ++i) store_vec<8>(o + 8 * i, v + 8 * i);
@@ -560,6 +627,33 @@ int mb_gemm_rows(const void* x, int x_dtype, int64_t ldx, int64_t m, const float
     else launch(rowgemm_kernel<PRO_COPY, EPI_RESIDUAL, false>, Plan<PRO_COPY, EPI_RESIDUAL, false>::SMEM);
   }
   return launch_status("gemm_rows");
+}
+
+int mb_hex_message_pass(const void* x, int64_t ldx, int64_t n, const int32_t* nbr, const void* w_image,
+                        const float* bias, void* out, int64_t ldo, void* stream) {
+  using namespace sm100;
+  MB_REQUIRE(n >= 0, "hex_message_pass: negative n");
+  if (n == 0) return MB_OK;
+  MB_REQUIRE(x && nbr && w_image && out, "hex_message_pass: null pointer");
+  MB_REQUIRE(x != out, "hex_message_pass: out must not alias x (neighbour rows are read while rows are written)");
+  MB_REQUIRE(aligned(x, 16) && (ldx * 2) % 16 == 0 && ldx >= KDIM, "hex_message_pass: x rows must be 16-byte aligned");
+  MB_REQUIRE(aligned(out, 16) && (ldo * 2) % 16 == 0 && ldo >= BN, "hex_message_pass: out rows must be 16-byte aligned");
+  MB_REQUIRE(aligned(nbr, 4) && aligned(w_image, 16), "hex_message_pass: misaligned table or weight image");
+  if (g_num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_num_sms <= 0) g_num_sms = 148;
+  }
+  Params prm{x, ldx, nullptr, nullptr, 0.f, (const __nv_bfloat16*)w_image, bias, n, 0, (__nv_bfloat16*)out, ldo,
+             nullptr, 0, nbr};
+  const int64_t tiles = cdiv(n, BM);
+  const int grid = (int)(tiles < g_num_sms ? tiles : g_num_sms);
+  auto kern = rowgemm_kernel<PRO_HEXMEAN, EPI_ADD_X, false>;
+  const int smem_bytes = Plan<PRO_HEXMEAN, EPI_ADD_X, false>::SMEM;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+  kern<<<grid, THREADS, smem_bytes, as_stream(stream)>>>(prm);
+  return launch_status("hex_message_pass");
 }
 
 }  // extern "C"

@@ -6,4 +6,5 @@
 #include "attention.cu"
 #include "gemm_simt.cu"
 #include "gemm_sm100.cu"
+#include "attention_sm100.cu"
 #include "noalloc.cu"

@@ -170,13 +170,19 @@ def network_evaluate(model, cfg):
 
     part = int(getattr(cfg, "part_positions", 256) or 0)
     pipelined = part > 0 and split_supported(fields)
+    # One copy stream for the closure's lifetime: the caching allocator keeps
+    # per-stream pools, so a fresh stream per call would allocate every run's
+    # device buffers anew.
+    streams = {}
 
     def run_parts(batch: Batch, eng):
         """Copy run k + 1 on a side stream while run k computes."""
         cuts = split_points(batch, max(1, batch.n_pos // part))
         off = _offsets(batch, fields)
         compute = torch.cuda.current_stream(device)
-        copy = torch.cuda.Stream(device)
+        copy = streams.get("copy")
+        if copy is None:
+            copy = streams["copy"] = torch.cuda.Stream(device)
 
         def issue(k):
             copy.wait_stream(compute)  # buffers the allocator hands out may still be read by compute

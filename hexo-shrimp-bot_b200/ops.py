@@ -686,3 +686,47 @@ def gemm_rows(x, w_img, bias=None, gamma=None, beta=None, relu=False, out=None, 
          ptr(b), int(relu), ptr(out), out.stride(0) if out is not None else 0, ptr(residual),
          residual.stride(0) if residual is not None else 0, stream_of(x.device))
     return out if out is not None else residual
+
+
+# ------------------------------------------------- isolated-op workloads
+def hex_message_pass(x, nbr, w_img, bias=None, out=None):
+    """out = x + W mean(x[present neighbours]) + bias, fused on the tensor
+    cores. x (n, 256) bf16 rows; nbr (n, 6) int32 (-1 absent); w_img from
+    ``weight_image(W)``; bias fp32 (256,) or None."""
+    _cuda(x, nbr, w_img)
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != GEMM_K or x.stride(1) != 1:
+        raise ValueError("hex_message_pass takes (n, 256) bf16 rows")
+    if nbr.dtype != torch.int32 or tuple(nbr.shape) != (x.shape[0], 6) or not nbr.is_contiguous():
+        raise ValueError("nbr must be a contiguous (n, 6) int32 table")
+    if bias is not None and (bias.dtype != torch.float32 or bias.numel() != GEMM_N or not bias.is_contiguous()):
+        raise ValueError("bias must be a contiguous fp32 (256,) vector")
+    if out is None:
+        out = torch.empty(x.shape[0], GEMM_N, dtype=torch.bfloat16, device=x.device)
+    call("mb_hex_message_pass", ptr(x), x.stride(0), x.shape[0], ptr(nbr), ptr(w_img), ptr(bias), ptr(out),
+         out.stride(0), stream_of(x.device))
+    return out
+
+
+def axial_attention(q, k, v, coords, valid, bias, out=None):
+    """Cell-token attention with the (dq, dr) relative-offset bias. q/k/v
+    (P, H, L, 32) bf16 (any strides with unit last stride, 16-byte aligned
+    rows); coords (P, L, 2) int32; valid (P,) int32; bias (33, 33, H) fp32.
+    Returns (P, H, L, 32) bf16 with rows past valid[p] zero."""
+    _cuda(q, k, v, coords, valid, bias)
+    if not (q.shape == k.shape == v.shape) or q.dim() != 4 or q.dtype != torch.bfloat16:
+        raise ValueError("q, k and v must be (P, H, L, d) bf16 of one shape")
+    if not (q.stride() == k.stride() == v.stride()) or q.stride(3) != 1:
+        raise ValueError("q, k and v must share strides with a unit last stride")
+    p, h, length, d = q.shape
+    if coords.dtype != torch.int32 or tuple(coords.shape) != (p, length, 2) or not coords.is_contiguous():
+        raise ValueError("coords must be a contiguous (P, L, 2) int32 tensor")
+    if valid.dtype != torch.int32 or tuple(valid.shape) != (p,):
+        raise ValueError("valid must be a (P,) int32 tensor")
+    if bias.dtype != torch.float32 or tuple(bias.shape) != (33, 33, h) or not bias.is_contiguous():
+        raise ValueError("bias must be a contiguous (33, 33, H) fp32 table")
+    if out is None:
+        out = torch.empty(p, h, length, d, dtype=torch.bfloat16, device=q.device)
+    call("mb_axial_attention", ptr(q), ptr(k), ptr(v), p, h, d, length, q.stride(0), q.stride(1), q.stride(2),
+         ptr(coords), ptr(valid), ptr(bias), ptr(out), out.stride(0), out.stride(1), out.stride(2),
+         stream_of(q.device))
+    return out

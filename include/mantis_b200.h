@@ -265,6 +265,38 @@ int mb_gemm_rows(const void* x, int x_dtype, int64_t ldx, int64_t m, const float
                  const void* w_image, const float* bias, int relu, void* out, int64_t ldo, float* residual,
                  int64_t ldr, void* stream);
 
+/* ------------------------------------------------- isolated-op workloads --
+ * The two isolated ops of the benchmark suite. Neither exists as an op in the
+ * reference; each restates its workload definition, and the CPU restatements
+ * in oracle/isolated.py pin them.
+ */
+
+/* Hex message passing over cell tokens, fused on the tensor cores:
+ *   out[i] = x[i] + W mean_{s: nbr[i,s] >= 0} x[nbr[i,s]] + bias
+ * x, out (n, 256) bf16 rows (leading dims ldx, ldo; out must not alias x);
+ * nbr (n, 6) int32 rows of x in the reference adjacency slot order
+ * (builder.py:458-471: axes Q, R, QR of builder.py:32, step -1 then +1), -1
+ * where the neighbour is not a token; a row with no neighbour aggregates to
+ * zero. w_image from mb_gemm_weight_image of W (256 x 256); bias fp32 (256,)
+ * or NULL. The mean is rounded to bf16 before the product; fp32 accumulate. */
+int mb_hex_message_pass(const void* x, int64_t ldx, int64_t n, const int32_t* nbr, const void* w_image,
+                        const float* bias, void* out, int64_t ldo, void* stream);
+
+/* Attention over a position's cell tokens with an additive per-head bias
+ * indexed by the relative axial offset, on the tensor cores:
+ *   out[p,h,i] = sum_j softmax_j(q_i.k_j / sqrt(32) + bias[dq+16, dr+16, h]) v_j
+ * dq, dr = key coordinate minus query coordinate (axial q, r), each clamped
+ * to [-16, 16]; keys j < valid[p] only; query rows i >= valid[p] are written
+ * as zeros. q/k/v element (p, h, t, d) at p*s_pos + h*s_head + t*s_row + d,
+ * out likewise with o_*; bf16, head_dim 32, length <= 256; coords (n_pos,
+ * length, 2) int32; valid (n_pos,) int32; bias (33, 33, heads) fp32. The
+ * score arithmetic follows the reference's additive-bias attention
+ * (cell_latents.py:552-555 adds a gathered fp32 bias to fp32 scores). */
+int mb_axial_attention(const void* q, const void* k, const void* v, int64_t n_pos, int heads, int head_dim,
+                       int64_t length, int64_t s_pos, int64_t s_head, int64_t s_row, const int32_t* coords,
+                       const int32_t* valid, const float* bias, void* out, int64_t o_pos, int64_t o_head,
+                       int64_t o_row, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

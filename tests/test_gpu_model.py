@@ -125,8 +125,9 @@ def test_bf16_contract_at_bench_architecture(blocks):
 @pytest.mark.parametrize("autocast", [False, True])
 def test_pipelined_evaluator_equals_one_shot(autocast):
     """Runs of positions copied on a side stream while the previous run
-    computes give the one-shot evaluation's outputs exactly (positions are
-    independent and every kernel works per row)."""
+    computes give the one-shot evaluation's outputs (positions are
+    independent; cuBLAS may pick another GEMM tiling for another row count,
+    so the contract is the reference's batched == single tolerance)."""
     cfg = mb.MantisConfig(h=64, blocks=2, heads=4, cell_latents=True, cell_nodes=True)
     torch.manual_seed(5)
     net = mb.MantisNet(cfg)
@@ -141,4 +142,4 @@ def test_pipelined_evaluator_equals_one_shot(autocast):
     want = one(batch)
     got = runs(batch)
     for a, b in zip(got, want):
-        assert torch.equal(a, b)
+        torch.testing.assert_close(a, b, rtol=0, atol=1e-5 if not autocast else 1e-2)
