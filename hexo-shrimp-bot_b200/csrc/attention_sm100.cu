@@ -7,16 +7,18 @@
 // keys j < valid[b] only; query rows i >= valid[b] are written as zeros.
 // head_dim 32, bf16 q/k/v/out, fp32 scores and softmax.
 //
-// One CTA per (position, head), 8 warps. Q, K and V^T are staged in shared
+// One CTA per (position, head), 16 warps. Q, K and V^T are staged in shared
 // memory in the 128-byte-swizzled K-major layout the UMMA descriptors read
 // (Q and K rows carry the 32 head columns in the first 64 bytes). One thread
 // issues S = Q K^T for both 128-query tiles into TMEM (M=128, N=256, two
-// K=16 steps each). Warps 0-3 own query tile 0 and warps 4-7 tile 1, a thread
-// per query row (TMEM lane quadrant = warp % 4): a first pass over the row's
-// 256 scores finds the biased maximum, a second writes exp(s - max) as bf16
-// into the P tile and sums it. P V^T (M=128, N=32, K=256) then lands in the
-// tile's own, now consumed, TMEM columns, and the row is scaled by 1/sum and
-// stored. Every mbarrier wait is bounded (see gemm_sm100.cu).
+// K=16 steps each). Eight warps own a query tile: a thread holds one query
+// row of one 128-key half (TMEM lane quadrant = warp % 4). A first pass adds
+// the offset bias, writes the biased scores back into TMEM and finds the half
+// maximum; the halves' maxima meet in shared memory; a second pass writes
+// exp(x - max) as bf16 into the P tile and sums it. P V^T (M=128, N=32,
+// K up to 256) then lands in the tile's own, now consumed, TMEM columns, and
+// the row is scaled by 1/sum and stored. Work is bounded by each position's
+// valid length. Every mbarrier wait is bounded (see gemm_sm100.cu).
 #include "common.cuh"
 
 namespace mb {
@@ -25,7 +27,7 @@ namespace sm100 {
 constexpr int AX_L = 256;          // tokens per position (maximum)
 constexpr int AX_D = 32;           // head dim
 constexpr int AX_SPAN = 33;        // relative offsets -16..16
-constexpr int AX_THREADS = 256;  // == AX_L: one thread per key for the coordinate copy
+constexpr int AX_THREADS = 512;
 constexpr int AX_Q_BYTES = AX_L * 128;           // 32 KB, rows padded to 128 B
 constexpr int AX_K_BYTES = AX_L * 128;           // 32 KB
 constexpr int AX_VT_KB = AX_D * 128;             // 4 KB per 64-key block of V^T (32 rows)
@@ -38,7 +40,8 @@ constexpr int AX_VT_OFF = AX_K_OFF + AX_K_BYTES;
 constexpr int AX_P_OFF = AX_VT_OFF + AX_VT_BYTES;
 constexpr int AX_BIAS_OFF = AX_P_OFF + 2 * AX_P_BYTES;
 constexpr int AX_COORD_OFF = AX_BIAS_OFF + 4400;  // 33*33 floats, rounded up
-constexpr int AX_BAR_OFF = AX_COORD_OFF + AX_L * 8;
+constexpr int AX_RED_OFF = AX_COORD_OFF + AX_L * 8;  // per-row half maxima / sums
+constexpr int AX_BAR_OFF = AX_RED_OFF + 2 * 2 * 128 * 4;
 constexpr int AX_SMEM = AX_BAR_OFF + 64 + 1024;   // + alignment slack
 static_assert(AX_SMEM <= 232448, "axial attention shared memory exceeds 227 KB");
 
@@ -56,6 +59,26 @@ __device__ __forceinline__ void umma_i(uint32_t tmem_d, uint64_t adesc, uint64_t
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+
+// tcgen05.st of 32 consecutive columns of this thread's TMEM lane (the
+// counterpart of tmem_ld32), and the wait that orders it before later loads.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Byte offset of 16-byte chunk `c` (0..7) of row `r` in a 128-byte-swizzled
 // K-major block whose rows are 128 bytes.
@@ -131,7 +154,8 @@ __global__ void __launch_bounds__(AX_THREADS, 1) axial_attention_kernel(
     const int idx = tid + u * AX_THREADS;
     bv[u] = idx < AX_SPAN * AX_SPAN ? __ldg(bias + (int64_t)idx * heads + h) : 0.f;
   }
-  const int2 kcv = tid < length ? make_int2(__ldg(cb + 2 * tid), __ldg(cb + 2 * tid + 1)) : make_int2(0, 0);
+  const int2 kcv = tid < length && tid < AX_L ? make_int2(__ldg(cb + 2 * tid), __ldg(cb + 2 * tid + 1))
+                                              : make_int2(0, 0);
 #pragma unroll
   for (int u = 0; u < PER; ++u) {
     const int idx = tid + u * AX_THREADS, r = idx >> 2, c = idx & 3;
@@ -149,7 +173,7 @@ __global__ void __launch_bounds__(AX_THREADS, 1) axial_attention_kernel(
     const int idx = tid + u * AX_THREADS;
     if (idx < AX_SPAN * AX_SPAN) bias_s[idx] = bv[u];
   }
-  kc[tid] = kcv;  // AX_THREADS == AX_L
+  if (tid < AX_L) kc[tid] = kcv;
   fence_proxy_async();  // generic-proxy shared stores -> visible to the tensor cores
   tc_fence_before();
   __syncthreads();
@@ -167,43 +191,63 @@ __global__ void __launch_bounds__(AX_THREADS, 1) axial_attention_kernel(
     }
   }
 
-  const int t = warp >> 2, qd = warp & 3;
+  // Warp roles: tile t = warp / 8 (queries 128t..128t+127), key half hf =
+  // (warp / 4) % 2 (keys 128hf..128hf+127), TMEM lane quadrant qd = warp % 4
+  // (rows 32qd..32qd+31 of the tile); a thread owns one query row of one half.
+  const int t = warp >> 3, hf = (warp >> 2) & 1, qd = warp & 3;
   const int row = t * 128 + qd * 32 + lane;  // this thread's query
   const int rl = qd * 32 + lane;             // row within the tile
   const float scale = 0.17677669529663687f;  // 1 / sqrt(32)
-  float inv = 0.f;
+  // Work is bounded by the valid length: score columns up to nv rounded to a
+  // 32-column load, P and the P V product up to nv rounded to a 64-key block,
+  // and warps whose 32 queries all lie past nv skip the softmax (their rows
+  // are written as zeros). TMEM loads are warp-collective, so the bound is
+  // per warp.
+  const int kend = min(AX_L, (nv + 31) & ~31);
+  const int kblocks = (nv + 63) >> 6;
+  const bool warp_live = t < n_tiles && t * 128 + qd * 32 < nv;
+  const int c_lo = hf * 128, c_hi = min(hf * 128 + 128, kend), p_hi = min(hf * 128 + 128, kblocks * 64);
+  float* red = reinterpret_cast<float*>(smem + AX_RED_OFF);  // [2 tiles][2 halves][128 rows]
+  float* red_t = red + t * 256;
   bool ok = true;
-  if (t < n_tiles) {
+  float m = -INFINITY, sum = 0.f;
+  const uint32_t taddr = tmem + ((uint32_t)(qd * 32) << 16) + t * AX_L;
+  if (warp_live) {
     ok = mbar_wait(smem_u32(&s_done[t]), 0, abort);
     tc_fence_after();
-    const int2 qc = row < length ? make_int2(cb[2 * row], cb[2 * row + 1]) : make_int2(0, 0);
-    const uint32_t taddr = tmem + ((uint32_t)(qd * 32) << 16) + t * AX_L;
-    auto biased = [&](int j, float s) {
-      const int2 c = kc[j];
-      const int dq = min(max(c.x - qc.x, -16), 16) + 16, dr = min(max(c.y - qc.y, -16), 16) + 16;
-      return s * scale + bias_s[dq * AX_SPAN + dr];
-    };
-    float m = -INFINITY;
+    const int2 qc = row < length ? make_int2(__ldg(cb + 2 * row), __ldg(cb + 2 * row + 1)) : make_int2(0, 0);
+    // pass 1: biased scores back into TMEM, the half-row maximum
     if (ok) {
 #pragma unroll 1
-      for (int c0 = 0; c0 < AX_L; c0 += 32) {
+      for (int c0 = c_lo; c0 < c_hi; c0 += 32) {
         float s[32];
         tmem_ld32(taddr + c0, s);
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj)
-          if (c0 + jj < nv) m = fmaxf(m, biased(c0 + jj, s[jj]));
+        for (int jj = 0; jj < 32; ++jj) {
+          const int j = c0 + jj;
+          const int2 c = kc[j];
+          const int dq = min(max(c.x - qc.x, -16), 16) + 16, dr = min(max(c.y - qc.y, -16), 16) + 16;
+          s[jj] = j < nv ? s[jj] * scale + bias_s[dq * AX_SPAN + dr] : -INFINITY;
+          m = fmaxf(m, s[jj]);
+        }
+        tmem_st32(taddr + c0, s);
       }
+      tmem_st_wait();
     }
-    float sum = 0.f;
+    red_t[hf * 128 + rl] = m;
+  }
+  asm volatile("bar.sync %0, 256;" ::"r"(1 + t) : "memory");
+  if (warp_live) {
+    m = fmaxf(red_t[rl], red_t[128 + rl]);
+    // pass 2: P = exp(x - m) in bf16 into the tile's P blocks, the half-row sum
     uint8_t* pt = ps + t * AX_P_BYTES;
 #pragma unroll 1
-    for (int c0 = 0; c0 < AX_L; c0 += 32) {
+    for (int c0 = c_lo; c0 < p_hi; c0 += 32) {
       float s[32];
-      if (ok) tmem_ld32(taddr + c0, s);
+      if (ok && c0 < c_hi) tmem_ld32(taddr + c0, s);
 #pragma unroll
       for (int jj = 0; jj < 32; ++jj) {
-        const int j = c0 + jj;
-        const float p = (ok && j < nv) ? __expf(biased(j, s[jj]) - m) : 0.f;
+        const float p = (ok && c0 + jj < nv) ? __expf(s[jj] - m) : 0.f;
         sum += p;
         s[jj] = p;
       }
@@ -212,41 +256,47 @@ __global__ void __launch_bounds__(AX_THREADS, 1) axial_attention_kernel(
       for (int u = 0; u < 4; ++u)
         store_vec<8>(reinterpret_cast<__nv_bfloat16*>(pt + blk * AX_P_KB + swz(rl, ((c0 & 63) >> 3) + u)), s + 8 * u);
     }
-    inv = sum > 0.f ? 1.f / sum : 0.f;
     fence_proxy_async();
     tc_fence_before();
   }
-  // the tile's four warps have written P and read all of S: O may overwrite S
-  asm volatile("bar.sync %0, 128;" ::"r"(1 + t) : "memory");
-  if (t < n_tiles && qd == 0 && lane == 0) {
+  // the maxima are read; the sums reuse the same slots after the barrier
+  asm volatile("bar.sync %0, 256;" ::"r"(1 + t) : "memory");
+  if (warp_live) red_t[hf * 128 + rl] = sum;
+  asm volatile("bar.sync %0, 256;" ::"r"(1 + t) : "memory");
+  // the tile's eight warps have written P and read all of S: O may overwrite S
+  if (t < n_tiles && hf == 0 && qd == 0 && lane == 0) {
     tc_fence_after();
     const uint32_t d = tmem + t * AX_L;
-    for (int blk = 0; blk < 4; ++blk) {
+    for (int blk = 0; blk < kblocks; ++blk) {
       const uint32_t a0 = smem_u32(ps + t * AX_P_BYTES + blk * AX_P_KB), b0 = smem_u32(vt + blk * AX_VT_KB);
 #pragma unroll
       for (int j = 0; j < 4; ++j) umma_i(d, smem_desc(a0 + j * 32), smem_desc(b0 + j * 32), AX_IDESC_O, (blk | j) != 0);
     }
     umma_commit(smem_u32(&o_done[t]));
   }
-  float o[AX_D];
+  if (hf == 0) {
+    float o[AX_D];
 #pragma unroll
-  for (int i = 0; i < AX_D; ++i) o[i] = 0.f;
-  if (t < n_tiles && ok) {
-    if (mbar_wait(smem_u32(&o_done[t]), 0, abort)) {
-      tc_fence_after();
-      tmem_ld32(tmem + ((uint32_t)(qd * 32) << 16) + t * AX_L, o);
+    for (int i = 0; i < AX_D; ++i) o[i] = 0.f;
+    if (warp_live && ok) {
+      const float tot = red_t[rl] + red_t[128 + rl];
+      const float inv = tot > 0.f ? 1.f / tot : 0.f;
+      if (mbar_wait(smem_u32(&o_done[t]), 0, abort)) {
+        tc_fence_after();
+        tmem_ld32(taddr, o);
 #pragma unroll
-      for (int i = 0; i < AX_D; ++i) o[i] *= inv;
+        for (int i = 0; i < AX_D; ++i) o[i] *= inv;
+      }
     }
-  }
-  if (row < length) {
-    if (row >= nv) {
+    if (row < length) {
+      if (row >= nv) {
 #pragma unroll
-      for (int i = 0; i < AX_D; ++i) o[i] = 0.f;
+        for (int i = 0; i < AX_D; ++i) o[i] = 0.f;
+      }
+      __nv_bfloat16* orow = ob + row * o_row;
+#pragma unroll
+      for (int i = 0; i < AX_D / 8; ++i) store_vec<8>(orow + 8 * i, o + 8 * i);
     }
-    __nv_bfloat16* orow = ob + row * o_row;
-#pragma unroll
-    for (int i = 0; i < AX_D / 8; ++i) store_vec<8>(orow + 8 * i, o + 8 * i);
   }
   tc_fence_before();
   __syncthreads();

@@ -176,7 +176,11 @@ struct Params {
 template <int PRO, int EPI, bool XS>
 struct Plan {
   static constexpr int A_BUFS = XS ? 1 : 2;
-  static constexpr int PRODUCERS = 7;           // warps writing the A tile
+  // Warps writing the A tile (1..PRODUCERS) and draining TMEM (the rest).
+  // The neighbour-gather prologue is latency-bound, so it gets more warps and
+  // the epilogue four (one per TMEM lane quadrant, all 256 columns each).
+  static constexpr int PRODUCERS = PRO == PRO_HEXMEAN ? 11 : 7;
+  static constexpr int EPI_WARPS = 16 - 1 - PRODUCERS;
   static constexpr int A_OFF = 0;
   static constexpr int W_OFF = A_OFF + A_BUFS * A_BYTES;
   static constexpr int X_OFF = W_OFF + W_STAGES * W_KB_BYTES;
@@ -218,7 +222,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
       mbar_init(smem_u32(&w_full[i]), 1);
       mbar_init(smem_u32(&w_empty[i]), 1);
       mbar_init(smem_u32(&t_full[i]), 1);
-      mbar_init(smem_u32(&t_empty[i]), EPILOGUE);
+      mbar_init(smem_u32(&t_empty[i]), L::EPI_WARPS);
     }
     for (int i = 0; i < X_STAGES; ++i) {
       mbar_init(smem_u32(&x_full[i]), 1);
@@ -305,7 +309,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
         if (!ok) break;
       }
     }
-  } else if (warp >= 1 && warp < 8) {
+  } else if (warp >= 1 && warp < 1 + L::PRODUCERS) {
     // ------------------------------------------------------ A producers
     const int kb = lane >> 3, chunk = lane & 7;  // lane owns columns [8*lane, 8*lane+8)
     // LayerNorm of NR rows at once: the NR warp reductions are interleaved so
@@ -390,13 +394,27 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
         if (lane == 0) mbar_arrive(smem_u32(&a_full[0]));
       }
     } else {
-      const int pw = warp - 1;  // 0..6: rows pw, pw + 7, ... of each tile
+      const int pw = warp - 1;  // rows pw, pw + PRODUCERS, ... of each tile
       for (int64_t t = 0; t < my_tiles && !*abort; ++t) {
         const int64_t tile = blockIdx.x + t * gridDim.x;
         const uint32_t ab = t % L::A_BUFS, aph = (t / L::A_BUFS) & 1;
         uint8_t* abuf = a_smem + ab * A_BYTES;
         bool ok = true;
         constexpr int NRB = PRO == PRO_HEXMEAN ? 3 : RB;  // rows in flight (6 gathers each for HEXMEAN)
+        // HEXMEAN: lanes 0-5 hold the six neighbour slots of each row of a
+        // batch; the next batch's slots are requested before this batch's
+        // gathers, so the table read overlaps the row gathers.
+        constexpr int NHX = PRO == PRO_HEXMEAN ? NRB : 1;
+        int hx_cur[NHX], hx_next[NHX];
+        auto fetch_slots = [&](int rb, int* out) {
+#pragma unroll
+          for (int u = 0; u < NHX; ++u) {
+            const int rr = (rb + u) * L::PRODUCERS + pw;
+            const int64_t row = tile * BM + rr;
+            out[u] = (rr < BM && row < p.m && lane < HEX_SLOTS) ? __ldg(p.nbr + row * HEX_SLOTS + lane) : -1;
+          }
+        };
+        if constexpr (PRO == PRO_HEXMEAN) fetch_slots(0, hx_cur);
         for (int r0 = 0; r0 * L::PRODUCERS + pw < BM; r0 += NRB) {
           float v[NRB][8];
 #pragma unroll
@@ -421,13 +439,8 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
             // 16-byte column chunk of each present neighbour row, all NRB rows'
             // gathers issued before the first is summed
             const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(p.x);
-            int my[NRB];
-#pragma unroll
-            for (int u = 0; u < NRB; ++u) {
-              const int64_t row = tile * BM + (r0 + u) * L::PRODUCERS + pw;
-              const bool live = (r0 + u) * L::PRODUCERS + pw < BM && row < p.m;
-              my[u] = (live && lane < HEX_SLOTS) ? __ldg(p.nbr + row * HEX_SLOTS + lane) : -1;
-            }
+            fetch_slots(r0 + NRB, hx_next);
+            const int* my = hx_cur;
             uint4 raw[NRB][HEX_SLOTS];
             int present[NRB];
 #pragma unroll
@@ -461,6 +474,8 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
 #pragma unroll
               for (int i = 0; i < 8; ++i) v[u][i] = acc[i] * inv;
             }
+#pragma unroll
+            for (int u = 0; u < NHX; ++u) hx_cur[u] = hx_next[u];
           }
           // the first batch is fetched before waiting for the buffer to drain
           if (r0 == 0 && !mbar_wait(smem_u32(&a_empty[ab]), aph ^ 1, abort)) { ok = false; break; }
@@ -477,11 +492,12 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
         if (lane == 0) mbar_arrive(smem_u32(&a_full[ab]));
       }
     }
-  } else if (warp >= 8) {
+  } else if (warp >= 1 + L::PRODUCERS) {
     // ------------------------------------------------------ epilogue
-    const int ew = warp - 8;          // 0..7
+    const int ew = warp - 1 - L::PRODUCERS;  // 0..EPI_WARPS-1
     const int q = warp & 3;           // TMEM lane quadrant this warp may access
-    const int half = ew >> 2;         // 128-column half
+    constexpr int PARTS = L::EPI_WARPS / 4;  // column ranges per quadrant
+    const int half = ew >> 2;                // this warp's column range
     float* stage = e_smem + ew * EPI_WARP_FLOATS;
     for (int64_t t = 0; t < my_tiles && !*abort; ++t) {
       const int64_t tile = blockIdx.x + t * gridDim.x;
@@ -491,7 +507,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
       const int64_t row0 = tile * BM + q * 32;  // this warp's 32 rows
       const int64_t row = row0 + lane;
 #pragma unroll 1
-      for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 32) {
+      for (int c0 = half * (BN / PARTS); c0 < (half + 1) * (BN / PARTS); c0 += 32) {
         float v[32];
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + tb * BN + c0, v);
         if (p.bias) {
