@@ -11,10 +11,11 @@
 // memory in the 128-byte-swizzled K-major layout the UMMA descriptors read
 // (Q and K rows carry the 32 head columns in the first 64 bytes). One thread
 // issues S = Q K^T for both 128-query tiles into TMEM (M=128, N=256, two
-// K=16 steps each). Eight warps own a query tile: a thread holds one query
-// row of one 128-key half (TMEM lane quadrant = warp % 4). A first pass adds
-// the offset bias, writes the biased scores back into TMEM and finds the half
-// maximum; the halves' maxima meet in shared memory; a second pass writes
+// K=16 steps each). The warps split each live tile's keys into parts (two
+// parts per tile when both tiles are live, else four): a thread holds one
+// query row of one part (TMEM lane quadrant = warp % 4). A first pass adds
+// the offset bias, writes the biased scores back into TMEM and finds the part
+// maximum; the parts' maxima meet in shared memory; a second pass writes
 // exp(x - max) as bf16 into the P tile and sums it. P V^T (M=128, N=32,
 // K up to 256) then lands in the tile's own, now consumed, TMEM columns, and
 // the row is scaled by 1/sum and stored. Work is bounded by each position's
@@ -194,7 +195,10 @@ __global__ void __launch_bounds__(AX_THREADS, 1) axial_attention_kernel(
   // Warp roles: tile t = warp / 8 (queries 128t..128t+127), key half hf =
   // (warp / 4) % 2 (keys 128hf..128hf+127), TMEM lane quadrant qd = warp % 4
   // (rows 32qd..32qd+31 of the tile); a thread owns one query row of one half.
-  const int t = warp >> 3, hf = (warp >> 2) & 1, qd = warp & 3;
+  // With one live query tile all sixteen warps work on it in four key parts;
+  // with two, eight warps per tile in two parts.
+  const int NP = n_tiles == 2 ? 2 : 4;
+  const int t = warp / (4 * NP), hf = (warp >> 2) % NP, qd = warp & 3;
   const int row = t * 128 + qd * 32 + lane;  // this thread's query
   const int rl = qd * 32 + lane;             // row within the tile
   const float scale = 0.17677669529663687f;  // 1 / sqrt(32)
@@ -206,9 +210,12 @@ __global__ void __launch_bounds__(AX_THREADS, 1) axial_attention_kernel(
   const int kend = min(AX_L, (nv + 31) & ~31);
   const int kblocks = (nv + 63) >> 6;
   const bool warp_live = t < n_tiles && t * 128 + qd * 32 < nv;
-  const int c_lo = hf * 128, c_hi = min(hf * 128 + 128, kend), p_hi = min(hf * 128 + 128, kblocks * 64);
-  float* red = reinterpret_cast<float*>(smem + AX_RED_OFF);  // [2 tiles][2 halves][128 rows]
-  float* red_t = red + t * 256;
+  // this part's keys: a multiple of 32, parts together covering kblocks * 64
+  const int span = ((kend + NP * 32 - 1) / (NP * 32)) * 32;
+  const int c_lo = hf * span, c_hi = min(c_lo + span, kend), p_hi = min(c_lo + span, kblocks * 64);
+  const int nthr = 128 * NP;  // threads of this tile's group
+  float* red = reinterpret_cast<float*>(smem + AX_RED_OFF);  // [tile][part][128 rows]
+  float* red_t = red + t * NP * 128;
   bool ok = true;
   float m = -INFINITY, sum = 0.f;
   const uint32_t taddr = tmem + ((uint32_t)(qd * 32) << 16) + t * AX_L;
@@ -236,9 +243,9 @@ __global__ void __launch_bounds__(AX_THREADS, 1) axial_attention_kernel(
     }
     red_t[hf * 128 + rl] = m;
   }
-  asm volatile("bar.sync %0, 256;" ::"r"(1 + t) : "memory");
+  asm volatile("bar.sync %0, %1;" ::"r"(1 + t), "r"(nthr) : "memory");
   if (warp_live) {
-    m = fmaxf(red_t[rl], red_t[128 + rl]);
+    for (int pp = 0; pp < NP; ++pp) m = fmaxf(m, red_t[pp * 128 + rl]);
     // pass 2: P = exp(x - m) in bf16 into the tile's P blocks, the half-row sum
     uint8_t* pt = ps + t * AX_P_BYTES;
 #pragma unroll 1
@@ -260,9 +267,9 @@ __global__ void __launch_bounds__(AX_THREADS, 1) axial_attention_kernel(
     tc_fence_before();
   }
   // the maxima are read; the sums reuse the same slots after the barrier
-  asm volatile("bar.sync %0, 256;" ::"r"(1 + t) : "memory");
+  asm volatile("bar.sync %0, %1;" ::"r"(1 + t), "r"(nthr) : "memory");
   if (warp_live) red_t[hf * 128 + rl] = sum;
-  asm volatile("bar.sync %0, 256;" ::"r"(1 + t) : "memory");
+  asm volatile("bar.sync %0, %1;" ::"r"(1 + t), "r"(nthr) : "memory");
   // the tile's eight warps have written P and read all of S: O may overwrite S
   if (t < n_tiles && hf == 0 && qd == 0 && lane == 0) {
     tc_fence_after();
@@ -279,7 +286,8 @@ __global__ void __launch_bounds__(AX_THREADS, 1) axial_attention_kernel(
 #pragma unroll
     for (int i = 0; i < AX_D; ++i) o[i] = 0.f;
     if (warp_live && ok) {
-      const float tot = red_t[rl] + red_t[128 + rl];
+      float tot = 0.f;
+      for (int pp = 0; pp < NP; ++pp) tot += red_t[pp * 128 + rl];
       const float inv = tot > 0.f ? 1.f / tot : 0.f;
       if (mbar_wait(smem_u32(&o_done[t]), 0, abort)) {
         tc_fence_after();
@@ -296,6 +304,16 @@ __global__ void __launch_bounds__(AX_THREADS, 1) axial_attention_kernel(
       __nv_bfloat16* orow = ob + row * o_row;
 #pragma unroll
       for (int i = 0; i < AX_D / 8; ++i) store_vec<8>(orow + 8 * i, o + 8 * i);
+    }
+  } else if (NP == 4 && hf == 1) {
+    // fewer than two live tiles: every warp worked on tile 0, so these warps
+    // write tile 1's rows, all past the valid length, as zeros
+    const int zrow = 128 + qd * 32 + lane;
+    if (zrow < length) {
+      float o[8] = {};
+      __nv_bfloat16* orow = ob + zrow * o_row;
+#pragma unroll
+      for (int i = 0; i < AX_D / 8; ++i) store_vec<8>(orow + 8 * i, o);
     }
   }
   tc_fence_before();

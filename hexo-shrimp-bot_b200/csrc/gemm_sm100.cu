@@ -512,7 +512,10 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + tb * BN + c0, v);
         if (p.bias) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] += __ldg(p.bias + c0 + i);
+          for (int i = 0; i < 8; ++i) {
+            const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + c0) + i);
+            v[4 * i] += bb.x; v[4 * i + 1] += bb.y; v[4 * i + 2] += bb.z; v[4 * i + 3] += bb.w;
+          }
         }
         if (p.relu) {
 #pragma unroll
@@ -616,6 +619,7 @@ int mb_gemm_rows(const void* x, int x_dtype, int64_t ldx, int64_t m, const float
   MB_REQUIRE(!residual || (aligned(residual, 16) && (ldr * 4) % 16 == 0),
              "gemm_rows: residual rows must be 16-byte aligned");
   MB_REQUIRE(aligned(w_image, 16), "gemm_rows: weight image must be 16-byte aligned");
+  MB_REQUIRE(!bias || aligned(bias, 16), "gemm_rows: bias must be 16-byte aligned");
   if (g_num_sms == 0) {
     int dev = 0;
     cudaGetDevice(&dev);
@@ -654,7 +658,8 @@ int mb_hex_message_pass(const void* x, int64_t ldx, int64_t n, const int32_t* nb
   MB_REQUIRE(x != out, "hex_message_pass: out must not alias x (neighbour rows are read while rows are written)");
   MB_REQUIRE(aligned(x, 16) && (ldx * 2) % 16 == 0 && ldx >= KDIM, "hex_message_pass: x rows must be 16-byte aligned");
   MB_REQUIRE(aligned(out, 16) && (ldo * 2) % 16 == 0 && ldo >= BN, "hex_message_pass: out rows must be 16-byte aligned");
-  MB_REQUIRE(aligned(nbr, 4) && aligned(w_image, 16), "hex_message_pass: misaligned table or weight image");
+  MB_REQUIRE(aligned(nbr, 4) && aligned(w_image, 16) && (!bias || aligned(bias, 16)),
+             "hex_message_pass: misaligned table, weight image or bias");
   if (g_num_sms == 0) {
     int dev = 0;
     cudaGetDevice(&dev);
