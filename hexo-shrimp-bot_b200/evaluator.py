@@ -88,16 +88,17 @@ _SPLIT_FIELDS = {
 }
 
 
-def split_points(batch: Batch, n_parts: int) -> list[int]:
-    """Position boundaries of up to ``n_parts`` runs with about equal cells."""
-    cells = batch.legal_offsets.numpy()
+def split_points(batch: Batch, part: int) -> list[int]:
+    """Position boundaries of the runs: a short lead run (a quarter of
+    ``part``, at most an eighth of the batch), whose copy is the only one
+    not hidden behind compute, then runs of ``part`` positions."""
     p = batch.n_pos
-    cuts = [0]
-    for k in range(1, n_parts):
-        c = int(np.searchsorted(cells, cells[-1] * k / n_parts))
-        if cuts[-1] < c < p:
-            cuts.append(c)
-    cuts.append(p)
+    lead = max(1, min(part // 4, p // 8))
+    cuts = [0, lead]
+    while cuts[-1] + part < p:
+        cuts.append(cuts[-1] + part)
+    if cuts[-1] < p:
+        cuts.append(p)
     return cuts
 
 
@@ -176,13 +177,17 @@ def network_evaluate(model, cfg):
     streams = {}
 
     def run_parts(batch: Batch, eng):
-        """Copy run k + 1 on a side stream while run k computes."""
-        cuts = split_points(batch, max(1, batch.n_pos // part))
+        """Copy run k + 1 in on a side stream while run k computes, and copy
+        run k's outputs out on it while run k + 1 computes, into one pinned
+        host buffer (the caching host allocator recycles it between calls)."""
+        cuts = split_points(batch, part)
         off = _offsets(batch, fields)
         compute = torch.cuda.current_stream(device)
         copy = streams.get("copy")
         if copy is None:
             copy = streams["copy"] = torch.cuda.Stream(device)
+        n = int(off["cell"][-1])
+        host_out = torch.empty(3 * n, dtype=torch.float32, pin_memory=True)
 
         def issue(k):
             copy.wait_stream(compute)  # buffers the allocator hands out may still be read by compute
@@ -192,7 +197,6 @@ def network_evaluate(model, cfg):
                 done.record(copy)
             return b, done
 
-        outs = []
         nxt = issue(0)
         for k in range(len(cuts) - 1):
             b, done = nxt
@@ -204,19 +208,29 @@ def network_evaluate(model, cfg):
                 nxt = issue(k + 1)
             policy, critic = eng.evaluate(b)
             q_score, q_values = ops.compose(critic, b.legal_offsets, cfg.mass_floor)
-            outs.append((policy.float(), q_score, q_values))
-        return [torch.cat(x) for x in zip(*outs)]
+            res = (policy.float(), q_score, q_values)
+            ready = torch.cuda.Event()
+            ready.record(compute)
+            copy.wait_event(ready)
+            c0, c1 = int(off["cell"][cuts[k]]), int(off["cell"][cuts[k + 1]])
+            with torch.cuda.stream(copy):
+                for j, t in enumerate(res):
+                    t.record_stream(copy)
+                    host_out[j * n + c0:j * n + c1].copy_(t, non_blocking=True)
+        copy.synchronize()
+        return host_out[:n], host_out[n:2 * n], host_out[2 * n:]
 
     def evaluate(batch: Batch):
         with _gpu_lock, torch.no_grad():
             eng = model.engine(dtype, gemm=gemm)
             if pipelined and batch.n_pos >= 2 * part:
-                policy, q_score, q_values = run_parts(batch, eng)
-            else:
-                b = to_device(batch, device, fields)
-                policy, critic = eng.evaluate(b)
-                q_score, q_values = ops.compose(critic, b.legal_offsets, cfg.mass_floor)
-                policy = policy.float()
+                out = run_parts(batch, eng)
+                check_device_error(device)
+                return out
+            b = to_device(batch, device, fields)
+            policy, critic = eng.evaluate(b)
+            q_score, q_values = ops.compose(critic, b.legal_offsets, cfg.mass_floor)
+            policy = policy.float()
             out = torch.cat([policy, q_score, q_values]).to("cpu")
             check_device_error(device)
             n = policy.shape[0]

@@ -24,12 +24,12 @@ def batch():
     return mb.collate([mb.from_spec(s) for s in specs])
 
 
-@pytest.mark.parametrize("n_parts", [1, 2, 3, 5])
-def test_runs_reassemble_the_batch(batch, n_parts):
+@pytest.mark.parametrize("part", [1, 2, 3, 5, 100])
+def test_runs_reassemble_the_batch(batch, part):
     cfg = mb.MantisConfig(h=32, blocks=1, heads=2, cell_latents=True, cell_nodes=True)
     fields = E.needed_fields(cfg)
     assert E.split_supported(fields)
-    cuts = E.split_points(batch, n_parts)
+    cuts = E.split_points(batch, part)
     assert cuts[0] == 0 and cuts[-1] == batch.n_pos and all(a < b for a, b in zip(cuts, cuts[1:]))
     off = E._offsets(batch, fields)
     parts = [E.part_to_device(batch, fields, off, a, b, "cpu") for a, b in zip(cuts, cuts[1:])]
