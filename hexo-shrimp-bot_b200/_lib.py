@@ -37,6 +37,7 @@ SIGNATURES = {
     "mb_segment_attention": "plpplilliiplpipppppilppp",
     "mb_segment_attention_grouped": "plpplilliiplpippppppllpilp",
     "mb_hex_message_pass": "pllpppplp",
+    "mb_gemm_rows_ln": "pllppplfpppilpppilpppilp",
     "mb_axial_attention": "pppliillllpppplllp",
     "mb_stone_attention": "pppiliilllplplipilllp",
     "mb_window_latent_read": "plpplilliipppippp",

@@ -98,7 +98,7 @@ __device__ __forceinline__ float head_sum(float x, int lph) {
 }
 
 // ------------------------------------------------------- segment attention
-// One warp per batch of kSegRows consecutive query rows (blocks of 8 warps,
+// One warp per batch of kSegRows consecutive query rows (blocks of 2 warps,
 // scheduled in row order, so the GPU works on a narrow band of positions at a
 // time and the gathered source rows stay L2-resident). The batch's run bounds
 // and its first 32 edge indices are fetched by one coalesced load each and
@@ -106,11 +106,12 @@ __device__ __forceinline__ float head_sum(float x, int lph) {
 // issued together with its query load) instead of three (run bounds, edge
 // indices, gathers). Two edges per iteration keep two K/V row pairs in flight
 // per lane.
-constexpr int kSegWarps = 8;
+constexpr int kSegWarps = 2;   // small blocks: a block's slot frees as soon as its 2 warps finish
 constexpr int kSegRows = 4;
+constexpr int kSegBlocksPerSM = 12;  // 24 resident warps at <= 80 registers
 
 template <typename T, typename TO, typename TV, int VEC, bool HAS_VCLS>
-__global__ void __launch_bounds__(kSegWarps * 32, 3) segment_attention_kernel(
+__global__ void __launch_bounds__(kSegWarps * 32, kSegBlocksPerSM) segment_attention_kernel(
     const T* __restrict__ q, int64_t ldq, const T* __restrict__ k, const T* __restrict__ v, int64_t ldkv, int64_t n_q,
     int64_t n_src, int heads, int hd, const float* __restrict__ bias, int64_t n_cls, const TV* __restrict__ vcls,
     const int64_t* __restrict__ seg_ptr, const int64_t* __restrict__ src, const int64_t* __restrict__ cls,
@@ -679,64 +680,86 @@ __global__ void __cluster_dims__(1, kReadSplit, 1) __launch_bounds__(kReadWarps 
   cluster.sync();  // every CTA's shared state stays alive until the first CTA has read it
 }
 
-// Broadcast: warp per window; the window's query row and its position's four
-// latent K and V rows are all requested before the first is used.
+// Broadcast: a warp takes kBcastWindows consecutive windows. Their positions
+// come in one load (a lane each) and their query rows are all requested at
+// once; a position's four latent K and V rows are fetched when the position
+// changes, so the run of windows of one position shares them.
+constexpr int kBcastWindows = 4;
+
 template <typename T, typename TO, int VEC>
 __global__ void __launch_bounds__(256) latent_broadcast_kernel(
     const T* __restrict__ q, int64_t ldq, const T* __restrict__ k, const T* __restrict__ v, int64_t ldkv,
     int64_t n_pos, int64_t n_windows, int heads, int hd, const int64_t* __restrict__ window_pos, TO* __restrict__ out,
     float* __restrict__ m_out, float* __restrict__ l_out, float scale) {
-  const int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (w >= n_windows) return;
+  const int64_t w0 = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * kBcastWindows;
+  if (w0 >= n_windows) return;
   const int lane = threadIdx.x & 31;
+  const int nw = (int)(n_windows - w0 < kBcastWindows ? n_windows - w0 : kBcastWindows);
   const int H = heads * hd;
   const int lph = hd / VEC;
-  const int64_t p = window_pos[w];
-  if (p < 0 || p >= n_pos) { report(ERR_INDEX); return; }
+  const int64_t my_pos = lane < nw ? window_pos[w0 + lane] : 0;
   for (int c0 = 0; c0 < H; c0 += 32 * VEC) {
     const int col = c0 + lane * VEC;
     const bool live = col < H;  // H < 32 leaves upper lanes idle
-    Raw<T, VEC> qr = {}, kr[4] = {}, vr[4] = {};
+    Raw<T, VEC> qr[kBcastWindows] = {}, kr[4] = {}, vr[4] = {};
     if (live) {
-      raw_load<false, VEC>(q + w * ldq + col, qr);
+#pragma unroll
+      for (int u = 0; u < kBcastWindows; ++u)
+        if (u < nw) raw_load<false, VEC>(q + (w0 + u) * ldq + col, qr[u]);
+    }
+    int64_t have = -1;  // the position whose latent rows kr / vr hold
+#pragma unroll
+    for (int u = 0; u < kBcastWindows; ++u) {
+      if (u >= nw) break;
+      const int64_t w = w0 + u;
+      const int64_t p = __shfl_sync(0xffffffffu, my_pos, u);
+      if (p < 0 || p >= n_pos) {
+        report(ERR_INDEX);
+        continue;
+      }
+      if (p != have) {
+        have = p;
+        if (live) {
+#pragma unroll
+          for (int s = 0; s < 4; ++s) {
+            raw_load<false, VEC>(k + (p * 4 + s) * ldkv + col, kr[s]);
+            raw_load<false, VEC>(v + (p * 4 + s) * ldkv + col, vr[s]);
+          }
+        }
+      }
+      float qv[VEC], sc[4], mx = kNegInf;
+      raw_unpack<VEC>(qr[u], qv);
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
-        raw_load<false, VEC>(k + (p * 4 + s) * ldkv + col, kr[s]);
-        raw_load<false, VEC>(v + (p * 4 + s) * ldkv + col, vr[s]);
+        float kv[VEC];
+        raw_unpack<VEC>(kr[s], kv);
+        float d = 0.f;
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) d += qv[i] * kv[i];
+        sc[s] = group_sum(d, lph) * scale;
+        mx = fmaxf(mx, sc[s]);
       }
-    }
-    float qv[VEC], sc[4], mx = kNegInf;
-    raw_unpack<VEC>(qr, qv);
+      float l = 0.f, acc[VEC];
 #pragma unroll
-    for (int s = 0; s < 4; ++s) {
-      float kv[VEC];
-      raw_unpack<VEC>(kr[s], kv);
-      float d = 0.f;
+      for (int i = 0; i < VEC; ++i) acc[i] = 0.f;
 #pragma unroll
-      for (int u = 0; u < VEC; ++u) d += qv[u] * kv[u];
-      sc[s] = group_sum(d, lph) * scale;
-      mx = fmaxf(mx, sc[s]);
-    }
-    float l = 0.f, acc[VEC];
+      for (int s = 0; s < 4; ++s) {
+        const float pr = __expf(sc[s] - mx);
+        l += pr;
+        float vv[VEC];
+        raw_unpack<VEC>(vr[s], vv);
 #pragma unroll
-    for (int u = 0; u < VEC; ++u) acc[u] = 0.f;
+        for (int i = 0; i < VEC; ++i) acc[i] += pr * vv[i];
+      }
+      const float inv = 1.f / l;
 #pragma unroll
-    for (int s = 0; s < 4; ++s) {
-      const float pr = __expf(sc[s] - mx);
-      l += pr;
-      float vv[VEC];
-      raw_unpack<VEC>(vr[s], vv);
-#pragma unroll
-      for (int u = 0; u < VEC; ++u) acc[u] += pr * vv[u];
-    }
-    const float inv = 1.f / l;
-#pragma unroll
-    for (int u = 0; u < VEC; ++u) acc[u] *= inv;
-    if (!live) continue;
-    store_vec<VEC>(out + w * H + col, acc);
-    if (m_out && lane % lph == 0) {
-      m_out[w * heads + col / hd] = mx;
-      l_out[w * heads + col / hd] = l;
+      for (int i = 0; i < VEC; ++i) acc[i] *= inv;
+      if (!live) continue;
+      store_vec<VEC>(out + w * H + col, acc);
+      if (m_out && lane % lph == 0) {
+        m_out[w * heads + col / hd] = mx;
+        l_out[w * heads + col / hd] = l;
+      }
     }
   }
 }
@@ -965,7 +988,7 @@ int mb_window_latent_broadcast(const void* q, int64_t ldq, const void* k, const 
   MB_DISPATCH_T(dtype, T, [&] {
     MB_DISPATCH_T(out_dtype, TO, [&] {
       MB_DISPATCH_VEC(vec, V, [&] {
-        latent_broadcast_kernel<T, TO, V><<<(unsigned)cdiv(n_windows, 8), 256, 0, s>>>(
+        latent_broadcast_kernel<T, TO, V><<<(unsigned)cdiv(n_windows, 8 * kBcastWindows), 256, 0, s>>>(
             (const T*)q, ldq, (const T*)k, (const T*)v, ldkv, n_pos, n_windows, heads, head_dim, window_pos,
             (TO*)out, m, l, scale);
       });

@@ -51,7 +51,6 @@ constexpr int KBLOCKS = KDIM / BK;                 // 4
 constexpr int A_BYTES = BM * KDIM * 2;             // 64 KB
 constexpr int A_KB_BYTES = BM * BK * 2;            // 16 KB per K-block
 constexpr int W_KB_BYTES = BN * BK * 2;            // 32 KB per K-block
-constexpr int W_STAGES = 2;
 constexpr int XG_ROWS = 32;                        // rows per staged group
 constexpr int XG_BYTES = XG_ROWS * KDIM * 4;       // 32 KB of fp32 rows
 constexpr int X_STAGES = 3;
@@ -59,13 +58,14 @@ constexpr int TMEM_COLS = 512;                     // 2 accumulators of 256 colu
 constexpr int EPILOGUE = 8;
 constexpr int THREADS = 32 * 16;
 constexpr int RB = 8;                              // rows in flight per direct producer warp
-constexpr int EPI_PITCH = 33;                      // padded transpose row (floats)
-constexpr int EPI_WARP_FLOATS = 32 * EPI_PITCH;
+constexpr int BOX_FLOATS = 32 * 32;
+constexpr int OUT_BOX_BYTES = 32 * 32 * 2;          // 32 rows x 32 bf16 LayerNorm outputs
 constexpr int BAR_BYTES = 256;
 constexpr long long kWaitCycles = 4000000000LL;   // ~2 s at 1.9 GHz
 
 enum Prologue { PRO_LN = 0, PRO_COPY = 1, PRO_HEXMEAN = 2 };
-enum Epilogue { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_ADD_X = 2 };
+enum Epilogue { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_ADD_X = 2, EPI_RESID_LN = 3 };
+constexpr int MAX_LN = 3;
 constexpr int HEX_SLOTS = 6;
 
 constexpr uint32_t ERR_TIMEOUT = 4;
@@ -113,6 +113,15 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
                : "memory");
 }
 
+// 16-byte cp.async (L2 only) that zero-fills the destination when `live` is
+// false, and the group commit / wait that orders a warp's boxes.
+__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, bool live) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(live ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -155,6 +164,26 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// tcgen05.st of 32 consecutive columns of this thread's TMEM lane (the
+// counterpart of tmem_ld32), and the wait that orders it before later loads.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 struct Params {
   const void* x;        // prologue input rows (fp32 for LN, bf16 for COPY)
   int64_t ldx;
@@ -170,12 +199,29 @@ struct Params {
   float* res;           // EPI_RESIDUAL
   int64_t ldr;
   const int32_t* nbr;   // PRO_HEXMEAN: (m, 6) neighbour rows of x, -1 = absent
+  // EPI_RESID_LN: up to three LayerNorms of the updated residual row
+  int n_ln;
+  float ln_eps;
+  const float* ln_g[MAX_LN];
+  const float* ln_b[MAX_LN];
+  void* ln_out[MAX_LN];
+  int ln_dtype[MAX_LN];
+  int64_t ln_ld[MAX_LN];
 };
 
 // Shared-memory plan of one variant (all region offsets 1024-byte aligned).
 template <int PRO, int EPI, bool XS>
 struct Plan {
-  static constexpr int A_BUFS = XS ? 1 : 2;
+  // The residual epilogues stream the residual through a shared-memory ring,
+  // which takes the second A buffer's space (the epilogue, not the MMA,
+  // bounds these variants).
+  static constexpr bool RESID = EPI == EPI_RESIDUAL || EPI == EPI_RESID_LN;
+  static constexpr int A_BUFS = (XS || RESID) ? 1 : 2;
+  // W K-blocks in flight. The residual epilogues are long enough to hide a
+  // one-stage W stream; the freed 32 KB hold the output staging boxes.
+  static constexpr int W_STAGES = RESID ? 1 : 2;
+  // Residual boxes (32 rows x 32 fp32 columns, 4 KB) per epilogue warp.
+  static constexpr int RING = 3;
   // Warps writing the A tile (1..PRODUCERS) and draining TMEM (the rest).
   // The neighbour-gather prologue is latency-bound, so it gets more warps and
   // the epilogue four (one per TMEM lane quadrant, all 256 columns each).
@@ -185,7 +231,12 @@ struct Plan {
   static constexpr int W_OFF = A_OFF + A_BUFS * A_BYTES;
   static constexpr int X_OFF = W_OFF + W_STAGES * W_KB_BYTES;
   static constexpr int E_OFF = X_OFF + (XS ? X_STAGES * XG_BYTES : 0);
-  static constexpr int BAR_OFF = E_OFF + (EPI == EPI_RESIDUAL ? EPILOGUE * EPI_WARP_FLOATS * 4 : 0);
+  static constexpr int OUT_OFF = E_OFF + (RESID ? EPILOGUE * RING * BOX_FLOATS * 4 : 0);
+  // bias and the LayerNorms' gamma / beta, copied once per CTA (uniform
+  // reads in the epilogue, kept out of the busy L1 miss path)
+  static constexpr int PAR_OFF = OUT_OFF + (EPI == EPI_RESID_LN ? EPILOGUE * OUT_BOX_BYTES : 0);
+  static constexpr int RED_OFF = PAR_OFF + (RESID ? (1 + 2 * MAX_LN) * BN * 4 : 0);
+  static constexpr int BAR_OFF = RED_OFF + (EPI == EPI_RESID_LN ? 4 * 64 * 4 : 0);
   static constexpr int SMEM = BAR_OFF + BAR_BYTES + 1024 /*alignment slack*/;
   static_assert(SMEM <= 232448, "shared memory plan exceeds 227 KB");
 };
@@ -237,6 +288,18 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  float* par = reinterpret_cast<float*>(smem + L::PAR_OFF);  // [bias | g0 b0 | g1 b1 | g2 b2] x BN
+  if constexpr (L::RESID) {
+    if (threadIdx.x < BN) {
+      const int c = threadIdx.x;
+      par[c] = p.bias ? p.bias[c] : 0.f;
+#pragma unroll
+      for (int o = 0; o < MAX_LN; ++o) {
+        par[(1 + 2 * o) * BN + c] = o < p.n_ln ? p.ln_g[o][c] : 0.f;
+        par[(2 + 2 * o) * BN + c] = o < p.n_ln ? p.ln_b[o][c] : 0.f;
+      }
+    }
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -249,7 +312,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
       uint64_t issued = 0;
       auto issue_w = [&](uint64_t upto) -> bool {
         for (; issued < upto && issued < total_kb; ++issued) {
-          const uint32_t s = issued % W_STAGES, ph = (issued / W_STAGES) & 1;
+          const uint32_t s = issued % L::W_STAGES, ph = (issued / L::W_STAGES) & 1;
           if (!mbar_wait(smem_u32(&w_empty[s]), ph ^ 1, abort)) return false;
           mbar_expect_tx(smem_u32(&w_full[s]), W_KB_BYTES);
           bulk_g2s(smem_u32(w_smem + s * W_KB_BYTES),
@@ -258,7 +321,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
         }
         return true;
       };
-      bool ok = issue_w(W_STAGES);
+      bool ok = issue_w(L::W_STAGES);
       uint64_t used = 0;
       for (int64_t t = 0; ok && t < my_tiles && !*abort; ++t) {
         const uint32_t tb = t & 1, tph = (t >> 1) & 1;
@@ -268,7 +331,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
         tc_fence_after();
         const uint32_t d = tmem_base + tb * BN;
         for (int kb = 0; kb < KBLOCKS; ++kb, ++used) {
-          const uint32_t s = used % W_STAGES, ph = (used / W_STAGES) & 1;
+          const uint32_t s = used % L::W_STAGES, ph = (used / L::W_STAGES) & 1;
           if (!mbar_wait(smem_u32(&w_full[s]), ph, abort)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a0 = smem_u32(a_smem + ab * A_BYTES + kb * A_KB_BYTES);
@@ -277,9 +340,10 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
           for (int j = 0; j < BK / 16; ++j)
             umma(d, smem_desc(a0 + j * 32), smem_desc(b0 + j * 32), (kb | j) != 0);
           umma_commit(smem_u32(&w_empty[s]));  // frees the W stage once these MMAs finish
-          // refill the stage the previous block used (its MMAs are older, so
-          // the wait rarely blocks the next group's issue)
-          if (!issue_w(used + W_STAGES)) { ok = false; break; }
+          // request block used + 1: with two stages it refills the stage the
+          // previous block used (its MMAs are older, so the wait rarely
+          // blocks); with one stage it waits for these MMAs
+          if (!issue_w(used + 2)) { ok = false; break; }
         }
         if (!ok) break;
         umma_commit(smem_u32(&a_empty[ab]));  // the A tile may be rewritten once these MMAs finish
@@ -498,7 +562,37 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
     const int q = warp & 3;           // TMEM lane quadrant this warp may access
     constexpr int PARTS = L::EPI_WARPS / 4;  // column ranges per quadrant
     const int half = ew >> 2;                // this warp's column range
-    float* stage = e_smem + ew * EPI_WARP_FLOATS;
+    // Residual variants: the warp's residual rows arrive by cp.async in
+    // boxes of 32 rows x 32 columns (one box per 32-column chunk of its
+    // column range, the chunks of all its tiles in one sequence). A box is
+    // requested as soon as its ring slot is free, RING boxes ahead, so the
+    // next tile's boxes load during this tile's LayerNorm passes and MMA. A box row's eight 16-byte
+    // pieces sit at piece j ^ (row & 7): reading a row (thread = row, TMEM
+    // order) and reading a column across rows (lane = column, for coalesced
+    // global stores) are both conflict-free.
+    constexpr int CHUNKS = (BN / PARTS) / 32;
+    constexpr int RING = L::RING;
+    float* ring = e_smem + ew * (RING * BOX_FLOATS);
+    const int64_t n_boxes = L::RESID ? my_tiles * CHUNKS : 0;
+    auto issue_box = [&](int64_t k) {
+      if (k < n_boxes) {
+        const int64_t tile = blockIdx.x + (k / CHUNKS) * gridDim.x;
+        const int col = half * (BN / PARTS) + (int)(k % CHUNKS) * 32 + (lane & 7) * 4;
+        float* box = ring + (k % RING) * BOX_FLOATS;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = (lane >> 3) + 4 * i;
+          const int64_t row = tile * BM + q * 32 + r;
+          const bool live = row < p.m;
+          cp_async16_zfill(smem_u32(box + r * 32 + (((lane & 7) ^ (r & 7)) << 2)),
+                           p.res + (live ? row : 0) * p.ldr + col, live);
+        }
+      }
+      cp_async_commit();  // an empty group past the end keeps the wait count uniform
+    };
+    if constexpr (L::RESID) {
+      for (int64_t k = 0; k < RING; ++k) issue_box(k);
+    }
     for (int64_t t = 0; t < my_tiles && !*abort; ++t) {
       const int64_t tile = blockIdx.x + t * gridDim.x;
       const uint32_t tb = t & 1, tph = (t >> 1) & 1;
@@ -506,6 +600,129 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
       tc_fence_after();
       const int64_t row0 = tile * BM + q * 32;  // this warp's 32 rows
       const int64_t row = row0 + lane;
+      if constexpr (L::RESID) {
+        // Pass 1 (thread = row): x = residual + acc + bias per chunk; x goes
+        // back into the box, from which the warp stores whole 128-byte row
+        // segments (lane = column), and, for the LayerNorm variant, into this
+        // tile's TMEM columns, summed per row. The two column halves of a row
+        // meet in shared memory (a 64-thread named barrier per quadrant).
+        // Passes 2 (squared deviations) and 3 (normalised outputs, thread =
+        // row, a 64- or 128-byte run of its row per store) read TMEM only, so
+        // the LayerNorm costs no further global reads. The TMEM buffer is
+        // released after the last pass.
+        constexpr bool LN = EPI == EPI_RESID_LN;
+        const int cbeg = half * (BN / PARTS);
+        const int nr = (int)(p.m - row0 < 32 ? (p.m - row0 < 0 ? 0 : p.m - row0) : 32);  // live rows of the warp
+        const uint32_t tcol = tmem_base + ((uint32_t)(q * 32) << 16) + tb * BN;
+        float s1 = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < CHUNKS; ++c) {
+          const int64_t k = t * CHUNKS + c;
+          const int c0 = cbeg + c * 32;
+          float v[32];
+          tmem_ld32(tcol + c0, v);
+          cp_async_wait<RING - 1>();
+          __syncwarp();
+          float* box = ring + (k % RING) * BOX_FLOATS;
+          float4* br = reinterpret_cast<float4*>(box + lane * 32);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 b4 = reinterpret_cast<const float4*>(par + c0)[j];
+            float* e = v + 4 * j;
+            e[0] += b4.x; e[1] += b4.y; e[2] += b4.z; e[3] += b4.w;
+            if (p.relu) {
+              e[0] = fmaxf(e[0], 0.f); e[1] = fmaxf(e[1], 0.f); e[2] = fmaxf(e[2], 0.f); e[3] = fmaxf(e[3], 0.f);
+            }
+            float4 r4 = br[j ^ (lane & 7)];
+            r4.x += e[0]; r4.y += e[1]; r4.z += e[2]; r4.w += e[3];
+            e[0] = r4.x; e[1] = r4.y; e[2] = r4.z; e[3] = r4.w;
+            br[j ^ (lane & 7)] = r4;
+            if constexpr (LN) s1 += (r4.x + r4.y) + (r4.z + r4.w);
+          }
+          if constexpr (LN) tmem_st32(tcol + c0, v);
+          __syncwarp();
+          // lane = 16-byte piece: each store covers 4 whole 128-byte row segments
+          float* dst = p.res + row0 * p.ldr + c0 + (lane & 7) * 4;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int r = 4 * i + (lane >> 3);
+            const float4 x4 = reinterpret_cast<const float4*>(box)[r * 8 + ((lane & 7) ^ (r & 7))];
+            if (r < nr) *reinterpret_cast<float4*>(dst + r * p.ldr) = x4;
+          }
+          __syncwarp();
+          issue_box(k + RING);  // into the slot just finished
+        }
+        if constexpr (LN) {
+          float* red = reinterpret_cast<float*>(smem + L::RED_OFF) + q * 64;  // [half][32 rows]
+          uint8_t* outbox = smem + L::OUT_OFF + ew * OUT_BOX_BYTES;
+          tmem_st_wait();
+          red[half * 32 + lane] = s1;
+          asm volatile("bar.sync %0, 64;" ::"r"(1 + q) : "memory");
+          const float mean = (red[lane] + red[32 + lane]) * (1.f / BN);
+          asm volatile("bar.sync %0, 64;" ::"r"(1 + q) : "memory");  // both halves have read the sums
+          float s2 = 0.f;
+#pragma unroll 1
+          for (int c0 = cbeg; c0 < cbeg + BN / PARTS; c0 += 32) {
+            float v[32];
+            tmem_ld32(tcol + c0, v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float d = v[i] - mean;
+              s2 += d * d;
+            }
+          }
+          red[half * 32 + lane] = s2;
+          asm volatile("bar.sync %0, 64;" ::"r"(1 + q) : "memory");
+          const float rstd = rsqrtf((red[lane] + red[32 + lane]) * (1.f / BN) + p.ln_eps);
+          asm volatile("bar.sync %0, 64;" ::"r"(1 + q) : "memory");  // both halves have read the squares
+#pragma unroll 1
+          for (int c0 = cbeg; c0 < cbeg + BN / PARTS; c0 += 32) {
+            float v[32];
+            tmem_ld32(tcol + c0, v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = (v[i] - mean) * rstd;
+#pragma unroll
+            for (int o = 0; o < MAX_LN; ++o) {
+              if (o >= p.n_ln) break;
+              float y[32];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float4 g4 = reinterpret_cast<const float4*>(par + (1 + 2 * o) * BN + c0)[i];
+                const float4 b4 = reinterpret_cast<const float4*>(par + (2 + 2 * o) * BN + c0)[i];
+                y[4 * i] = v[4 * i] * g4.x + b4.x;
+                y[4 * i + 1] = v[4 * i + 1] * g4.y + b4.y;
+                y[4 * i + 2] = v[4 * i + 2] * g4.z + b4.z;
+                y[4 * i + 3] = v[4 * i + 3] * g4.w + b4.w;
+              }
+              // Through the warp's staging box (32 rows of 64 bytes, 16-byte
+              // piece j of row r at j ^ ((r >> 1) & 3); the row-wise writes and
+              // the piece-wise reads are both conflict-free), so that each
+              // store writes whole 64-byte row segments, 8 rows at a time.
+              __syncwarp();  // the previous output's reads of the box are done
+              uint4* sb = reinterpret_cast<uint4*>(outbox);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                uint4 w;
+                __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(y[8 * j + 2 * e], y[8 * j + 2 * e + 1]);
+                sb[lane * 4 + (j ^ ((lane >> 1) & 3))] = w;
+              }
+              __syncwarp();
+              __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.ln_out[o]) + row0 * p.ln_ld[o] + c0 + (lane & 3) * 8;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int r = 8 * i + (lane >> 2);
+                const uint4 w = sb[r * 4 + ((lane & 3) ^ ((r >> 1) & 3))];
+                if (r < nr) *reinterpret_cast<uint4*>(d + r * p.ln_ld[o]) = w;
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&t_empty[tb]));
+      } else {
 #pragma unroll 1
       for (int c0 = half * (BN / PARTS); c0 < (half + 1) * (BN / PARTS); c0 += 32) {
         float v[32];
@@ -537,25 +754,14 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
 #pragma unroll
             for (int i = 0; i < 4; ++i) store_vec<8>(o + 8 * i, v + 8 * i);
           }
-        } else {
-          // transpose through shared memory: lane = column afterwards
-#pragma unroll
-          for (int i = 0; i < 32; ++i) stage[lane * EPI_PITCH + i] = v[i];
-          __syncwarp();
-          float acc[32];
-#pragma unroll
-          for (int r = 0; r < 32; ++r)
-            acc[r] = (row0 + r < p.m) ? p.res[(row0 + r) * p.ldr + c0 + lane] : 0.f;
-#pragma unroll
-          for (int r = 0; r < 32; ++r)
-            if (row0 + r < p.m) p.res[(row0 + r) * p.ldr + c0 + lane] = acc[r] + stage[r * EPI_PITCH + lane];
-          __syncwarp();
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&t_empty[tb]));
+      }
     }
+    if constexpr (L::RESID) cp_async_wait<0>();  // no box load outlives the loop
   }
 
   tc_fence_before();
@@ -647,6 +853,55 @@ int mb_gemm_rows(const void* x, int x_dtype, int64_t ldx, int64_t m, const float
     else launch(rowgemm_kernel<PRO_COPY, EPI_RESIDUAL, false>, Plan<PRO_COPY, EPI_RESIDUAL, false>::SMEM);
   }
   return launch_status("gemm_rows");
+}
+
+int mb_gemm_rows_ln(const void* a, int64_t lda, int64_t m, const void* w_image, const float* bias, float* residual,
+                    int64_t ldr, float eps, const float* g0, const float* b0, void* o0, int o0_dtype, int64_t ld0,
+                    const float* g1, const float* b1, void* o1, int o1_dtype, int64_t ld1, const float* g2,
+                    const float* b2, void* o2, int o2_dtype, int64_t ld2, void* stream) {
+  using namespace sm100;
+  MB_REQUIRE(m >= 0, "gemm_rows_ln: negative m");
+  if (m == 0) return MB_OK;
+  MB_REQUIRE(a && w_image && residual, "gemm_rows_ln: null pointer");
+  MB_REQUIRE(aligned(a, 16) && (lda * 2) % 16 == 0 && lda >= KDIM, "gemm_rows_ln: a rows must be 16-byte aligned");
+  MB_REQUIRE(aligned(residual, 16) && ldr % 4 == 0 && ldr >= BN, "gemm_rows_ln: residual rows must be 16-byte aligned");
+  MB_REQUIRE(aligned(w_image, 16) && (!bias || aligned(bias, 16)), "gemm_rows_ln: misaligned weight image or bias");
+  Params prm{a, lda, nullptr, nullptr, 0.f, (const __nv_bfloat16*)w_image, bias, m, 0, nullptr, 0, residual, ldr,
+             nullptr};
+  const float* gs[MAX_LN] = {g0, g1, g2};
+  const float* bs[MAX_LN] = {b0, b1, b2};
+  void* os[MAX_LN] = {o0, o1, o2};
+  const int dts[MAX_LN] = {o0_dtype, o1_dtype, o2_dtype};
+  const int64_t lds[MAX_LN] = {ld0, ld1, ld2};
+  prm.n_ln = 0;
+  prm.ln_eps = eps;
+  for (int j = 0; j < MAX_LN; ++j) {
+    if (!os[j]) break;
+    MB_REQUIRE(gs[j] && bs[j], "gemm_rows_ln: LayerNorm output %d lacks gamma or beta", j);
+    MB_REQUIRE(dts[j] == MB_BF16, "gemm_rows_ln: LayerNorm output %d must be bf16", j);
+    MB_REQUIRE(aligned(os[j], 16) && (lds[j] * dtype_size(dts[j])) % 16 == 0 && lds[j] >= BN,
+               "gemm_rows_ln: LayerNorm output %d rows must be 16-byte aligned", j);
+    prm.ln_g[j] = gs[j];
+    prm.ln_b[j] = bs[j];
+    prm.ln_out[j] = os[j];
+    prm.ln_dtype[j] = dts[j];
+    prm.ln_ld[j] = lds[j];
+    prm.n_ln = j + 1;
+  }
+  for (int j = prm.n_ln; j < MAX_LN; ++j) MB_REQUIRE(!os[j], "gemm_rows_ln: outputs must be given in order");
+  if (g_num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_num_sms <= 0) g_num_sms = 148;
+  }
+  const int64_t tiles = cdiv(m, BM);
+  const int grid = (int)(tiles < g_num_sms ? tiles : g_num_sms);
+  auto kern = rowgemm_kernel<PRO_COPY, EPI_RESID_LN, false>;
+  const int smem_bytes = Plan<PRO_COPY, EPI_RESID_LN, false>::SMEM;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+  kern<<<grid, THREADS, smem_bytes, as_stream(stream)>>>(prm);
+  return launch_status("gemm_rows_ln");
 }
 
 int mb_hex_message_pass(const void* x, int64_t ldx, int64_t n, const int32_t* nbr, const void* w_image,

@@ -393,15 +393,17 @@ class _Tables:
 class Engine:
     """Prepared weights plus the forward schedule over the kernels."""
 
-    GEMM_MODES = ("tcgen05", "tcgen05-res", "cublas", "native")
+    GEMM_MODES = ("tcgen05", "tcgen05-res", "tcgen05-ln", "cublas", "native")
 
     def __init__(self, model: MantisNet, dtype: torch.dtype, gemm: str = "cublas"):
         """``gemm`` picks the dense-projection path: ``tcgen05`` (the fused
         LayerNorm-prologue and residual-epilogue row GEMMs of the library
         wherever the shape is 256 x 256, cuBLAS elsewhere), ``tcgen05-res``
-        (only the residual-epilogue fusion), ``cublas`` (separate LayerNorm /
-        cuBLAS / residual kernels) or ``native`` (the CUDA-core fp32 GEMM,
-        the fp32 parity mode)."""
+        (only the residual-epilogue fusion), ``tcgen05-ln`` (the projections
+        that feed a residual update emit the update and the next LayerNorms
+        from the GEMM epilogue; cuBLAS elsewhere), ``cublas`` (separate
+        LayerNorm / cuBLAS / residual kernels) or ``native`` (the CUDA-core
+        fp32 GEMM, the fp32 parity mode)."""
         if dtype not in (torch.float32, torch.bfloat16):
             raise ValueError("dtype must be torch.float32 or torch.bfloat16")
         if gemm == "torch":
@@ -580,6 +582,22 @@ class Engine:
             return out
         return self.linear(a, lin, relu=relu)
 
+    def linear_update(self, a: Tensor, lin: _Lin, x: Tensor, lns) -> list[Tensor]:
+        """x += a @ W^T + b, then the LayerNorms ``lns`` of the updated rows
+        (as ``update``): one tcgen05 launch in ``tcgen05-ln`` mode."""
+        if (self.gemm == "tcgen05-ln" and lin.imgs is not None and lin.n == ops.GEMM_N and 1 <= len(lns) <= 3
+                and a.dtype == torch.bfloat16 and a.stride(1) == 1 and x.dtype == torch.float32 and x.stride(1) == 1
+                and self.cd == torch.bfloat16
+                and all(not isinstance(e, tuple) or e[1] is None or e[1].dtype == torch.bfloat16 for e in lns)):
+            outs = []
+            for e in lns:
+                p, o = e if isinstance(e, tuple) else (e, None)
+                if o is None:
+                    o = torch.empty(x.shape[0], x.shape[1], dtype=self.cd, device=x.device)
+                outs.append((p.g, p.b, o))
+            return ops.gemm_rows_ln(a, lin.imgs[0], lin.b, x, outs)
+        return self.update(x, self.linear(a, lin), lns)
+
     def linear_residual(self, a: Tensor, lin: _Lin, x: Tensor) -> None:
         """x += a @ W^T + b with the residual add in the GEMM epilogue."""
         if self._fused(lin) and lin.n == ops.GEMM_N and a.dtype == torch.bfloat16 and x.dtype == torch.float32:
@@ -694,12 +712,15 @@ class Engine:
         x = self.ln_linear(s, blk["ln_ws_s"], blk["u"])
         ops.run_reduce(x, b.inc_stone, T.window_ptr, T.N_w, add=self.ws_table[:, i * h:(i + 1) * h],
                        add_idx=b.window_feat, out=buf_w[:, h:])
-        y = self.linear(self.linear(buf_w, blk["mlp_w"][0], relu=True), blk["mlp_w"][1])
+        hid_w = self.linear(buf_w, blk["mlp_w"][0], relu=True)
         # §5.1b
         if cfg.uses_cell_state:
-            zw_cr, zw_wr = self.update(w, y, [blk["ln_cr_w"], blk["ln_wr_w"]])
-            y, c, zc, cells = self._cell_stage(blk, nxt, s, c, T, zc, zw_cr, zw_wr)
+            zw_cr, zw_wr = self.linear_update(hid_w, blk["mlp_w"][1], w, [blk["ln_cr_w"], blk["ln_wr_w"]])
+            back, c, zc, cells = self._cell_stage(blk, nxt, s, c, T, zc, zw_cr, zw_wr)
+            zw_sw, zw_read, zw_bq = self.linear_update(back, blk["wr_wo"], w,
+                                                       [blk["ln_sw_w"], blk["ln_read_w"], blk["ln_bcast_q"]])
         else:
+            y = self.linear(hid_w, blk["mlp_w"][1])
             buf2 = torch.empty(T.N_w, 2 * h, dtype=cd, device=w.device)
             zin, _ = self.update(w, y, [blk["ln_cp_in"], (blk["ln_cp_w"], buf2[:, :h])])
             xr = self.linear(zin, blk["u_cp"])
@@ -707,7 +728,7 @@ class Engine:
                                             b.relay_win_ptr, b.relay_wcell, b.relay_cls_ptr, b.relay_ccell))
             y = self.linear(self.linear(buf2, blk["mlp_cp"][0], relu=True), blk["mlp_cp"][1])
             cells = None
-        zw_sw, zw_read, zw_bq = self.update(w, y, [blk["ln_sw_w"], blk["ln_read_w"], blk["ln_bcast_q"]])
+            zw_sw, zw_read, zw_bq = self.update(w, y, [blk["ln_sw_w"], blk["ln_read_w"], blk["ln_bcast_q"]])
         # §5.2 stones <- windows (fp32 sum) + class rows
         yv = self.linear(zw_sw, blk["v"])
         sw = sw_all[:, i * h:(i + 1) * h]
@@ -735,14 +756,13 @@ class Engine:
         kv = self.ln_linear(g, blk["ln_bcast_l"], blk["kv_bcast"])
         q = self.linear(zw_bq, blk["wq_bcast"])
         bc = ops.latent_broadcast(q, kv[:, :h], kv[:, h:], cfg.heads, T.window_pos, T.P, out_dtype=cd)
-        y = self.linear(bc, blk["wo_bcast"])
         w_out = None
         if nxt is not None:
             buf_w = torch.empty(T.N_w, 2 * h, dtype=cd, device=w.device)
-            self.update(w, y, [(nxt["ln_ws_w"], buf_w[:, :h])])
+            self.linear_update(bc, blk["wo_bcast"], w, [(nxt["ln_ws_w"], buf_w[:, :h])])
         else:
             w_out = self._exit_w
-            self.update(w, y, [(self.ln_out, w_out)])
+            self.linear_update(bc, blk["wo_bcast"], w, [(self.ln_out, w_out)])
         # FFN (row-wise; the stone half is skipped in the last block)
         for x_ in ((s, g) if update_stones else (g,)):
             hid = self.ln_linear(x_, blk["ln_ffn"], blk["ffn0"], relu=True)
@@ -750,9 +770,10 @@ class Engine:
         return s, w, g, c, buf_w, zc, w_out, cells
 
     def _cell_stage(self, blk, nxt, s, c, T: _Tables, zc_cr, zw_cr, zw_wr):
-        """model.py:397-490. Returns the window update of the read-back (not
-        yet applied), the updated cells, the next block's LN_cr_c(c) and, after
-        the last block, ln_out(c) (fp32)."""
+        """model.py:397-490. Returns the window read-back rows (before their
+        output projection, which the caller fuses with the window update),
+        the updated cells, the next block's LN_cr_c(c) and, after the last
+        block, ln_out(c)."""
         cfg, cd, h = self.cfg, self.cd, self.h
         zstate = self.ln(c, blk["ln_c"]) if cfg.cell_structure else None
         q = self.linear(zc_cr, blk["cr_wq"])
@@ -760,10 +781,16 @@ class Engine:
         with self.timed("cell_read"):
             read = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["cr_bias"], blk["cr_vclass"], T.cell_ptr,
                                          T.dec_window, T.dec_class, out_dtype=cd)
-        reads = self.linear(read, blk["cr_wo"])
         simple = not (cfg.cell_structure or cfg.cell_adjacency)
+        exit_ln = (nxt["ln_cr_c"], None) if nxt is not None else (self.ln_out, self._exit_c)
+        reads = None
+        if cfg.cell_nodes and not cfg.cell_structure:
+            (zc_rad,) = self.linear_update(read, blk["cr_wo"], c, [blk["ln_radius_c"]])
+        else:
+            reads = self.linear(read, blk["cr_wo"])
         if cfg.cell_nodes:
-            (zc_rad,) = self.update(c, reads, [blk["ln_radius_c"]])
+            if reads is not None:
+                (zc_rad,) = self.update(c, reads, [blk["ln_radius_c"]])
             q = self.linear(zc_rad, blk["radius_wq"])
             kv = self.ln_linear(s, blk["ln_radius_s"], blk["radius_kv"])
             with self.timed("radius_read"):
@@ -775,15 +802,17 @@ class Engine:
                 else:
                     read = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["radius_bias"], blk["radius_vclass"],
                                                  T.r_ptr, T.r_src, T.r_cls, skip_ptr=T.skip, out_dtype=cd)
-            y = self.linear(read, blk["radius_wo"])
-            if cfg.cell_structure:
-                reads = (reads.float() + y.float()).to(cd)
+            if simple:
+                zc_wr, zc_out = self.linear_update(read, blk["radius_wo"], c, [blk["ln_wr_c"], exit_ln])
+            else:
+                y = self.linear(read, blk["radius_wo"])
+                if cfg.cell_structure:
+                    reads = (reads.float() + y.float()).to(cd)
         else:
             y = reads
-        exit_ln = (nxt["ln_cr_c"], None) if nxt is not None else (self.ln_out, self._exit_c)
-        if simple:
+        if simple and not cfg.cell_nodes:
             zc_wr, zc_out = self.update(c, y, [blk["ln_wr_c"], exit_ln])
-        else:
+        elif not simple:
             self.update(c, y, [])
             if cfg.cell_structure:
                 mlp = blk["mlp_c"]
@@ -800,10 +829,9 @@ class Engine:
         kv = self.linear(zc_wr, blk["wr_kv"])
         back = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["wr_bias"], None, T.win_ptr, T.edge_wcell,
                                      T.edge_wclass, out_dtype=cd)
-        y_w = self.linear(back, blk["wr_wo"])
         if nxt is not None:
-            return y_w, c, zc_out, None
-        return y_w, c, None, zc_out
+            return back, c, zc_out, None
+        return back, c, None, zc_out
 
     # ---------------------------------------------------------------- heads
     def heads(self, w: Tensor, g: Tensor, cells, b: Batch):

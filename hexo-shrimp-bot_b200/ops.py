@@ -688,6 +688,29 @@ def gemm_rows(x, w_img, bias=None, gamma=None, beta=None, relu=False, out=None, 
     return out if out is not None else residual
 
 
+def gemm_rows_ln(a, w_img, bias, residual, outs, eps=1e-5):
+    """residual += a @ W^T + bias (fp32 rows, in place), then one LayerNorm of
+    each updated row per ``outs`` entry ``(gamma, beta, out)`` (out bf16, unit
+    column stride, up to three), in one tcgen05 launch."""
+    _rowmajor(a, "a")
+    if a.dtype != torch.bfloat16 or a.shape[1] != GEMM_K:
+        raise ValueError(f"gemm_rows_ln takes bf16 rows of width {GEMM_K}")
+    if residual.dtype != torch.float32 or residual.shape != (a.shape[0], GEMM_N) or residual.stride(1) != 1:
+        raise ValueError("residual must be (m, 256) fp32 rows")
+    if len(outs) > 3:
+        raise ValueError("at most three LayerNorm outputs")
+    args = []
+    for g, b, o in outs:
+        if o.shape != residual.shape or o.stride(1) != 1 or o.dtype != torch.bfloat16:
+            raise ValueError("LayerNorm outputs must be bf16 and match the residual's shape with unit column stride")
+        args += [ptr(g), ptr(b), ptr(o), dtype_code(o.dtype), o.stride(0)]
+    args += [None, None, None, 0, 0] * (3 - len(outs))
+    bb = bias.float().contiguous() if bias is not None else None
+    call("mb_gemm_rows_ln", ptr(a), a.stride(0), a.shape[0], ptr(w_img), ptr(bb), ptr(residual), residual.stride(0),
+         float(eps), *args, stream_of(a.device))
+    return [o for _, _, o in outs]
+
+
 # ------------------------------------------------- isolated-op workloads
 def hex_message_pass(x, nbr, w_img, bias=None, out=None):
     """out = x + W mean(x[present neighbours]) + bias, fused on the tensor

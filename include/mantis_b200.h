@@ -265,6 +265,20 @@ int mb_gemm_rows(const void* x, int x_dtype, int64_t ldx, int64_t m, const float
                  const void* w_image, const float* bias, int relu, void* out, int64_t ldo, float* residual,
                  int64_t ldr, void* stream);
 
+/* Fused projection + residual update + LayerNorms on the tensor cores:
+ *   x[r] += a[r] W^T + bias;  out_j[r] = LN_j(x[r])  for each given output j,
+ * a (m, 256) bf16 rows, x = residual (m, 256) fp32 rows updated in place,
+ * w_image from mb_gemm_weight_image; up to three LayerNorm outputs (gamma,
+ * beta, destination, dtype, leading dim; fill in order, NULL to stop; dtype
+ * must be MB_BF16), each from the same updated row with two-pass fp32
+ * statistics. One pass over the
+ * residual row replaces the reference's Linear, residual add and following
+ * LayerNorm calls (model.py:397-490 cell stage, :543-692 window updates). */
+int mb_gemm_rows_ln(const void* a, int64_t lda, int64_t m, const void* w_image, const float* bias, float* residual,
+                    int64_t ldr, float eps, const float* g0, const float* b0, void* o0, int o0_dtype, int64_t ld0,
+                    const float* g1, const float* b1, void* o1, int o1_dtype, int64_t ld1, const float* g2,
+                    const float* b2, void* o2, int o2_dtype, int64_t ld2, void* stream);
+
 /* ------------------------------------------------- isolated-op workloads --
  * The two isolated ops of the benchmark suite. Neither exists as an op in the
  * reference; each restates its workload definition, and the CPU restatements

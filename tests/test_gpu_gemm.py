@@ -64,3 +64,43 @@ def test_strided_output_and_no_bias():
     want = F.layer_norm(x, (256,)).to(torch.bfloat16).float() @ w.to(torch.bfloat16).float().t()
     _close(buf[:, 256:], want)
     assert torch.count_nonzero(buf[:, :256]) == 0
+
+
+@pytest.mark.parametrize("m", [1, 129, 1000, 40000])
+@pytest.mark.parametrize("n_ln", [1, 2, 3])
+def test_residual_layernorm_epilogue(m, n_ln):
+    """x += a W^T + b and up to three LayerNorms of the updated rows (bf16
+    destinations, one of them a column view) from one launch."""
+    g = torch.Generator(device="cpu").manual_seed(m + n_ln)
+    a = torch.randn(m, 256, generator=g).to(torch.bfloat16).to(DEV)
+    w = (torch.randn(256, 256, generator=g) / 16).to(DEV).to(torch.bfloat16)
+    b = torch.randn(256, generator=g).to(DEV)
+    x = (torch.randn(m, 256, generator=g) * 3 + 1).to(DEV)
+    want_x = x + a.float() @ w.float().t() + b
+    lns, outs = [], []
+    wide = torch.empty(m, 512, dtype=torch.bfloat16, device=DEV)
+    for j in range(n_ln):
+        gam = torch.randn(256, generator=g).to(DEV)
+        bet = torch.randn(256, generator=g).to(DEV)
+        o = wide[:, 256:] if j == 0 else torch.empty(m, 256, dtype=torch.bfloat16, device=DEV)
+        lns.append((gam, bet, o))
+    ops.gemm_rows_ln(a, ops.weight_image(w), b, x, lns)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(x, want_x, rtol=1e-4, atol=1e-3)
+    for gam, bet, o in lns:
+        want = F.layer_norm(want_x, (256,), gam, bet)
+        tol = 2e-2
+        torch.testing.assert_close(o.float(), want, rtol=tol, atol=tol * max(1.0, want.abs().max().item()) / 4)
+    mb._lib.check_device_error()
+
+
+@pytest.mark.gpu
+def test_residual_layernorm_rejects_fp32_outputs():
+    """The fused epilogue stages bf16 row segments only: an fp32 LayerNorm
+    destination is refused before launch (the caller takes the unfused path)."""
+    a = torch.zeros(64, 256, dtype=torch.bfloat16, device=DEV)
+    x = torch.zeros(64, 256, device=DEV)
+    w = ops.weight_image(torch.zeros(256, 256, device=DEV))
+    one, zero = torch.ones(256, device=DEV), torch.zeros(256, device=DEV)
+    with pytest.raises(ValueError):
+        ops.gemm_rows_ln(a, w, None, x, [(one, zero, torch.empty(64, 256, device=DEV))])

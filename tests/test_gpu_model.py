@@ -95,8 +95,9 @@ def test_evaluator_contract_and_batched_equals_single():
         off += g.n_legal
 
 
+@pytest.mark.parametrize("gemm", ["cublas", "tcgen05-ln"])
 @pytest.mark.parametrize("blocks", [2, 8])
-def test_bf16_contract_at_bench_architecture(blocks):
+def test_bf16_contract_at_bench_architecture(blocks, gemm):
     """north_star bf16 contract: h=256, 8 heads, F=4, cell_latents +
     cell_nodes, random init at std 0.02 (decoder outputs included, so the
     logits have a realistic scale) on engine positions of 40-150 stones:
@@ -116,7 +117,13 @@ def test_bf16_contract_at_bench_architecture(blocks):
     P = {k: v.detach().clone() for k, v in net.state_dict().items()}
     ref = O.forward(O.Cfg(**{k: v for k, v in cfg.to_dict().items() if k != "dropout"}), P, batch, 0.2)
     net = net.to(DEV).eval()
-    out = net(batch.to(DEV), 0.2)
+    eng = net.engine(torch.bfloat16, gemm=gemm)
+    bd = batch.to(DEV)
+    w, gg, cells = eng.trunk(bd)
+    value, _, _ = eng.value_head(w, gg, bd)
+    policy, critic = eng.heads(w, gg, cells, bd)
+    q_score, q_values = mb.ops.compose(critic, bd.legal_offsets, 0.2)
+    out = mb.model.ModelOutput(policy.float(), q_score, q_values, value, None, None)
     assert (out.policy_logits.cpu() - ref["policy_logits"]).abs().max() <= 2e-2
     assert (out.q_values.cpu() - ref["q_values"]).abs().max() <= 1e-2
     assert (out.value.cpu() - ref["value"]).abs().max() <= 1e-2
