@@ -463,6 +463,27 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
         const int64_t tile = blockIdx.x + t * gridDim.x;
         const uint32_t ab = t % L::A_BUFS, aph = (t / L::A_BUFS) & 1;
         uint8_t* abuf = a_smem + ab * A_BYTES;
+        if constexpr (PRO == PRO_COPY) {
+          // bf16 rows need no arithmetic: each lane cp.asyncs its 16-byte
+          // chunk of every row of the warp straight into the swizzled slot
+          // (zero-filled past m), so the whole tile is in flight at once with
+          // no register cost; the warp then waits for its own copies and
+          // fences them for the tensor core's (async-proxy) reads.
+          if (!mbar_wait(smem_u32(&a_empty[ab]), aph ^ 1, abort)) break;
+          const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(p.x);
+          for (int r = pw; r < BM; r += L::PRODUCERS) {
+            const int64_t row = tile * BM + r;
+            const bool live = row < p.m;
+            cp_async16_zfill(smem_u32(abuf + kb * A_KB_BYTES + r * 128 + ((chunk ^ (r & 7)) << 4)),
+                             xb + (live ? row : 0) * p.ldx + lane * 8, live);
+          }
+          cp_async_commit();
+          cp_async_wait<0>();
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&a_full[ab]));
+          continue;
+        }
         bool ok = true;
         constexpr int NRB = PRO == PRO_HEXMEAN ? 3 : RB;  // rows in flight (6 gathers each for HEXMEAN)
         // HEXMEAN: lanes 0-5 hold the six neighbour slots of each row of a
