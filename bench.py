@@ -451,7 +451,7 @@ def main():
     ap.add_argument("--cpu-sample", type=int, default=4)
     ap.add_argument("--ref-sample", type=int, default=4)
     ap.add_argument("--latency", type=int, default=1)
-    ap.add_argument("--gemm", default="cublas", help="dense projection path (see model.Engine)")
+    ap.add_argument("--gemm", default="tcgen05-ln", help="dense projection path (see model.Engine)")
     ap.add_argument("--op", default=None, choices=["hex", "axial"],
                     help="time one isolated-op workload instead of the evaluator (config 3 / config 2)")
     args = ap.parse_args()

@@ -11,33 +11,38 @@
 //             RESIDUAL - x_res[row] += result (fp32, in place)
 //             ADD_X    - out[row] = x[row] + result (bf16), the fused
 //                        message-passing update y = x + W mean(x[nbr]) + b
+//             RESID_LN - RESIDUAL, then up to three LayerNorms of each
+//                        updated row (bf16 outputs), from the same launch
 //
 // K = 256 (one model width), N = 256 output columns per launch, M any.
-// The op is HBM-bound (about 1.5-2.5 KB of row traffic per 131 kFLOP), so the
+// The op is HBM-bound (about 1.5-4 KB of row traffic per 131 kFLOP), so the
 // design is about keeping row bytes in flight and accesses coalesced.
 //
 // Persistent, warp-specialised CTA (one per SM, 16 warps = 4 per SM
 // sub-partition, so every thread may hold 128 registers):
 //   warp 0      lane 0 streams pre-swizzled 64-wide K-blocks of W (32 KB,
-//               L2-resident) through a 2-stage ring with cp.async.bulk and
-//               issues the tcgen05.mma stream (M=128, N=256, K=16, bf16 x bf16
-//               -> fp32) into a double-buffered TMEM accumulator, signalling
-//               with tcgen05.commit.
-//   warps 1-7   A producers, two variants:
+//               L2-resident) through a 1- or 2-stage ring with cp.async.bulk
+//               and issues the tcgen05.mma stream (M=128, N=256, K=16, bf16 x
+//               bf16 -> fp32) into a double-buffered TMEM accumulator,
+//               signalling with tcgen05.commit.
+//   warps 1-7   A producers (11 for the neighbour gather), three variants:
 //               staged (LayerNorm of contiguous fp32 rows): lane 1 of warp 0
-//                 bulk-copies 32-row groups (32 KB) into a 3-deep ring, so 96 KB
-//                 per SM are in flight with no register cost; warps 1-7
-//                 normalise rows out of shared memory into the A tile;
-//               direct (bf16 rows, or strided fp32 rows): warps 1-7 load rows
-//                 with 16-byte vector loads, 8 rows in flight per warp.
-//               Both write bf16 into the 128-byte-swizzled K-major layout the
+//                 bulk-copies 32-row groups (32 KB) into a 3-deep ring; warps
+//                 1-7 normalise rows out of shared memory into the A tile;
+//               copy (bf16 rows): every lane cp.asyncs its 16-byte chunk of
+//                 each of its warp's rows straight into the swizzled slot, so
+//                 the whole 64 KB tile is in flight at once;
+//               direct (strided fp32 rows, neighbour means): 16-byte vector
+//                 loads, several rows in flight per warp.
+//               The A tile is bf16 in the 128-byte-swizzled K-major layout the
 //               UMMA descriptor reads.
 //   warps 8-15  epilogue: two warps per TMEM lane quadrant, one per 128-column
 //               half; tcgen05.ld 32 columns at a time (thread = row). A bf16
-//               result is stored directly; a residual update goes through a
-//               padded shared-memory transpose so each warp reads, adds and
-//               writes whole 128-byte row segments (coalesced), 32 rows in
-//               flight.
+//               result is stored directly. The residual variants stream the
+//               residual rows through a per-warp cp.async ring of 32 x 32
+//               boxes and write back whole row segments; the LayerNorm variant
+//               keeps the updated rows in TMEM for its statistics and output
+//               passes (see the epilogue).
 //
 // Every mbarrier wait is bounded by a clock deadline; on expiry the CTA
 // records a device error, stops issuing work, and still frees its TMEM.

@@ -153,7 +153,7 @@ class EvaluatorConfig:
     device: str = "cuda"
     autocast: bool = True
     mass_floor: float = 0.2
-    gemm: str = "cublas"
+    gemm: str = "tcgen05-ln"
     # Batches of at least 2 * part_positions positions are evaluated as runs
     # of about part_positions positions whose host-to-device copies overlap
     # the previous run's compute; 0 turns this off.
@@ -163,7 +163,7 @@ class EvaluatorConfig:
 def network_evaluate(model, cfg):
     """The self-play evaluator: CPU fp32 (policy, q_score, q_values)."""
     dtype = torch.bfloat16 if getattr(cfg, "autocast", True) else torch.float32
-    gemm = getattr(cfg, "gemm", "cublas")
+    gemm = getattr(cfg, "gemm", "tcgen05-ln")
     fields = needed_fields(model.cfg)
     device = torch.device(cfg.device)
     if device.type != "cuda":

@@ -246,7 +246,7 @@ class MantisNet(nn.Module):
                 nn.init.zeros_(block.mlp_c.out.bias)
 
     # --------------------------------------------------------------- engine
-    def engine(self, dtype: torch.dtype = torch.bfloat16, gemm: str = "cublas") -> "Engine":
+    def engine(self, dtype: torch.dtype = torch.bfloat16, gemm: str = "tcgen05-ln") -> "Engine":
         """The prepared-weight runner for the module's device and ``dtype``;
         rebuilt when any parameter changes (in-place updates bump versions)."""
         if self.training and self.cfg.dropout > 0:
@@ -395,13 +395,14 @@ class Engine:
 
     GEMM_MODES = ("tcgen05", "tcgen05-res", "tcgen05-ln", "cublas", "native")
 
-    def __init__(self, model: MantisNet, dtype: torch.dtype, gemm: str = "cublas"):
+    def __init__(self, model: MantisNet, dtype: torch.dtype, gemm: str = "tcgen05-ln"):
         """``gemm`` picks the dense-projection path: ``tcgen05`` (the fused
         LayerNorm-prologue and residual-epilogue row GEMMs of the library
         wherever the shape is 256 x 256, cuBLAS elsewhere), ``tcgen05-res``
         (only the residual-epilogue fusion), ``tcgen05-ln`` (the projections
         that feed a residual update emit the update and the next LayerNorms
-        from the GEMM epilogue; cuBLAS elsewhere), ``cublas`` (separate
+        from the GEMM epilogue; cuBLAS elsewhere; the default, and in fp32
+        the same as ``cublas``), ``cublas`` (separate
         LayerNorm / cuBLAS / residual kernels) or ``native`` (the CUDA-core
         fp32 GEMM, the fp32 parity mode)."""
         if dtype not in (torch.float32, torch.bfloat16):
