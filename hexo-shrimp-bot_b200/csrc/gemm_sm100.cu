@@ -710,28 +710,26 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
 #pragma unroll
             for (int o = 0; o < MAX_LN; ++o) {
               if (o >= p.n_ln) break;
-              float y[32];
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float4 g4 = reinterpret_cast<const float4*>(par + (1 + 2 * o) * BN + c0)[i];
-                const float4 b4 = reinterpret_cast<const float4*>(par + (2 + 2 * o) * BN + c0)[i];
-                y[4 * i] = v[4 * i] * g4.x + b4.x;
-                y[4 * i + 1] = v[4 * i + 1] * g4.y + b4.y;
-                y[4 * i + 2] = v[4 * i + 2] * g4.z + b4.z;
-                y[4 * i + 3] = v[4 * i + 3] * g4.w + b4.w;
-              }
               // Through the warp's staging box (32 rows of 64 bytes, 16-byte
               // piece j of row r at j ^ ((r >> 1) & 3); the row-wise writes and
               // the piece-wise reads are both conflict-free), so that each
               // store writes whole 64-byte row segments, 8 rows at a time.
+              // Each 8-column piece is scaled, shifted and packed on its own,
+              // so no second 32-value row is held in registers.
               __syncwarp();  // the previous output's reads of the box are done
               uint4* sb = reinterpret_cast<uint4*>(outbox);
+              const float4* g4 = reinterpret_cast<const float4*>(par + (1 + 2 * o) * BN + c0);
+              const float4* b4 = reinterpret_cast<const float4*>(par + (2 + 2 * o) * BN + c0);
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
+                const float4 ga = g4[2 * j], gb = g4[2 * j + 1], ba = b4[2 * j], bb = b4[2 * j + 1];
+                const float* x = v + 8 * j;
                 uint4 w;
                 __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&w);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(y[8 * j + 2 * e], y[8 * j + 2 * e + 1]);
+                h[0] = __floats2bfloat162_rn(x[0] * ga.x + ba.x, x[1] * ga.y + ba.y);
+                h[1] = __floats2bfloat162_rn(x[2] * ga.z + ba.z, x[3] * ga.w + ba.w);
+                h[2] = __floats2bfloat162_rn(x[4] * gb.x + bb.x, x[5] * gb.y + bb.y);
+                h[3] = __floats2bfloat162_rn(x[6] * gb.z + bb.z, x[7] * gb.w + bb.w);
                 sb[lane * 4 + (j ^ ((lane >> 1) & 3))] = w;
               }
               __syncwarp();
