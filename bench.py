@@ -275,9 +275,14 @@ def run_ours(args, rank, world, local_rank):
     h2d = batch_bytes(host, fields) * n_chunks
     d2h = 3 * host.n_cells * 4 * n_chunks
 
-    # Roofline of the dominant native kernel, the radius read, from its
-    # launches inside the timed region.
-    roof = radius_roofline(probe, tables, cfg) if rank == 0 else None
+    # Roofline of the dominant native kernel (the larger total time inside the
+    # timed region): the fused projection launches or the radius read.
+    roof = None
+    if rank == 0:
+        radius = radius_roofline(probe, tables, cfg)
+        if radius is not None:
+            radius["total_ms"] = radius["launch_ms"] * radius["launches_timed"]
+        roof = dominant_roofline([resid_ln_roofline(probe), radius])
 
     # p50 batch-64 latency (config-4 distribution: 40-150 stones), end to end
     p50 = None
@@ -366,6 +371,45 @@ def radius_roofline(probe, T, cfg):
             "cell_read_launch_ms": statistics.mean(cell_ms) if cell_ms else None}
 
 
+# DRAM bytes (read + write) over algorithmic bytes of the fused projection +
+# residual + LayerNorm launch, from the ncu capture of
+# `bench.py --op resid_ln --rows 262144` (2 outputs): 886.1 MB over 939.5 MB.
+# Below 1 because part of the last writes is still in L2 when the kernel ends.
+RESID_LN_TRAFFIC_RATIO = 886.1 / 939.5
+
+
+def resid_ln_roofline(probe):
+    """The fused projection + residual + LayerNorm launches inside the timed
+    region: algorithmic bytes over CUDA-event time, per launch on average."""
+    ev = probe.get("resid_ln", [])
+    byt = probe.get("resid_ln_bytes", [])
+    if not ev or len(ev) != len(byt):
+        return None
+    ms = [s.elapsed_time(e) for s, e in ev]
+    sec = statistics.mean(ms) / 1000.0
+    algo = statistics.mean(byt)
+    pk, kind = peaks()
+    achieved = algo / sec / 1e9
+    return {"kernel": "rowgemm_kernel<COPY, RESID_LN> (projection + residual + LayerNorms, tcgen05)", "bound": "hbm",
+            "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+            "traffic": algo * RESID_LN_TRAFFIC_RATIO,
+            "traffic_source": "ncu capture of bench.py --op resid_ln --rows 262144, DRAM/algorithmic ratio",
+            "peak_kind": kind, "algorithmic_bytes": algo, "launch_ms": sec * 1000.0, "launches_timed": len(ms),
+            "total_ms": sum(ms)}
+
+
+def dominant_roofline(cands):
+    """The candidate with the largest total time in the timed region, with the
+    runner-up under ``next`` (None when there is no candidate)."""
+    cands = sorted((r for r in cands if r is not None), key=lambda r: -r["total_ms"])
+    if not cands:
+        return None
+    roof = dict(cands[0])
+    if len(cands) > 1:
+        roof["next"] = cands[1]
+    return roof
+
+
 def _time_launches(fn, steps, warmup):
     """Mean CUDA-event time of ``fn`` over ``steps`` launches after ``warmup``."""
     import torch
@@ -396,7 +440,24 @@ def run_op(args):
     pk, kind = peaks()
     g = torch.Generator(device=dev).manual_seed(0)
     p = args.positions
-    if args.op == "hex":
+    if args.op == "resid_ln":
+        # x += a W^T + b, then LayerNorms of x: the trunk's residual updates
+        m, n_out = args.rows, args.ln_outputs
+        a = torch.randn(m, 256, device=dev, generator=g).to(torch.bfloat16)
+        img = ops.weight_image(torch.randn(256, 256, device=dev, generator=g) * 0.05)
+        b = torch.randn(256, device=dev, generator=g) * 0.1
+        x = torch.randn(m, 256, device=dev, generator=g)
+        outs = [(torch.randn(256, device=dev, generator=g) * 0.1 + 1, torch.randn(256, device=dev, generator=g) * 0.1,
+                 torch.empty(m, 256, dtype=torch.bfloat16, device=dev)) for _ in range(n_out)]
+        ms = _time_launches(lambda: ops.gemm_rows_ln(a, img, b, x, outs), args.steps, args.warmup)
+        algo = m * (512 + 2048 + 512 * n_out)
+        line = {"metric": "fused projection + residual + LayerNorm rows/s", "value": m / (ms / 1000.0),
+                "unit": "rows/s", "ms_per_step": ms,
+                "config": {"workload": f"{m} rows x 256, bf16 input, fp32 residual, {n_out} bf16 LayerNorm outputs"},
+                "roofline": {"kernel": "rowgemm_kernel<COPY, RESID_LN>", "bound": "hbm", "achieved": algo / ms / 1e6,
+                             "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": algo / ms / 1e6 / pk["hbm_gbs"],
+                             "peak_kind": kind, "algorithmic_bytes": algo}}
+    elif args.op == "hex":
         nbr, _ = mb.hexgraph.message_graph(p, 256, 40, 200, seed=1)
         n = nbr.shape[0]
         x = torch.randn(n, 256, device=dev, generator=g).to(torch.bfloat16)
@@ -452,8 +513,11 @@ def main():
     ap.add_argument("--ref-sample", type=int, default=4)
     ap.add_argument("--latency", type=int, default=1)
     ap.add_argument("--gemm", default="tcgen05-ln", help="dense projection path (see model.Engine)")
-    ap.add_argument("--op", default=None, choices=["hex", "axial"],
-                    help="time one isolated-op workload instead of the evaluator (config 3 / config 2)")
+    ap.add_argument("--op", default=None, choices=["hex", "axial", "resid_ln"],
+                    help="time one isolated-op workload instead of the evaluator (config 3 / config 2 / the "
+                         "fused projection + residual + LayerNorm launch)")
+    ap.add_argument("--rows", type=int, default=1814720, help="rows of --op resid_ln (default: one chunk's windows)")
+    ap.add_argument("--ln-outputs", type=int, default=2, help="LayerNorm outputs of --op resid_ln (1-3)")
     args = ap.parse_args()
     if args.op:
         run_op(args)

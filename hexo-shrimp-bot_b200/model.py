@@ -596,7 +596,10 @@ class Engine:
                 if o is None:
                     o = torch.empty(x.shape[0], x.shape[1], dtype=self.cd, device=x.device)
                 outs.append((p.g, p.b, o))
-            return ops.gemm_rows_ln(a, lin.imgs[0], lin.b, x, outs)
+            if self.probe is not None:  # algorithmic bytes of the launch: a, residual in + out, outputs
+                self.probe.setdefault("resid_ln_bytes", []).append(x.shape[0] * (512 + 2048 + 512 * len(outs)))
+            with self.timed("resid_ln"):
+                return ops.gemm_rows_ln(a, lin.imgs[0], lin.b, x, outs)
         return self.update(x, self.linear(a, lin), lns)
 
     def linear_residual(self, a: Tensor, lin: _Lin, x: Tensor) -> None:
