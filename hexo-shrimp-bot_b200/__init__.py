@@ -17,7 +17,7 @@ __all__ = [
 ]
 
 
-_SUBMODULES = ("_lib", "ops", "model", "evaluator", "vocab", "engine", "builder", "config", "build", "sharding",
+_SUBMODULES = ("_lib", "ops", "model", "evaluator", "vocab", "engine", "builder", "encoder", "config", "build", "sharding",
                "hexgraph")
 
 

@@ -56,6 +56,11 @@ SIGNATURES = {
     "mb_linear": "pilllpiplipilp",
     "mb_gemm_weight_image": "pllpp",
     "mb_gemm_rows": "pillppfppiplplp",
+    "mb_encode_positions": "lpppppppip",
+    "mb_encoding_sizes": "pp",
+    "mb_encoding_fill": "ppi",
+    "mb_encoding_free": "p",
+    "mb_encoder_table": "ipl",
 }
 _CT = {"p": ctypes.c_void_p, "i": ctypes.c_int, "l": ctypes.c_int64, "f": ctypes.c_float}
 

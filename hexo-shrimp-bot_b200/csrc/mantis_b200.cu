@@ -8,3 +8,4 @@
 #include "gemm_sm100.cu"
 #include "attention_sm100.cu"
 #include "noalloc.cu"
+#include "encoder.cu"

@@ -311,6 +311,90 @@ int mb_axial_attention(const void* q, const void* k, const void* v, int64_t n_po
                        const int32_t* valid, const float* bias, void* out, int64_t o_pos, int64_t o_head,
                        int64_t o_row, void* stream);
 
+/* --------------------------------------------------------------- encoder --
+ * Host-side batch builder: game positions to the collated batch arrays that
+ * the evaluator reads. HOST pointers, no stream, no GPU needed. Replaces the
+ * reference's batch builder: the Python build / collate / batch_from_arrays
+ * (python/mantisnet/mantisnet/builder.py:486-956 with the relay views of
+ * relay.py:48-94) and the production Rust encoder
+ * (crates/models/mantisnet/src/encoder.rs:1047-1660). Every array equals the
+ * Python builder's, order included.
+ *
+ * Usage: mb_encode_positions builds every position's graph (threads: 0 = one
+ * per hardware thread) and returns a handle; mb_encoding_sizes reports the
+ * batch sizes; the caller allocates one buffer per field (host memory,
+ * pinned or not) and mb_encoding_fill writes them; mb_encoding_free releases
+ * the handle. A position the builder refuses (no legal moves, moves_remaining
+ * not 1 or 2, duplicate stones, a legal cell occupied or beyond distance 8
+ * of every stone) fails the whole call with MB_INVALID_ARGUMENT and a message
+ * naming the position.
+ *
+ * Inputs: positions i in [0, n_pos) own stones [stone_off[i], stone_off[i+1])
+ * of stone_qr (axial q, r pairs) and stone_owner, the player to move
+ * mover[i], legal cells [legal_off[i], legal_off[i+1]) of legal_qr, and
+ * moves_remaining[i] (1 or 2). */
+typedef struct mb_encoding mb_encoding;
+
+/* sizes[]: */
+enum {
+  MB_ENC_P = 0, MB_ENC_NS, MB_ENC_NW, MB_ENC_NINC, MB_ENC_NC, MB_ENC_NRADIUS, MB_ENC_NADJ, MB_ENC_NDEC,
+  MB_ENC_MAX_T, MB_ENC_MAX_W, MB_ENC_NCOVERED, MB_ENC_NSIZES
+};
+/* fields[], each a host buffer: shape in sizes[] terms, dtype i64 unless
+ * noted (u8 = one byte per flag, 0 or 1). */
+enum {
+  MB_ENC_STONE_OWN = 0,  /* (NS) */
+  MB_ENC_WINDOW_FEAT,    /* (NW) */
+  MB_ENC_WINDOW_ID,      /* (NW, 3): axis, start q, start r */
+  MB_ENC_MOVES_IDX,      /* (P) */
+  MB_ENC_INC_STONE,      /* (NINC) */
+  MB_ENC_INC_WINDOW,     /* (NINC) */
+  MB_ENC_INC_CLASS,      /* (NINC) */
+  MB_ENC_STONE_SLOT,     /* (NS) */
+  MB_ENC_COORDS,         /* (P, MAX_T, 2) i32 */
+  MB_ENC_ATTN_VALID,     /* (P, MAX_T) u8 */
+  MB_ENC_WINDOW_SLOT,    /* (NW) */
+  MB_ENC_VALUE_VALID,    /* (P, MAX_W) u8 */
+  MB_ENC_LEGAL_OFFSETS,  /* (P + 1) */
+  MB_ENC_CELL_POS,       /* (NC) */
+  MB_ENC_CELL_NEAREST,   /* (NC) */
+  MB_ENC_RADIUS_SRC,     /* (NRADIUS) */
+  MB_ENC_RADIUS_DST,
+  MB_ENC_RADIUS_ORBIT,
+  MB_ENC_RADIUS_OWN,
+  MB_ENC_RADIUS_ON_AXIS,
+  MB_ENC_ADJ_SRC,        /* (NADJ) */
+  MB_ENC_ADJ_DST,
+  MB_ENC_ADJ_AXIS,
+  MB_ENC_DEC_CELL,       /* (NDEC) */
+  MB_ENC_DEC_WINDOW,
+  MB_ENC_DEC_CLASS,
+  MB_ENC_RELAY_CELL_PTR, /* (NCOVERED + 1) */
+  MB_ENC_RELAY_WINDOW,   /* (NDEC) */
+  MB_ENC_RELAY_CLASS,    /* (NDEC) */
+  MB_ENC_RELAY_WIN_PTR,  /* (NW + 1) */
+  MB_ENC_RELAY_WCELL,    /* (NDEC) */
+  MB_ENC_RELAY_CLS_PTR,  /* (727) */
+  MB_ENC_RELAY_CCELL,    /* (NDEC) */
+  MB_ENC_ACT_CLASS,      /* (NDEC) */
+  MB_ENC_ACT_REV,        /* (NDEC) */
+  MB_ENC_ACT_EMPTY,      /* (NC, 3) */
+  MB_ENC_ACT_TACTICAL,   /* (NC, 11) f32 */
+  MB_ENC_NFIELDS
+};
+int mb_encode_positions(int64_t n_pos, const int64_t* stone_off, const int64_t* stone_qr, const int64_t* stone_owner,
+                        const int64_t* mover, const int64_t* legal_off, const int64_t* legal_qr,
+                        const int64_t* moves_remaining, int threads, mb_encoding** out);
+int mb_encoding_sizes(const mb_encoding* encoding, int64_t* sizes);
+int mb_encoding_fill(const mb_encoding* encoding, void* const* fields, int threads);
+int mb_encoding_free(mb_encoding* encoding);
+/* The encoder's vocabulary tables (0 window-pattern rank [729], 1 occupied-
+ * slot class [729 x 6], 2 decoder class [729 x 6], 3 post-placement class
+ * [729 x 6], 4 displacement orbit [25 x 25]; -1 where undefined), for
+ * checking them against another derivation. Follows the reference
+ * definitions at builder.py:41-229. */
+int mb_encoder_table(int which, int64_t* out, int64_t capacity);
+
 #ifdef __cplusplus
 }
 #endif
