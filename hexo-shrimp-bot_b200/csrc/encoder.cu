@@ -23,10 +23,11 @@
 // Work: phase 1 builds each position's graph on its own (a thread per slice
 // of positions); phase 2 writes the batch into caller-owned buffers, each
 // position's rows at its offsets, then the batch-wide relay sorts (counting
-// sorts, stable). Coordinate lookups go through open-addressing hash tables
-// keyed by the packed coordinate, so a position costs O(cells) whatever its
-// extent.
+// sorts, stable). Coordinate lookups read dense grids over the position's
+// bounding box (hash tables keyed by the packed coordinate when the box is
+// huge), so a position costs O(cells).
 #include <algorithm>
+#include <cstdint>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -183,18 +184,56 @@ class KeyMap {
   size_t mask_;
 };
 
+// Cell coordinate -> index. A dense grid over the position's bounding box
+// (plus a margin covering every offset the builder looks at) when that box is
+// modest, else the hash table above; lookups outside the box miss.
+class CellIndex {
+ public:
+  CellIndex(int64_t q0, int64_t r0, int64_t nq, int64_t nr, bool dense, size_t n)
+      : q0_(q0), r0_(r0), nq_(nq), nr_(nr), dense_(dense), map_(dense ? 0 : n) {
+    if (dense_) grid_.assign((size_t)(nq * nr), -1);
+  }
+  void insert(int64_t q, int64_t r, int64_t v) {
+    if (!dense_) { map_.insert(pack(q, r), v); return; }
+    const int64_t dq = q - q0_, dr = r - r0_;
+    if ((uint64_t)dq >= (uint64_t)nq_ || (uint64_t)dr >= (uint64_t)nr_) return;
+    int32_t& g = grid_[(size_t)(dq * nr_ + dr)];
+    if (g < 0) g = (int32_t)v;
+  }
+  int64_t find(int64_t q, int64_t r) const {
+    if (!dense_) return map_.find(pack(q, r));
+    const int64_t dq = q - q0_, dr = r - r0_;
+    if ((uint64_t)dq >= (uint64_t)nq_ || (uint64_t)dr >= (uint64_t)nr_) return -1;
+    return grid_[(size_t)(dq * nr_ + dr)];
+  }
+
+ private:
+  int64_t q0_, r0_, nq_, nr_;
+  bool dense_;
+  KeyMap map_;
+  std::vector<int32_t> grid_;
+};
+
 // ------------------------------------------------------------- one position
+// One position's rows in compact per-position form (local indices); the
+// batch arrays are int64 and offset, written in phase 2.
+struct RadiusEdge { int32_t src, dst; uint8_t orbit, own, on_axis; };
+struct AdjEdge { int32_t src, dst; uint8_t axis; };
+struct IncRow { int32_t stone, window; int16_t cls; };
+struct DecRow { int32_t cell, window; int16_t cls, post1; };
 struct Graph {
   int64_t n_s = 0, n_w = 0, n_l = 0, moves = 1;
-  std::vector<int64_t> stone_qr, stone_own;
-  std::vector<int64_t> window_feat, window_id;             // window_id: (axis, q, r) per window
-  std::vector<int64_t> inc_stone, inc_window, inc_class;
-  std::vector<int64_t> nearest;
-  std::vector<int64_t> r_src, r_dst, r_orbit, r_own, r_axis;
-  std::vector<int64_t> a_src, a_dst, a_axis;
-  std::vector<int64_t> dec_cell, dec_window, dec_class;
-  std::vector<int64_t> act_class, act_empty;               // act_empty: 3 per cell
-  std::vector<float> tactical;                             // 11 per cell
+  std::vector<int32_t> stone_qr;                            // as the int32 coords field stores them
+  std::vector<uint8_t> stone_own;
+  std::vector<int16_t> window_feat;
+  std::vector<int64_t> window_id;                           // (axis, q, r) per window
+  std::vector<IncRow> inc;
+  std::vector<uint8_t> nearest;
+  std::vector<RadiusEdge> radius;
+  std::vector<AdjEdge> adj;
+  std::vector<DecRow> dec;
+  std::vector<uint8_t> act_empty;                           // 3 per cell
+  std::vector<float> tactical;                              // 11 per cell
 };
 
 struct PosIn {
@@ -217,89 +256,99 @@ std::string build_one(const PosIn& in, Graph& g) {
   g.n_s = n_s;
   g.n_l = n_l;
   g.moves = in.moves;
-  g.stone_qr.assign(in.stone_qr, in.stone_qr + 2 * n_s);
+  g.stone_qr.resize(2 * n_s);
+  for (int64_t i = 0; i < 2 * n_s; ++i) g.stone_qr[i] = (int32_t)in.stone_qr[i];
   g.stone_own.resize(n_s);
   for (int64_t i = 0; i < n_s; ++i) g.stone_own[i] = in.owner[i] != in.mover;
 
-  // legal cells: packed key -> legal row (the first row holding that key)
-  KeyMap legal(n_l);
-  for (int64_t c = 0; c < n_l; ++c) legal.insert(pack(in.legal_qr[2 * c], in.legal_qr[2 * c + 1]), c);
+  // Bounding box of stones and legal cells, widened by the farthest offset
+  // any lookup uses (distance 8 from a stone, 5 along a line, 1 to a
+  // neighbour); a dense grid serves it when it holds at most 4M cells.
+  int64_t qlo = INT64_MAX, qhi = INT64_MIN, rlo = INT64_MAX, rhi = INT64_MIN;
+  auto widen = [&](const int64_t* qr, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) {
+      qlo = std::min(qlo, qr[2 * i]); qhi = std::max(qhi, qr[2 * i]);
+      rlo = std::min(rlo, qr[2 * i + 1]); rhi = std::max(rhi, qr[2 * i + 1]);
+    }
+  };
+  widen(in.stone_qr, n_s);
+  widen(in.legal_qr, n_l);
+  constexpr int64_t MARGIN = LEGAL_RADIUS + 1;
+  const bool bounded = qhi - qlo < (int64_t(1) << 20) && rhi - rlo < (int64_t(1) << 20) &&
+                       qlo > -(int64_t(1) << 40) && rlo > -(int64_t(1) << 40) && qhi < (int64_t(1) << 40) &&
+                       rhi < (int64_t(1) << 40);
+  const int64_t nq = bounded ? qhi - qlo + 1 + 2 * MARGIN : 0, nr = bounded ? rhi - rlo + 1 + 2 * MARGIN : 0;
+  const bool dense = bounded && nq * nr <= (int64_t(1) << 22);
+  auto index = [&](size_t n) { return CellIndex(qlo - MARGIN, rlo - MARGIN, nq, nr, dense, n); };
+
+  // legal cells: coordinate -> legal row (the first row holding that cell)
+  CellIndex legal = index(n_l);
+  for (int64_t c = 0; c < n_l; ++c) legal.insert(in.legal_qr[2 * c], in.legal_qr[2 * c + 1], c);
 
   // ---- radius edges and nearest-stone distance (reference builder.py:427-460)
   const int nd = (int)T.disk_q.size();
   g.nearest.assign(n_l, n_s ? LEGAL_RADIUS + 1 : NEAREST_UNREACHED);
   if (n_s) {
-    std::vector<int64_t> cnt(n_l + 1, 0);
-    std::vector<int64_t> hit_c, hit_s;
-    std::vector<int> hit_d;
-    hit_c.reserve(n_s * 64); hit_s.reserve(n_s * 64); hit_d.reserve(n_s * 64);
+    std::vector<int32_t> cnt(n_l + 1, 0);
+    struct Hit { int32_t c, s, d; };
+    std::vector<Hit> hits;
+    hits.reserve(n_s * 96);
     for (int64_t s = 0; s < n_s; ++s) {
       const int64_t q = in.stone_qr[2 * s], r = in.stone_qr[2 * s + 1];
       for (int d = 0; d < nd; ++d) {
-        const int64_t c = legal.find(pack(q + T.disk_q[d], r + T.disk_r[d]));
+        const int64_t c = legal.find(q + T.disk_q[d], r + T.disk_r[d]);
         if (c < 0) continue;
-        hit_c.push_back(c); hit_s.push_back(s); hit_d.push_back(d);
+        hits.push_back({(int32_t)c, (int32_t)s, d});
         ++cnt[c + 1];
-        g.nearest[c] = std::min<int64_t>(g.nearest[c], T.disk_dist[d]);
+        g.nearest[c] = std::min<uint8_t>(g.nearest[c], (uint8_t)T.disk_dist[d]);
       }
     }
     bool bad = false;
     for (int64_t c = 0; c < n_l && !bad; ++c) bad = g.nearest[c] > LEGAL_RADIUS;
     if (!bad) {
-      KeyMap stones(n_s);
-      for (int64_t s = 0; s < n_s; ++s) stones.insert(pack(in.stone_qr[2 * s], in.stone_qr[2 * s + 1]), s);
-      for (int64_t c = 0; c < n_l && !bad; ++c) bad = stones.find(pack(in.legal_qr[2 * c], in.legal_qr[2 * c + 1])) >= 0;
+      CellIndex stones = index(n_s);
+      for (int64_t s = 0; s < n_s; ++s) stones.insert(in.stone_qr[2 * s], in.stone_qr[2 * s + 1], s);
+      for (int64_t c = 0; c < n_l && !bad; ++c) bad = stones.find(in.legal_qr[2 * c], in.legal_qr[2 * c + 1]) >= 0;
     }
     if (bad) return "legal cells must be empty and within radius 8 of a stone";
     // stable counting sort by destination: sources stay ascending within a cell
     for (int64_t c = 0; c < n_l; ++c) cnt[c + 1] += cnt[c];
-    const size_t ne = hit_c.size();
-    g.r_src.resize(ne); g.r_dst.resize(ne); g.r_orbit.resize(ne); g.r_own.resize(ne); g.r_axis.resize(ne);
-    std::vector<int64_t> at(cnt.begin(), cnt.end() - 1);
-    for (size_t e = 0; e < ne; ++e) {
-      const int64_t i = at[hit_c[e]]++;
-      g.r_src[i] = hit_s[e];
-      g.r_dst[i] = hit_c[e];
-      g.r_orbit[i] = T.disk_orbit[hit_d[e]];
-      g.r_own[i] = g.stone_own[hit_s[e]];
-      g.r_axis[i] = T.disk_on_axis[hit_d[e]];
-    }
+    g.radius.resize(hits.size());
+    for (const Hit& h : hits)
+      g.radius[cnt[h.c]++] = {h.s, h.c, (uint8_t)T.disk_orbit[h.d], g.stone_own[h.s], (uint8_t)T.disk_on_axis[h.d]};
   }
 
   // ---- directed distance-one neighbours among legal cells (builder.py:462-483)
   {
     static const int steps[6][2] = {{-1, 0}, {0, -1}, {-1, 1}, {1, 0}, {0, 1}, {1, -1}};
-    std::vector<int64_t> cnt(n_l + 1, 0), hs, hd, ha;
+    std::vector<int32_t> cnt(n_l + 1, 0);
+    std::vector<AdjEdge> hits;
+    hits.reserve(6 * n_l);
     for (int64_t c = 0; c < n_l; ++c) {
       const int64_t q = in.legal_qr[2 * c], r = in.legal_qr[2 * c + 1];
       for (int j = 0; j < 6; ++j) {
-        const int64_t dst = legal.find(pack(q + steps[j][0], r + steps[j][1]));
+        const int64_t dst = legal.find(q + steps[j][0], r + steps[j][1]);
         if (dst < 0) continue;
-        hs.push_back(c); hd.push_back(dst); ha.push_back(j % 3);
+        hits.push_back({(int32_t)c, (int32_t)dst, (uint8_t)(j % 3)});
         ++cnt[dst + 1];
       }
     }
     for (int64_t c = 0; c < n_l; ++c) cnt[c + 1] += cnt[c];
-    g.a_src.resize(hs.size()); g.a_dst.resize(hs.size()); g.a_axis.resize(hs.size());
-    std::vector<int64_t> at(cnt.begin(), cnt.end() - 1);
-    for (size_t e = 0; e < hs.size(); ++e) {
-      const int64_t i = at[hd[e]]++;
-      g.a_src[i] = hs[e]; g.a_dst[i] = hd[e]; g.a_axis[i] = ha[e];
-    }
+    g.adj.resize(hits.size());
+    for (const AdjEdge& h : hits) g.adj[cnt[h.dst]++] = h;
   }
 
   // ---- stones: duplicates refused (builder.py:567-570)
-  KeyMap stones(n_s);
+  CellIndex stones = index(n_s);
   {
     std::vector<int64_t> keys(n_s);
     for (int64_t s = 0; s < n_s; ++s) keys[s] = pack(in.stone_qr[2 * s], in.stone_qr[2 * s + 1]);
-    std::vector<int64_t> sorted = keys;
-    std::sort(sorted.begin(), sorted.end());
-    if (std::adjacent_find(sorted.begin(), sorted.end()) != sorted.end()) return "duplicate stone coordinates";
-    for (int64_t s = 0; s < n_s; ++s) stones.insert(keys[s], s);
+    std::sort(keys.begin(), keys.end());
+    if (std::adjacent_find(keys.begin(), keys.end()) != keys.end()) return "duplicate stone coordinates";
+    for (int64_t s = 0; s < n_s; ++s) stones.insert(in.stone_qr[2 * s], in.stone_qr[2 * s + 1], s);
   }
   auto digit_at = [&](int64_t q, int64_t r) -> int {  // 0 empty, 1 own (mover's), 2 opponent's
-    const int64_t s = stones.find(pack(q, r));
+    const int64_t s = stones.find(q, r);
     return s < 0 ? 0 : 1 + (int)g.stone_own[s];
   };
 
@@ -318,44 +367,44 @@ std::string build_one(const PosIn& in, Graph& g) {
              cand.end());
   const int64_t n_w = (int64_t)cand.size();
   g.n_w = n_w;
-  KeyMap live(n_w);
+  CellIndex live[3] = {index(n_w), index(n_w), index(n_w)};  // window start -> window, per axis
   std::vector<int> pattern(n_w);
   g.window_feat.resize(n_w);
   g.window_id.resize(3 * n_w);
   for (int64_t w = 0; w < n_w; ++w) {
     const Cand& c = cand[w];
-    live.insert(c.key, w);
+    live[c.a].insert(c.q, c.r, w);
     int pat = 0;
     for (int j = 0; j < W; ++j) {
       const int64_t q = c.q + AX[c.a][0] * j, r = c.r + AX[c.a][1] * j;
-      const int64_t s = stones.find(pack(q, r));
+      const int64_t s = stones.find(q, r);
       if (s < 0) continue;
       pat += (1 + (int)g.stone_own[s]) * T.pow3[j];
-      g.inc_stone.push_back(s);
-      g.inc_window.push_back(w);
-      g.inc_class.push_back(j);  // slot for now; class once the pattern is known
+      g.inc.push_back({(int32_t)s, (int32_t)w, (int16_t)j});  // slot for now; class once the pattern is known
     }
     pattern[w] = pat;
-    g.window_feat[w] = T.rank[pat];
+    g.window_feat[w] = (int16_t)T.rank[pat];
     g.window_id[3 * w] = c.a;
     g.window_id[3 * w + 1] = c.q;
     g.window_id[3 * w + 2] = c.r;
   }
-  for (size_t e = 0; e < g.inc_class.size(); ++e) {
-    const int cls = T.occ[pattern[g.inc_window[e]]][g.inc_class[e]];
+  for (IncRow& e : g.inc) {
+    const int cls = T.occ[pattern[e.window]][e.cls];
     if (cls < 0) return "incidence entry pairs a window with a slot it does not occupy";
-    g.inc_class[e] = cls;
+    e.cls = (int16_t)cls;
   }
 
   // ---- decoder rows and action rows (builder.py:587-600, 292-424)
   g.act_empty.assign(3 * n_l, 0);
   g.tactical.assign(TACTICAL * n_l, 0.f);
-  std::vector<int64_t> win_index(n_l * 3 * W);
-  std::vector<int> own_c(n_l * 3 * W), opp_c(n_l * 3 * W);
+  g.dec.reserve(18 * n_l / 4 + 16);
+  std::vector<uint8_t> five_hit(n_l, 0);
   std::vector<char> five_mark(n_w, 0), four_mark(n_w, 0);
   int64_t five_remaining = 0, four_remaining = 0;
+  const float rows_total = (float)(3 * W);
   for (int64_t c = 0; c < n_l; ++c) {
     const int64_t q0 = in.legal_qr[2 * c], r0 = in.legal_qr[2 * c + 1];
+    int any_win = 0, max_own = 0, max_opp = 0, make5 = 0, make4 = 0, hit5 = 0, four_rows = 0, kept_rows = 0;
     for (int a = 0; a < 3; ++a) {
       int line[2 * W - 1];
       for (int o = 0; o < 2 * W - 1; ++o)
@@ -369,47 +418,36 @@ std::string build_one(const PosIn& in, Graph& g) {
           own += d == 1;
           opp += d == 2;
         }
-        const int64_t w = live.find(pack(q0 - AX[a][0] * k, r0 - AX[a][1] * k) * 4 + a);
-        const int idx = (int)(c * 3 * W + a * W + k);
-        win_index[idx] = w;
-        own_c[idx] = own;
-        opp_c[idx] = opp;
         const int post1 = T.post1[pre + T.pow3[k]][k];
         if (post1 < 0) return "a post-placement row lost its own stone";
         const bool kept = own > 0 || opp > 0;
+        // only a row holding a stone can name a live window
+        const int64_t w = kept ? live[a].find(q0 - AX[a][0] * k, r0 - AX[a][1] * k) : -1;
         if ((w >= 0) != kept) return "the kept-window set disagrees with the action-row walk";
+        max_own = std::max(max_own, own);
+        max_opp = std::max(max_opp, opp);
+        if (opp == 0 && own == W - 1) any_win = 1;
+        if (opp == 0 && own + 1 == 5) ++make5;
+        if (opp == 0 && own + 1 == 4) ++make4;
         if (kept) {
           const int cls = T.dec[pattern[w]][k];
           if (cls < 0) return "decoder entry pairs a window with a slot it already occupies";
-          g.dec_cell.push_back(c);
-          g.dec_window.push_back(w);
-          g.dec_class.push_back(cls);
-          g.act_class.push_back(post1);
+          g.dec.push_back({(int32_t)c, (int32_t)w, (int16_t)cls, (int16_t)post1});
+          ++kept_rows;
           if (opp > 0 && own == 0) {
-            if (opp == 5 && !five_mark[w]) { five_mark[w] = 1; ++five_remaining; }
-            if (opp == 4 && !four_mark[w]) { four_mark[w] = 1; ++four_remaining; }
+            if (opp == 5) {
+              ++hit5;
+              if (!five_mark[w]) { five_mark[w] = 1; ++five_remaining; }
+            }
+            if (opp == 4) {
+              ++four_rows;
+              if (!four_mark[w]) { four_mark[w] = 1; ++four_remaining; }
+            }
           }
         } else {
           ++g.act_empty[3 * c + T.slot_orbit[k]];
         }
       }
-    }
-  }
-  const float rows_total = (float)(3 * W);
-  const float five_f = (float)std::min<int64_t>(five_remaining, THREAT_CAP) / (float)THREAT_CAP;
-  const float four_f = (float)std::min<int64_t>(four_remaining, THREAT_CAP) / (float)THREAT_CAP;
-  for (int64_t c = 0; c < n_l; ++c) {
-    int any_win = 0, max_own = 0, max_opp = 0, make5 = 0, make4 = 0, five_hit = 0, four_rows = 0, kept = 0;
-    for (int i = 0; i < 3 * W; ++i) {
-      const int own = own_c[c * 3 * W + i], opp = opp_c[c * 3 * W + i];
-      max_own = std::max(max_own, own);
-      max_opp = std::max(max_opp, opp);
-      if (opp == 0 && own == W - 1) any_win = 1;
-      if (opp == 0 && own + 1 == 5) ++make5;
-      if (opp == 0 && own + 1 == 4) ++make4;
-      if (opp > 0 && own == 0 && opp == 5) ++five_hit;
-      if (opp > 0 && own == 0 && opp == 4) ++four_rows;
-      kept += own > 0 || opp > 0;
     }
     float* t = &g.tactical[TACTICAL * c];
     t[0] = (float)any_win;
@@ -417,12 +455,19 @@ std::string build_one(const PosIn& in, Graph& g) {
     t[2] = (float)max_opp / (float)W;
     t[3] = (float)make5 / rows_total;
     t[4] = (float)make4 / rows_total;
-    t[5] = (float)five_hit / rows_total;
+    t[5] = (float)hit5 / rows_total;
     t[6] = (float)four_rows / rows_total;
+    t[10] = (float)kept_rows / rows_total;
+    five_hit[c] = (uint8_t)hit5;
+  }
+  // the position-wide threat counts, known once every cell is walked
+  const float five_f = (float)std::min<int64_t>(five_remaining, THREAT_CAP) / (float)THREAT_CAP;
+  const float four_f = (float)std::min<int64_t>(four_remaining, THREAT_CAP) / (float)THREAT_CAP;
+  for (int64_t c = 0; c < n_l; ++c) {
+    float* t = &g.tactical[TACTICAL * c];
     t[7] = five_f;
     t[8] = four_f;
-    t[9] = (float)(five_remaining > 0 && five_hit == five_remaining);
-    t[10] = (float)kept / rows_total;
+    t[9] = (float)(five_remaining > 0 && five_hit[c] == five_remaining);
   }
   return std::string();
 }
@@ -454,6 +499,7 @@ struct mb_encoding {
   // per-position offsets (n_pos + 1 each): stones, windows, incidences,
   // cells, radius edges, adjacency edges, decoder rows
   std::vector<int64_t> off[7];
+  std::vector<int64_t> cov_off;  // covered (decoder-row) cells per position
   int64_t max_t = 0, max_w = 0, n_covered = 0;
 };
 
@@ -489,17 +535,21 @@ int mb_encode_positions(int64_t n_pos, const int64_t* stone_off, const int64_t* 
       return mb::fail(MB_INVALID_ARGUMENT, "position %lld: %s", (long long)i, err[i].c_str());
     }
   for (auto& o : e->off) o.assign(n_pos + 1, 0);
+  e->cov_off.assign(n_pos + 1, 0);
   int64_t max_s = 0, max_w = 0;
   for (int64_t i = 0; i < n_pos; ++i) {
     const Graph& g = e->graphs[i];
-    const int64_t n[7] = {g.n_s, g.n_w, (int64_t)g.inc_stone.size(), g.n_l, (int64_t)g.r_src.size(),
-                          (int64_t)g.a_src.size(), (int64_t)g.dec_cell.size()};
+    const int64_t n[7] = {g.n_s, g.n_w, (int64_t)g.inc.size(), g.n_l, (int64_t)g.radius.size(),
+                          (int64_t)g.adj.size(), (int64_t)g.dec.size()};
     for (int f = 0; f < 7; ++f) e->off[f][i + 1] = e->off[f][i] + n[f];
     max_s = std::max(max_s, g.n_s);
     max_w = std::max(max_w, g.n_w);
     // decoder rows are cell-major, so distinct cells are counted in one pass
-    for (size_t r = 0; r < g.dec_cell.size(); ++r) e->n_covered += r == 0 || g.dec_cell[r] != g.dec_cell[r - 1];
+    int64_t cov = 0;
+    for (size_t r = 0; r < g.dec.size(); ++r) cov += r == 0 || g.dec[r].cell != g.dec[r - 1].cell;
+    e->cov_off[i + 1] = e->cov_off[i] + cov;
   }
+  e->n_covered = e->cov_off[n_pos];
   e->max_t = max_s + GLOBAL_ROWS;
   e->max_w = max_w + 1;
   *out = e;
@@ -529,6 +579,7 @@ int mb_encoding_fill(const mb_encoding* e, void* const* fields, int threads) {
   const auto& dof = e->off[6];
   const int64_t max_t = e->max_t, max_w = e->max_w;
   auto L = [&](int f) { return static_cast<int64_t*>(fields[f]); };
+  std::vector<int32_t> cls_hist((size_t)P * DEC_CLASSES, 0);
   parallel_for(P, threads, [&](int64_t i) {
     const Graph& g = e->graphs[i];
     const int64_t s0 = so[i], w0 = wo[i], i0 = io[i], c0 = co[i], r0 = ro[i], a0 = ao[i], d0 = dof[i];
@@ -542,10 +593,10 @@ int mb_encoding_fill(const mb_encoding* e, void* const* fields, int threads) {
       L(MB_ENC_WINDOW_SLOT)[w0 + w] = i * max_w + 1 + w;
     }
     L(MB_ENC_MOVES_IDX)[i] = g.moves - 1;
-    for (size_t x = 0; x < g.inc_stone.size(); ++x) {
-      L(MB_ENC_INC_STONE)[i0 + x] = g.inc_stone[x] + s0;
-      L(MB_ENC_INC_WINDOW)[i0 + x] = g.inc_window[x] + w0;
-      L(MB_ENC_INC_CLASS)[i0 + x] = g.inc_class[x];
+    for (size_t x = 0; x < g.inc.size(); ++x) {
+      L(MB_ENC_INC_STONE)[i0 + x] = g.inc[x].stone + s0;
+      L(MB_ENC_INC_WINDOW)[i0 + x] = g.inc[x].window + w0;
+      L(MB_ENC_INC_CLASS)[i0 + x] = g.inc[x].cls;
     }
     int32_t* coords = static_cast<int32_t*>(fields[MB_ENC_COORDS]) + i * max_t * 2;
     uint8_t* attn = static_cast<uint8_t*>(fields[MB_ENC_ATTN_VALID]) + i * max_t;
@@ -567,58 +618,82 @@ int mb_encoding_fill(const mb_encoding* e, void* const* fields, int threads) {
       std::memcpy(static_cast<float*>(fields[MB_ENC_ACT_TACTICAL]) + TACTICAL * (c0 + c), &g.tactical[TACTICAL * c],
                   TACTICAL * sizeof(float));
     }
-    for (size_t x = 0; x < g.r_src.size(); ++x) {
-      L(MB_ENC_RADIUS_SRC)[r0 + x] = g.r_src[x] + s0;
-      L(MB_ENC_RADIUS_DST)[r0 + x] = g.r_dst[x] + c0;
-      L(MB_ENC_RADIUS_ORBIT)[r0 + x] = g.r_orbit[x];
-      L(MB_ENC_RADIUS_OWN)[r0 + x] = g.r_own[x];
-      L(MB_ENC_RADIUS_ON_AXIS)[r0 + x] = g.r_axis[x];
+    for (size_t x = 0; x < g.radius.size(); ++x) {
+      const RadiusEdge& r = g.radius[x];
+      L(MB_ENC_RADIUS_SRC)[r0 + x] = r.src + s0;
+      L(MB_ENC_RADIUS_DST)[r0 + x] = r.dst + c0;
+      L(MB_ENC_RADIUS_ORBIT)[r0 + x] = r.orbit;
+      L(MB_ENC_RADIUS_OWN)[r0 + x] = r.own;
+      L(MB_ENC_RADIUS_ON_AXIS)[r0 + x] = r.on_axis;
     }
-    for (size_t x = 0; x < g.a_src.size(); ++x) {
-      L(MB_ENC_ADJ_SRC)[a0 + x] = g.a_src[x] + c0;
-      L(MB_ENC_ADJ_DST)[a0 + x] = g.a_dst[x] + c0;
-      L(MB_ENC_ADJ_AXIS)[a0 + x] = g.a_axis[x];
+    for (size_t x = 0; x < g.adj.size(); ++x) {
+      L(MB_ENC_ADJ_SRC)[a0 + x] = g.adj[x].src + c0;
+      L(MB_ENC_ADJ_DST)[a0 + x] = g.adj[x].dst + c0;
+      L(MB_ENC_ADJ_AXIS)[a0 + x] = g.adj[x].axis;
     }
-    for (size_t x = 0; x < g.dec_cell.size(); ++x) {
-      L(MB_ENC_DEC_CELL)[d0 + x] = g.dec_cell[x] + c0;
-      L(MB_ENC_DEC_WINDOW)[d0 + x] = g.dec_window[x] + w0;
-      L(MB_ENC_DEC_CLASS)[d0 + x] = g.dec_class[x];
-      L(MB_ENC_ACT_CLASS)[d0 + x] = g.act_class[x];
+    for (size_t x = 0; x < g.dec.size(); ++x) {
+      const DecRow& d = g.dec[x];
+      L(MB_ENC_DEC_CELL)[d0 + x] = d.cell + c0;
+      L(MB_ENC_DEC_WINDOW)[d0 + x] = d.window + w0;
+      L(MB_ENC_DEC_CLASS)[d0 + x] = d.cls;
+      L(MB_ENC_ACT_CLASS)[d0 + x] = d.post1;
+      L(MB_ENC_RELAY_WINDOW)[d0 + x] = d.window + w0;
+      L(MB_ENC_RELAY_CLASS)[d0 + x] = d.cls;
     }
+    // Relay views of this position's rows (reference relay.py:48-94): rows
+    // are cell-major already, so cell runs are read off directly; the window
+    // view is a counting sort within the position, because a position's
+    // windows and rows both form one contiguous block. Class counts feed the
+    // batch-wide class view below.
+    const int64_t k0 = e->cov_off[i];
+    int64_t* cell_ptr = L(MB_ENC_RELAY_CELL_PTR);
+    const size_t nd = g.dec.size();
+    std::vector<int64_t> ecell(nd);
+    int64_t k = k0 - 1;
+    for (size_t x = 0; x < nd; ++x) {
+      if (x == 0 || g.dec[x].cell != g.dec[x - 1].cell) cell_ptr[++k] = d0 + (int64_t)x;
+      ecell[x] = k;
+    }
+    int64_t* win_ptr = L(MB_ENC_RELAY_WIN_PTR) + w0;
+    std::vector<int64_t> at(g.n_w + 1, 0);
+    for (size_t x = 0; x < nd; ++x) ++at[g.dec[x].window + 1];
+    for (int64_t w = 0; w < g.n_w; ++w) at[w + 1] += at[w];
+    for (int64_t w = 0; w < g.n_w; ++w) win_ptr[w] = d0 + at[w];
+    for (size_t x = 0; x < nd; ++x) {
+      const int64_t pos = d0 + at[g.dec[x].window]++;
+      L(MB_ENC_ACT_REV)[pos] = d0 + (int64_t)x;
+      L(MB_ENC_RELAY_WCELL)[pos] = ecell[x];
+    }
+    int32_t* h = &cls_hist[(size_t)i * DEC_CLASSES];
+    for (size_t x = 0; x < nd; ++x) ++h[g.dec[x].cls];
   });
 
-  // Relay views and the action rows' window order (reference relay.py:48-94,
-  // builder.py:840-878): stable counting sorts of the decoder rows. The rows
-  // are already cell-major, so the cell-major view is the rows themselves.
+  // Batch-wide ends of the relay views, then the class view: a stable
+  // counting sort whose per-(class, position) starts come from the counts,
+  // so each position scatters its own rows.
   const int64_t n_d = dof[P], n_w = wo[P];
-  const int64_t* dcell = L(MB_ENC_DEC_CELL);
-  const int64_t* dwin = L(MB_ENC_DEC_WINDOW);
-  const int64_t* dcls = L(MB_ENC_DEC_CLASS);
-  int64_t* cell_ptr = L(MB_ENC_RELAY_CELL_PTR);
-  std::vector<int64_t> edge_cell(n_d);
-  int64_t nc = 0;
-  for (int64_t r = 0; r < n_d; ++r) {
-    if (r == 0 || dcell[r] != dcell[r - 1]) cell_ptr[nc++] = r;
-    edge_cell[r] = nc - 1;
+  L(MB_ENC_RELAY_CELL_PTR)[e->n_covered] = n_d;
+  L(MB_ENC_RELAY_WIN_PTR)[n_w] = n_d;
+  int64_t* cls_ptr = L(MB_ENC_RELAY_CLS_PTR);
+  std::vector<int64_t> start((size_t)P * DEC_CLASSES);
+  int64_t run = 0;
+  for (int c = 0; c < DEC_CLASSES; ++c) {
+    cls_ptr[c] = run;
+    for (int64_t i = 0; i < P; ++i) {
+      start[(size_t)i * DEC_CLASSES + c] = run;
+      run += cls_hist[(size_t)i * DEC_CLASSES + c];
+    }
   }
-  cell_ptr[nc] = n_d;
-  std::memcpy(L(MB_ENC_RELAY_WINDOW), dwin, n_d * sizeof(int64_t));
-  std::memcpy(L(MB_ENC_RELAY_CLASS), dcls, n_d * sizeof(int64_t));
-  auto counting_sort = [&](const int64_t* key, int64_t n_keys, int64_t* ptr, int64_t* order) {
-    std::fill(ptr, ptr + n_keys + 1, 0);
-    for (int64_t r = 0; r < n_d; ++r) ++ptr[key[r] + 1];
-    for (int64_t k = 0; k < n_keys; ++k) ptr[k + 1] += ptr[k];
-    std::vector<int64_t> at(ptr, ptr + n_keys);
-    for (int64_t r = 0; r < n_d; ++r) order[at[key[r]]++] = r;
-  };
-  int64_t* act_rev = L(MB_ENC_ACT_REV);
-  counting_sort(dwin, n_w, L(MB_ENC_RELAY_WIN_PTR), act_rev);
-  int64_t* wcell = L(MB_ENC_RELAY_WCELL);
-  for (int64_t r = 0; r < n_d; ++r) wcell[r] = edge_cell[act_rev[r]];
-  std::vector<int64_t> corder(n_d);
-  counting_sort(dcls, DEC_CLASSES, L(MB_ENC_RELAY_CLS_PTR), corder.data());
-  int64_t* ccell = L(MB_ENC_RELAY_CCELL);
-  for (int64_t r = 0; r < n_d; ++r) ccell[r] = edge_cell[corder[r]];
+  cls_ptr[DEC_CLASSES] = run;
+  parallel_for(P, threads, [&](int64_t i) {
+    const Graph& g = e->graphs[i];
+    int64_t* st = &start[(size_t)i * DEC_CLASSES];
+    int64_t k = e->cov_off[i] - 1;
+    for (size_t x = 0; x < g.dec.size(); ++x) {
+      if (x == 0 || g.dec[x].cell != g.dec[x - 1].cell) ++k;
+      L(MB_ENC_RELAY_CCELL)[st[g.dec[x].cls]++] = k;
+    }
+  });
   return MB_OK;
 }
 
