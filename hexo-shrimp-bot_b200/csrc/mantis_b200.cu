@@ -9,3 +9,4 @@
 #include "attention_sm100.cu"
 #include "noalloc.cu"
 #include "encoder.cu"
+#include "klent.cu"

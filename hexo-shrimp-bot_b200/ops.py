@@ -753,3 +753,56 @@ def axial_attention(q, k, v, coords, valid, bias, out=None):
          ptr(coords), ptr(valid), ptr(bias), ptr(out), out.stride(0), out.stride(1), out.stride(2),
          stream_of(q.device))
     return out
+
+
+# ----------------------------------------------------- KLENT improvement
+class ImprovedPolicy(NamedTuple):
+    """pi' and its per-position diagnostics, flat over the legal cells
+    (reference klent/improve.py:18-24)."""
+    probs: torch.Tensor
+    v_hat: torch.Tensor
+    kl: torch.Tensor
+    norm_entropy: torch.Tensor
+
+
+class Draw(NamedTuple):
+    """The self-play move draw (reference klent/selfplay.py:180-190)."""
+    stored: torch.Tensor     # (N,) float32 pi' renormalised in float64
+    ranks: torch.Tensor      # (P,) int64 chosen legal-cell rank
+    pi_top1: torch.Tensor    # (P,) float64
+    pi_chosen: torch.Tensor  # (P,) float64
+
+
+def improved_policy(policy_logits, q_score, q_value, offsets, tau, lam, uniforms=None):
+    """klent/improve.py:27-69 on the device (float32 inputs; sums in float64).
+    With ``uniforms`` (one float64 in [0, 1) per position) also the move draw:
+    returns (ImprovedPolicy, Draw), else the ImprovedPolicy."""
+    if tau < 0 or lam < 0 or tau + lam <= 0:
+        raise ValueError(f"need tau, lam >= 0 with tau + lam > 0, got ({tau}, {lam})")
+    if q_score.shape != q_value.shape:
+        raise ValueError("q_score and q_value must have the same shape, got "
+                         f"{tuple(q_score.shape)} and {tuple(q_value.shape)}")
+    _cuda(policy_logits, q_score, q_value, offsets)
+    if policy_logits.shape != q_score.shape or policy_logits.dim() != 1:
+        raise ValueError("policy_logits, q_score and q_value must be one-dimensional and one length")
+    if offsets.dtype != _I64 or offsets.dim() != 1 or offsets.shape[0] < 1:
+        raise ValueError("offsets must be a (P + 1,) int64 tensor")
+    x, sc, q = (t.float().contiguous() for t in (policy_logits, q_score, q_value))
+    off = offsets.contiguous()
+    n, p = x.shape[0], off.shape[0] - 1
+    dev = x.device
+    probs = torch.empty(n, dtype=torch.float32, device=dev)
+    v_hat, kl, ne = (torch.empty(p, dtype=torch.float32, device=dev) for _ in range(3))
+    draw = None
+    if uniforms is not None:
+        u = uniforms.to(device=dev, dtype=torch.float64).contiguous()
+        if u.shape != (p,):
+            raise ValueError(f"uniforms must hold one draw per position ({p})")
+        draw = Draw(torch.empty(n, dtype=torch.float32, device=dev), torch.empty(p, dtype=torch.int64, device=dev),
+                    torch.empty(p, dtype=torch.float64, device=dev), torch.empty(p, dtype=torch.float64, device=dev))
+    call("mb_klent_improve", ptr(x), ptr(sc), ptr(q), ptr(off), p, n, float(tau), float(lam), ptr(probs), ptr(v_hat),
+         ptr(kl), ptr(ne), ptr(u) if draw else None, ptr(draw.stored) if draw else None,
+         ptr(draw.ranks) if draw else None, ptr(draw.pi_top1) if draw else None,
+         ptr(draw.pi_chosen) if draw else None, stream_of(dev))
+    imp = ImprovedPolicy(probs, v_hat, kl, ne)
+    return (imp, draw) if draw is not None else imp

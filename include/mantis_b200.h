@@ -311,6 +311,24 @@ int mb_axial_attention(const void* q, const void* k, const void* v, int64_t n_po
                        const int32_t* valid, const float* bias, void* out, int64_t o_pos, int64_t o_head,
                        int64_t o_row, void* stream);
 
+/* ---------------------------------------------------------------- KLENT --
+ * Policy improvement over each position's legal cells (reference
+ * python/mantisnet/mantisnet/klent/improve.py:27-69, eq. 3 of the KLENT
+ * note; Rust crates/models/mantisnet/src/improvement.rs:104): pi' = softmax(
+ * (q_score + tau log softmax(logits)) / (tau + lam)) into probs, and per
+ * position v_hat = E_pi'[q_values], kl = KL(pi' || pi), norm_entropy =
+ * H(pi') / log|A| (0 for one legal cell). offsets: (n_pos + 1) int64 segment
+ * bounds over n cells. With uniforms (n_pos float64 draws in [0, 1)) it also
+ * draws each position's move as the self-play loop does
+ * (klent/selfplay.py:180-190): stored = pi' renormalised in float64 (written
+ * as float32), ranks = first cell whose cumulative probability reaches the
+ * uniform (clipped to the segment), pi_top1 and pi_chosen in float64.
+ * uniforms NULL skips the draw. All device pointers. */
+int mb_klent_improve(const float* policy_logits, const float* q_score, const float* q_values, const int64_t* offsets,
+                     int64_t n_pos, int64_t n, float tau, float lam, float* probs, float* v_hat, float* kl,
+                     float* norm_entropy, const double* uniforms, float* stored, int64_t* ranks, double* pi_top1,
+                     double* pi_chosen, void* stream);
+
 /* --------------------------------------------------------------- encoder --
  * Host-side batch builder: game positions to the collated batch arrays that
  * the evaluator reads. HOST pointers, no stream, no GPU needed. Replaces the
