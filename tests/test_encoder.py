@@ -85,3 +85,16 @@ def test_refusals_match_the_builder():
         assert "position 1" in str(native.value) and str(py.value) in str(native.value)
     with pytest.raises(ValueError):
         enc.encode([])
+
+
+@pytest.mark.gpu
+def test_pinned_output_matches():
+    """pin_memory=True writes the same arrays into page-locked buffers."""
+    _library_built()
+    specs = eng.random_positions(6, 30, 90, seed=8)
+    pinned = enc.encode(specs, pin_memory=True)
+    plain = enc.encode(specs)
+    for k, v in vars(plain).items():
+        if isinstance(v, torch.Tensor):
+            p = getattr(pinned, k)
+            assert p.is_pinned() and torch.equal(p, v), k
