@@ -221,11 +221,7 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.synchronize()
 
     def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return mb.sharding.max_over_ranks(x, device)
 
     for _ in range(args.warmup):
         step_device()
