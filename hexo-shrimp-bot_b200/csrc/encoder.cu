@@ -292,7 +292,7 @@ std::string build_one(const PosIn& in, Graph& g) {
     std::vector<int32_t> cnt(n_l + 1, 0);
     struct Hit { int32_t c, s, d; };
     std::vector<Hit> hits;
-    hits.reserve(n_s * 96);
+    hits.reserve(n_s * T.disk_q.size());  // at most one hit per disk offset
     for (int64_t s = 0; s < n_s; ++s) {
       const int64_t q = in.stone_qr[2 * s], r = in.stone_qr[2 * s + 1];
       for (int d = 0; d < nd; ++d) {
