@@ -410,14 +410,30 @@ std::string build_one(const PosIn& in, Graph& g) {
       for (int o = 0; o < 2 * W - 1; ++o)
         line[o] = digit_at(q0 + AX[a][0] * (o - (W - 1)), r0 + AX[a][1] * (o - (W - 1)));
       if (line[W - 1] != 0) return "a legal action cell is occupied";
-      for (int k = 0; k < W; ++k) {
+      // The window starting k steps before the cell covers line[5 - k ..
+      // 10 - k]; its pattern and counts slide from k = 5 down to k = 0.
+      int pre_k[W], own_k[W], opp_k[W];
+      {
         int pre = 0, own = 0, opp = 0;
         for (int j = 0; j < W; ++j) {
-          const int d = line[j + (W - 1) - k];
+          const int d = line[j];
           pre += d * T.pow3[j];
           own += d == 1;
           opp += d == 2;
         }
+        for (int k = W - 1;; --k) {
+          pre_k[k] = pre;
+          own_k[k] = own;
+          opp_k[k] = opp;
+          if (k == 0) break;
+          const int out = line[W - 1 - k], in = line[2 * W - 1 - k];
+          pre = (pre - out) / 3 + in * T.pow3[W - 1];
+          own += (in == 1) - (out == 1);
+          opp += (in == 2) - (out == 2);
+        }
+      }
+      for (int k = 0; k < W; ++k) {
+        const int pre = pre_k[k], own = own_k[k], opp = opp_k[k];
         const int post1 = T.post1[pre + T.pow3[k]][k];
         if (post1 < 0) return "a post-placement row lost its own stone";
         const bool kept = own > 0 || opp > 0;
