@@ -1,0 +1,28 @@
+"""bench.py's output contract, checked through the reference arm (which runs
+on the host cores, so no GPU is needed): one JSON line with the driver's keys,
+the reference marker, and an end-to-end object with zero copy bytes."""
+
+from __future__ import annotations
+
+import json
+import subprocess
+import sys
+
+from golden_io import REPO
+
+KEYS = {"metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
+        "vs_baseline", "dtype", "data", "config", "impl", "cpu_baseline", "e2e"}
+
+
+def test_reference_arm_prints_one_contract_line():
+    out = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "0",
+                          "--ref-sample", "1"], cwd=REPO, capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [l for l in out.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert KEYS <= set(d), KEYS - set(d)
+    assert d["impl"] == "reference" and d["value"] > 0 and d["higher_is_better"] is True
+    assert d["e2e"]["value"] == d["value"] and d["e2e"]["h2d_bytes_per_step"] == 0
+    assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["value"] == d["value"]
+    assert d["metric"] == json.loads((REPO / "BASELINE.json").read_text())["metric"]
