@@ -5,9 +5,12 @@ the same weights.
 
 The forward is inference-only (KLENT's evaluator path). It runs on CUDA only;
 every data-dependent step (CSR views, gathers, attention, reductions, norms,
-composition) is a kernel of libmantis_b200.so. Dense projections go through
-``Engine.linear``: the fused tcgen05 GEMM of the library (``gemm='native'``)
-or cuBLAS (``gemm='torch'``).
+composition) is a kernel of libmantis_b200.so. The dense projections follow
+``Engine``'s ``gemm`` mode: by default (``tcgen05-ln``) every projection that
+feeds a residual update is one fused tcgen05 launch of the library that also
+writes the updated residual and the next LayerNorms; ``native`` is the
+library's CUDA-core fp32 GEMM (the fp32 parity mode); ``cublas`` runs the
+projections through torch (see ``Engine.__init__`` for every mode).
 
 Numerics follow the reference's bf16 autocast contract (klent/train.py:
 105-118): fp32 residual streams, LayerNorm statistics in fp32, projections in
@@ -418,6 +421,10 @@ class Engine:
         # Optional launch timing: when a dict, the named stages of each forward
         # append a (start, end) CUDA event pair recorded on the launching stream.
         self.probe = None
+        # Most sources a radius-read group stages in shared memory (None: the
+        # batch's largest stone count, so every group is staged); groups of
+        # more stones read their K/V rows from global memory.
+        self.radius_stage_rows = None
         h = cfg.h
         m = model
         dev = m.latent_base.device
@@ -802,7 +809,9 @@ class Engine:
                     # block-diagonal: position p's cells read only position p's stones
                     read = ops.segment_attention_grouped(
                         q, kv[:, :h], kv[:, h:], blk["radius_bias"], blk["radius_vclass"], T.r_ptr, T.r_src,
-                        T.r_cls, T.cell_off, T.stone_off, T.max_t - GLOBAL_ROWS, skip_ptr=T.skip, out_dtype=cd)
+                        T.r_cls, T.cell_off, T.stone_off,
+                        self.radius_stage_rows if self.radius_stage_rows is not None else T.max_t - GLOBAL_ROWS,
+                        skip_ptr=T.skip, out_dtype=cd)
                 else:
                     read = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["radius_bias"], blk["radius_vclass"],
                                                  T.r_ptr, T.r_src, T.r_cls, skip_ptr=T.skip, out_dtype=cd)

@@ -5,6 +5,8 @@ GPU box; the committed ``.npz`` files travel instead):
 
     python tests/golden/make_golden.py --reference <path to python/mantisnet>
 
+(or set MANTISNET_REFERENCE to that path).
+
 The reference's PyO3 extension ``hexo_py`` needs cargo to build; the only
 module-level use is the ``MODEL_REPR_VERSION`` constant (builder.py:26), so a
 stub module carrying that constant is installed before importing. Positions
@@ -20,6 +22,14 @@ Fixtures written next to this script:
   parameters perturbed so every path carries signal), a collated batch, the
   reference outputs of ``MantisNet.forward`` and ``trunk``.
 - ``ops.npz``: op-level reference outputs on seeded random inputs.
+- ``forward_config1_<relay|prod>.npz``: the config-1 architecture (the
+  reference's default ``MantisConfig()``: h=128, 4 blocks, 4 heads of dim 32,
+  F=2) on 16 positions of 10-40 stones, relay (default knobs) and production
+  knobs (cell_latents + cell_nodes). Weights are seeded N(0, 0.02) everywhere
+  (``golden_io.config1_params``), so the fixture stores the seed and one
+  checksum per tensor instead of the 4.5-5.2 M parameters; the generator
+  checks that the reference's own module, given the same seed, holds exactly
+  the weights this repository's module regenerates.
 """
 
 from __future__ import annotations
@@ -28,6 +38,7 @@ import argparse
 import dataclasses
 import importlib
 import json
+import os
 import sys
 import types
 from pathlib import Path
@@ -194,19 +205,65 @@ def make_ops(mn):
     np.savez_compressed(HERE / "ops.npz", **{k: x.numpy() for k, x in a.items()})
 
 
+CONFIG1 = {"relay": dict(), "prod": dict(cell_latents=True, cell_nodes=True)}
+
+
+def make_config1(mn, eng, name: str, knobs: dict):
+    """Config 1: the reference's default architecture, 16 positions of 10-40
+    stones from seeded random legal play, std-0.02 weights, fp32 eager CPU."""
+    sys.path.insert(0, str(REPO / "tests"))
+    gio = importlib.import_module("golden_io")
+    seed = gio.CONFIG1_SEED[name]
+    cfg = mn.MantisConfig(**knobs)
+    ours = gio.config1_model(name)  # this repository's module, same seed
+    torch.manual_seed(seed)
+    model = mn.MantisNet(cfg).eval()
+    gio.config1_reinit(model, seed)
+    want = ours.state_dict()
+    got = model.state_dict()
+    assert list(want) == list(got), "parameter names / order differ from the reference"
+    for k in want:
+        assert torch.equal(want[k], got[k]), f"seeded weights differ from the reference at {k}"
+    specs = eng.random_positions(16, 10, 40, seed=gio.CONFIG1_POSITIONS_SEED)
+    graphs = [mn.builder.build(s.stone_qr, s.stone_owner, s.mover, s.legal_qr, s.moves_remaining) for s in specs]
+    batch = mn.builder.collate(graphs)
+    with torch.no_grad():
+        out = model(batch, 0.2)
+        w, g, cells = model.trunk(batch)
+        policy, critic = model.cell_head_logits(w, g, cells, batch)
+    arrays = {"config": np.array(json.dumps(dataclasses.asdict(cfg))), "mass_floor": np.array(0.2),
+              "seed": np.array(seed)}
+    for k, v in got.items():
+        arrays["checksum." + k] = np.array(gio.param_checksum(v))
+    arrays.update(_batch_arrays(batch, "batch."))
+    for k, v in vars(out).items():
+        arrays["out." + k] = v.numpy()
+    arrays["out.critic_logits"] = critic.numpy()
+    arrays["out.trunk_g"] = g.numpy()
+    np.savez_compressed(HERE / f"forward_config1_{name}.npz", **arrays)
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference/python/mantisnet")
+    ap.add_argument("--reference", default=os.environ.get("MANTISNET_REFERENCE"),
+                    help="path to the reference's python/mantisnet directory")
+    ap.add_argument("--only", choices=["all", "config1"], default="all")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference <path to python/mantisnet> or set MANTISNET_REFERENCE")
     torch.set_num_threads(max(1, torch.get_num_threads()))
     mn = _import_reference(args.reference)
     importlib.import_module("mantisnet.builder")
     eng = _engine()
-    specs = make_builder(mn, eng)
-    for i, (name, knobs) in enumerate(MODELS.items()):
-        make_forward(mn, specs, name, knobs, seed=100 + i)
-        print("forward", name, "done", flush=True)
-    make_ops(mn)
+    if args.only == "all":
+        specs = make_builder(mn, eng)
+        for i, (name, knobs) in enumerate(MODELS.items()):
+            make_forward(mn, specs, name, knobs, seed=100 + i)
+            print("forward", name, "done", flush=True)
+        make_ops(mn)
+    for name, knobs in CONFIG1.items():
+        make_config1(mn, eng, name, knobs)
+        print("config1", name, "done", flush=True)
     print("wrote fixtures to", HERE)
 
 

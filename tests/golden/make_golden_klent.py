@@ -23,6 +23,7 @@ from __future__ import annotations
 import argparse
 import importlib
 import json
+import os
 import sys
 import types
 from pathlib import Path
@@ -43,8 +44,11 @@ def _import_improve(checkout: Path):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("HEXO_REFERENCE"),
+                    help="path to the reference checkout (the directory holding python/ and crates/)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference <checkout> or set HEXO_REFERENCE")
     checkout = Path(args.reference)
     imp = _import_improve(checkout)
     out = {}

@@ -1,0 +1,163 @@
+"""Full-forward parity at the benchmark's configurations.
+
+- Config 1 (the reference's default architecture: h=128, 4 blocks, 4 heads of
+  dim 32, F=2; 16 positions of 10-40 stones; relay and production knobs): the
+  GPU fp32 mode against the reference's own eager-CPU fp32 outputs
+  (``forward_config1_*.npz``) within 1e-4 relative, and the bf16 mode within
+  the north_star bf16 contract of them (2e-2 absolute on logits, 1e-2 on Q
+  and value).
+- Config 5 (the benched workload: late positions of 150-300 stones at the
+  config-4 architecture h=256 / 8 blocks / 8 heads / F=4, cell_latents +
+  cell_nodes, bf16, built by the native encoder, evaluated through
+  ``network_evaluate`` as the bench does: a 512-position call split into a
+  64-position lead run and a 448-position run): every checked position
+  within the north_star bf16 contract of the fp32 CPU oracle. One checked
+  position has 300 stones (stone attention over T = 304 tokens), and the
+  radius read is also run with its shared-memory stage smaller than that
+  position's stone count, so its group reads K/V from global memory.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+import golden_io
+from golden_io import mb
+from oracle import forward as O
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _ocfg(cfg: dict) -> O.Cfg:
+    return O.Cfg(**{k: v for k, v in cfg.items() if k != "dropout"})
+
+
+def _rel(got, want, rtol, what):
+    scale = want.abs().max().clamp(min=1e-6)
+    err = (got.float().cpu() - want).abs().max()
+    assert err <= rtol * scale, f"{what}: max err {err:.3e} vs scale {scale:.3e}"
+
+
+@pytest.mark.parametrize("gemm", ["native", "cublas"])
+@pytest.mark.parametrize("name", golden_io.CONFIG1_CASES)
+def test_config1_fp32_matches_reference(name, gemm):
+    cfg, P, batch, want, mf = golden_io.config1_case(name)
+    net = mb.MantisNet(mb.MantisConfig(**cfg))
+    net.load_state_dict(P, strict=True)
+    net = net.to(DEV).eval()
+    b = batch.to(DEV)
+    eng = net.engine(torch.float32, gemm=gemm)
+    w, g, cells = eng.trunk(b)
+    policy, critic = eng.heads(w, g, cells, b)
+    q_score, q_values = mb.ops.compose(critic, b.legal_offsets, mf)
+    value, _, logits = eng.value_head(w, g, b)
+    for got, k in ((policy, "policy_logits"), (critic, "critic_logits"), (q_values, "q_values"),
+                   (q_score, "q_score"), (value, "value"), (logits, "value_logits")):
+        _rel(got, want[k], 1e-4, f"{name}/{gemm}:{k}")
+    mb._lib.check_device_error()
+
+
+@pytest.mark.parametrize("name", golden_io.CONFIG1_CASES)
+def test_config1_bf16_contract(name):
+    cfg, P, batch, want, mf = golden_io.config1_case(name)
+    net = mb.MantisNet(mb.MantisConfig(**cfg))
+    net.load_state_dict(P, strict=True)
+    net = net.to(DEV).eval()
+    ev = mb.network_evaluate(net, mb.evaluator.EvaluatorConfig(device=DEV, autocast=True, mass_floor=mf))
+    policy, q_score, q_values = ev(batch)
+    assert (policy - want["policy_logits"]).abs().max() <= 2e-2
+    assert (q_values - want["q_values"]).abs().max() <= 1e-2
+    out = net(batch.to(DEV), mf)
+    assert (out.value.cpu() - want["value"]).abs().max() <= 1e-2
+    assert (out.policy_logits.cpu() - want["policy_logits"]).abs().max() <= 2e-2
+
+
+BENCH_ARCH = dict(h=256, blocks=8, heads=8, ffn_factor=4, cell_latents=True, cell_nodes=True)
+
+
+def _bench_model(seed=41):
+    torch.manual_seed(seed)
+    net = mb.MantisNet(mb.MantisConfig(**BENCH_ARCH)).eval()
+    golden_io.config1_reinit(net, seed)  # every weight N(0, 0.02), LayerNorms 1 / 0
+    return net
+
+
+@pytest.fixture(scope="module")
+def config5():
+    checked = mb.engine.random_positions(9, 150, 300, seed=505) + mb.engine.random_positions(1, 300, 300, seed=506)
+    assert max(len(s.stone_qr) for s in checked) == 300
+    filler = mb.engine.random_positions(62, 150, 300, seed=507)
+    specs = checked[:5] + (filler * 9)[:502] + checked[5:]
+    assert len(specs) == 512
+    batch = mb.encoder.encode(specs)
+    lone = mb.encoder.encode(checked)
+    net = _bench_model()
+    P = {k: v.detach().clone() for k, v in net.state_dict().items()}
+    cfg = net.cfg.to_dict()
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    ref = O.forward(_ocfg(cfg), P, lone, 0.2)
+    return net.to(DEV), batch, lone, ref
+
+
+def _slices(batch, lone):
+    """(rows of the 512-position batch, rows of the checked batch) of the
+    checked positions: the first five and the last five."""
+    off = batch.legal_offsets
+    lo = lone.legal_offsets
+    n_lead = int(off[5])
+    n_tail = int(off[-1] - off[-6])
+    return [(slice(0, n_lead), slice(0, int(lo[5]))),
+            (slice(int(off[-6]), int(off[-1])), slice(int(lo[5]), int(lo[5]) + n_tail))]
+
+
+def test_config5_pipelined_evaluator_bf16_contract(config5):
+    net, batch, lone, ref = config5
+    cfg = mb.evaluator.EvaluatorConfig(device=DEV, autocast=True, mass_floor=0.2)
+    assert mb.evaluator.split_points(batch, cfg.part_positions) == [0, 64, 512]
+    ev = mb.network_evaluate(net, cfg)
+    policy, q_score, q_values = ev(batch)
+    for mine, theirs in _slices(batch, lone):
+        assert (policy[mine] - ref["policy_logits"][theirs]).abs().max() <= 2e-2
+        assert (q_values[mine] - ref["q_values"][theirs]).abs().max() <= 1e-2
+    assert torch.isfinite(policy).all() and torch.isfinite(q_score).all()
+
+
+@pytest.mark.parametrize("stage_rows", [None, 200])
+def test_config5_forward_bf16_contract(config5, stage_rows):
+    """The checked positions alone: every head, value included; with
+    stage_rows=200 the 300-stone position's radius group (and those of the
+    other positions above 200 stones) reads K/V from global memory."""
+    net, batch, lone, ref = config5
+    eng = net.engine(torch.bfloat16)
+    eng.radius_stage_rows = stage_rows
+    try:
+        b = lone.to(DEV)
+        w, g, cells = eng.trunk(b)
+        value, _, _ = eng.value_head(w, g, b)
+        policy, critic = eng.heads(w, g, cells, b)
+        q_score, q_values = mb.ops.compose(critic, b.legal_offsets, 0.2)
+    finally:
+        eng.radius_stage_rows = None
+    assert int(b.attn_valid.sum(1).max()) == 304
+    assert (policy.float().cpu() - ref["policy_logits"]).abs().max() <= 2e-2
+    assert (q_values.cpu() - ref["q_values"]).abs().max() <= 1e-2
+    assert (value.cpu() - ref["value"]).abs().max() <= 1e-2
+    mb._lib.check_device_error()
+
+
+def test_config5_fp32_matches_oracle(config5):
+    """The fp32 mode on the checked late positions: 1e-4 relative to the
+    fp32 oracle (north_star fp32 contract) on every head."""
+    net, batch, lone, ref = config5
+    eng = net.engine(torch.float32, gemm="native")
+    b = lone.to(DEV)
+    w, g, cells = eng.trunk(b)
+    value, _, _ = eng.value_head(w, g, b)
+    policy, critic = eng.heads(w, g, cells, b)
+    q_score, q_values = mb.ops.compose(critic, b.legal_offsets, 0.2)
+    _rel(policy, ref["policy_logits"], 1e-4, "policy")
+    _rel(critic, ref["critic_logits"], 1e-4, "critic")
+    _rel(q_values, ref["q_values"], 1e-4, "q_values")
+    _rel(value, ref["value"], 1e-4, "value")

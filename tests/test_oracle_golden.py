@@ -81,3 +81,16 @@ def test_oracle_batched_equals_per_position():
         torch.testing.assert_close(full["value"][i:i + 1], one["value"], rtol=0, atol=1e-6)
         offset += n
     assert offset == full["policy_logits"].shape[0] == batch.n_cells
+
+
+@pytest.mark.parametrize("name", golden_io.CONFIG1_CASES)
+def test_oracle_config1_matches_reference(name):
+    """Config 1 (the reference's default architecture: h=128, 4 blocks, 4
+    heads of dim 32) on 16 positions of 10-40 stones, fp32, 1e-4 relative."""
+    cfg, P, batch, want, mf = golden_io.config1_case(name)
+    assert cfg["h"] == 128 and cfg["blocks"] == 4 and cfg["heads"] == 4 and batch.n_pos == 16
+    got = O.forward(_cfg(cfg), P, batch, mf)
+    for k in ("policy_logits", "critic_logits", "q_score", "q_values", "value", "value_logits", "trunk_g"):
+        scale = want[k].abs().max().clamp(min=1e-6)
+        err = (got[k] - want[k]).abs().max()
+        assert err <= 1e-4 * scale, f"{name}:{k} max err {err:.3e} vs scale {scale:.3e}"
