@@ -66,6 +66,8 @@ def _lookup(sorted_keys: np.ndarray, keys: np.ndarray) -> np.ndarray:
     return np.where(sorted_keys[pos] == keys, pos, -1)
 
 
+_MSG_REACH = "every legal cell must be empty and at most 8 steps from a stone"
+
 # Offsets of the radius-8 disk without its centre, for stone -> cell edges.
 _DISK = np.array(
     [
@@ -138,7 +140,7 @@ def _cell_node_fields(stone_qr, stone_own, legal_qr, legal_key, legal_sorted, le
         nearest = np.full(n_legal, LEGAL_RADIUS + 1, dtype=np.int64)
         np.minimum.at(nearest, dst, _DISK_DIST[disk])
         if np.any(nearest > LEGAL_RADIUS) or np.any(_lookup(np.sort(_pack(stone_qr)), legal_key) >= 0):
-            raise ValueError("legal cells must be empty and within radius 8 of a stone")
+            raise ValueError(_MSG_REACH)
         # The displacement is cell - stone, which is the disk offset itself.
         radius = dict(
             radius_src=src.astype(np.int64),
@@ -171,160 +173,181 @@ def _cell_node_fields(stone_qr, stone_own, legal_qr, legal_key, legal_sorted, le
     return dict(cell_qr=legal_qr.copy(), cell_nearest=nearest, **radius, **adj)
 
 
-def _action_tables(legal_qr, stone_sorted, stone_order, stone_own, live_key):
-    """18 hypothetical post-placement rows per legal action plus the tactical
-    scalars (reference builder.py:292-424)."""
-    n_legal = len(legal_qr)
-    offs = np.arange(-(WINDOW_LEN - 1), WINDOW_LEN, dtype=np.int64)
-    cells = legal_qr[:, None, None, :] + AXES[None, :, None, :] * offs[None, None, :, None]
-    occ = _lookup(stone_sorted, _pack(cells))
-    occupant = np.where(occ >= 0, stone_order[np.maximum(occ, 0)] if len(stone_order) else 0, -1)
-    digit = np.where(occupant >= 0, np.where(stone_own[np.maximum(occupant, 0)] == 0, 1, 2), 0) \
-        if len(stone_own) else np.zeros(occupant.shape, dtype=np.int64)
-    line = digit.reshape(n_legal, 3, 2 * WINDOW_LEN - 1)
-    if line[:, :, WINDOW_LEN - 1].any():
-        raise ValueError("a legal action cell is occupied")
-    # slot j of the window starting k steps before the cell sits at line[j + 5 - k]
-    j_idx = np.arange(WINDOW_LEN)[None, :] + (WINDOW_LEN - 1) - np.arange(WINDOW_LEN)[:, None]
-    win_digits = line[:, :, j_idx]  # (n_legal, 3, k, j)
-    pre = (win_digits * POW3).sum(axis=-1)
-    own_count = (win_digits == 1).sum(axis=-1)
-    opp_count = (win_digits == 2).sum(axis=-1)
-    has_own, has_opp = own_count > 0, opp_count > 0
-    status = np.where(
-        has_own & ~has_opp, ACTION_OWN,
-        np.where(has_opp & ~has_own, ACTION_OPP,
-                 np.where(has_own & has_opp, ACTION_MIXED, ACTION_EMPTY)),
-    )
-    k_arr = np.arange(WINDOW_LEN)[None, None, :]
-    post1 = TERN_POST1_CLASS[pre + POW3[None, None, :], k_arr]
-    if post1.min(initial=0) < 0:
-        raise ValueError("a post-placement row lost its own stone")
+# ---------------------------------------------------------------- windows
+# Format of the window, decoder and action tables (the representation
+# contract the checkpoints and the Rust bridge read):
+#
+# A window is six consecutive cells along one of the three line axes
+# (``AXES``: Q, R, QR); slot j of the window (axis a, start s) is the cell
+# s + j * AXES[a]. Each slot holds a ternary digit: 0 empty, 1 a stone of
+# the player to move, 2 an opponent stone; the window's pattern is
+# sum_j digit_j * 3**j. The live windows are those with at least one stone,
+# listed by ascending key pack(s) * 4 + a. Each live window has an
+# incidence row per occupied slot (window by window, slots ascending) with
+# the class of (pattern, slot).
+#
+# Every legal cell c sits at slot k of the six windows of each axis that
+# start k steps before it (k = 0..5): 18 candidate rows per cell, listed
+# axis-major then k. A candidate whose window is live is a decoder row
+# (class of (pattern, empty slot k)); every candidate also yields an action
+# row: the pattern after the mover places a stone at slot k, its status
+# (which players the window held before the placement) and the window's
+# index when live (-1 otherwise). Eleven tactical scalars per cell summarise
+# a cell's 18 candidates.
 
-    starts = legal_qr[:, None, None, :] - AXES[None, :, None, :] * np.arange(WINDOW_LEN)[None, None, :, None]
-    wkey = _pack(starts) * 4 + np.arange(3)[None, :, None]
-    window_index = _lookup(live_key, wkey)
-    kept = status != ACTION_EMPTY
-    if ((window_index >= 0) != kept).any():
-        raise ValueError("the kept-window set disagrees with the action-row walk")
+_SLOT = np.arange(WINDOW_LEN)
+_REACH = WINDOW_LEN - 1  # a window through a cell spans 5 cells either side
+# line offset of slot j in the window starting k cells before the centre
+_WINDOW_AT = (_REACH - _SLOT)[:, None] + _SLOT[None, :]  # (k, j)
 
-    opp_only = has_opp & ~has_own
-    five_rows = opp_only & (opp_count == 5)
-    four_rows = opp_only & (opp_count == 4)
-    five_remaining = len(np.unique(window_index[five_rows]))
-    four_remaining = len(np.unique(window_index[four_rows]))
-    ax = (1, 2)
-    opp_five_hit = five_rows.sum(axis=ax)
-    rows_total = np.float32(3 * WINDOW_LEN)
+_MSG_TERMINAL = "terminal position: no legal move left to evaluate"
+_MSG_DUPLICATE = "two stones occupy the same cell"
+_MSG_OCCUPIED = "a legal cell holds a stone"
+
+
+class _Board:
+    """Stones by coordinate: the stone row at a cell and its ternary digit
+    (0 empty, 1 the mover's stone, 2 an opponent stone)."""
+
+    def __init__(self, stone_qr: np.ndarray, opponent: np.ndarray):
+        key = _pack(stone_qr)
+        self.order = np.argsort(key, kind="stable")
+        self.keys = key[self.order]
+        if len(self.keys) > 1 and np.any(self.keys[1:] == self.keys[:-1]):
+            raise ValueError(_MSG_DUPLICATE)
+        self.digit_of = 1 + opponent
+
+    def rows_at(self, qr: np.ndarray) -> np.ndarray:
+        hit = _lookup(self.keys, _pack(qr))
+        if len(self.order) == 0:
+            return hit
+        return np.where(hit >= 0, self.order[np.maximum(hit, 0)], -1)
+
+    def lines(self, centres: np.ndarray):
+        """Stone rows and digits on the 11-cell line through each centre along
+        each axis: arrays (n, 3, 11), offset o at line index o + 5."""
+        offs = np.arange(-_REACH, _REACH + 1)
+        qr = centres[:, None, None, :] + AXES[None, :, None, :] * offs[None, None, :, None]
+        rows = self.rows_at(qr)
+        digits = np.where(rows >= 0, self.digit_of[np.maximum(rows, 0)] if len(self.digit_of) else 0, 0)
+        return rows, digits
+
+
+def _live_windows(board: _Board, stone_qr: np.ndarray):
+    """Every live window once, in key order: (axis, start (n, 2), pattern,
+    stone row per slot (n, 6), -1 where empty).
+
+    A window is enumerated from its lowest occupied slot only: the stone at
+    line offset 0 is slot k of the window starting k cells before it, and it
+    is that window's lowest stone when the k cells before it are empty."""
+    n_s = len(stone_qr)
+    rows, digits = board.lines(stone_qr)
+    before = digits[:, :, :_REACH] == 0  # the five cells before the stone
+    # clear[..., k]: the k cells right before the stone are empty
+    suffix = np.flip(np.logical_and.accumulate(np.flip(before, -1), -1), -1)
+    clear = np.concatenate([np.ones((n_s, 3, 1), bool), np.flip(suffix, -1)], axis=-1)
+    stone, axis, k = np.nonzero(clear)
+    start = stone_qr[stone] - AXES[axis] * k[:, None]
+    slots = rows[stone, axis][np.arange(len(k))[:, None], _WINDOW_AT[k]]
+    pattern = (digits[stone, axis][np.arange(len(k))[:, None], _WINDOW_AT[k]] * POW3).sum(1)
+    key = _pack(start) * 4 + axis
+    by_key = np.argsort(key, kind="stable")
+    return axis[by_key].astype(np.int64), start[by_key], pattern[by_key], slots[by_key], key[by_key]
+
+
+# tactical scalar columns (the checkpoint reads them in this order)
+(_T_WIN_NOW, _T_OWN_BEST, _T_OPP_BEST, _T_MAKE_FIVE, _T_MAKE_FOUR, _T_BLOCK_FIVE, _T_BLOCK_FOUR,
+ _T_FIVES_LEFT, _T_FOURS_LEFT, _T_BLOCKS_ALL_FIVES, _T_LIVE_ROWS) = range(TACTICAL_FEATURES)
+
+
+def _cell_rows(board: _Board, legal_qr: np.ndarray, win_key: np.ndarray, win_pattern: np.ndarray):
+    """Decoder rows and action rows of every legal cell's 18 candidates, and
+    the cells' tactical scalars."""
+    n_c = len(legal_qr)
+    _, digits = board.lines(legal_qr)
+    if np.any(digits[:, :, _REACH] != 0):
+        raise ValueError(_MSG_OCCUPIED)
+    cand = digits[:, :, _WINDOW_AT]  # (n_c, 3, k, j): digits of the window starting k before the cell
+    before = (cand * POW3).sum(-1)  # pattern before the placement
+    mine = (cand == 1).sum(-1)
+    theirs = (cand == 2).sum(-1)
+    live = (mine + theirs) > 0
+    start = legal_qr[:, None, None, :] - AXES[None, :, None, :] * _SLOT[None, None, :, None]
+    window = np.where(live, _lookup(win_key, _pack(start) * 4 + np.arange(3)[None, :, None]), -1)
+    if np.any((window >= 0) != live):
+        raise ValueError("internal: a window through a stone is missing from the live set")
+    status = np.select([live & (theirs == 0), live & (mine == 0), live], [ACTION_OWN, ACTION_OPP, ACTION_MIXED],
+                       ACTION_EMPTY)
+    placed = TERN_POST1_CLASS[before + POW3[None, None, :], _SLOT[None, None, :]]
+
+    cell, axis, k = np.nonzero(live)  # cell-major, then axis, then k
+    dec_window = window[cell, axis, k]
+    dec_class = TERN_DEC_CLASS[win_pattern[dec_window], k]
+
+    # tactical scalars
     f32 = np.float32
-
-    tactical = np.stack(
-        [
-            (~has_opp & (own_count == WINDOW_LEN - 1)).any(axis=ax).astype(f32),
-            (own_count.max(axis=ax) + 1).astype(f32) / f32(WINDOW_LEN),
-            opp_count.max(axis=ax).astype(f32) / f32(WINDOW_LEN),
-            (~has_opp & (own_count + 1 == 5)).sum(axis=ax).astype(f32) / rows_total,
-            (~has_opp & (own_count + 1 == 4)).sum(axis=ax).astype(f32) / rows_total,
-            opp_five_hit.astype(f32) / rows_total,
-            four_rows.sum(axis=ax).astype(f32) / rows_total,
-            np.full(n_legal, f32(min(five_remaining, GLOBAL_THREAT_CAP)) / f32(GLOBAL_THREAT_CAP), dtype=f32),
-            np.full(n_legal, f32(min(four_remaining, GLOBAL_THREAT_CAP)) / f32(GLOBAL_THREAT_CAP), dtype=f32),
-            ((five_remaining > 0) & (opp_five_hit == five_remaining)).astype(f32),
-            kept.sum(axis=ax).astype(f32) / rows_total,
-        ],
-        axis=1,
-    ).astype(f32)
-    return window_index, post1, status, tactical
+    per_cell = (1, 2)
+    n_rows = f32(3 * WINDOW_LEN)
+    clean = theirs == 0
+    blocks_five = live & (mine == 0) & (theirs == WINDOW_LEN - 1)
+    blocks_four = live & (mine == 0) & (theirs == WINDOW_LEN - 2)
+    fives_left = np.unique(window[blocks_five]).size
+    fours_left = np.unique(window[blocks_four]).size
+    five_hits = blocks_five.sum(per_cell)
+    cap = f32(GLOBAL_THREAT_CAP)
+    tac = np.empty((n_c, TACTICAL_FEATURES), dtype=f32)
+    tac[:, _T_WIN_NOW] = (clean & (mine == WINDOW_LEN - 1)).any(per_cell)
+    tac[:, _T_OWN_BEST] = (mine.max(per_cell) + 1).astype(f32) / f32(WINDOW_LEN)
+    tac[:, _T_OPP_BEST] = theirs.max(per_cell).astype(f32) / f32(WINDOW_LEN)
+    tac[:, _T_MAKE_FIVE] = (clean & (mine == 4)).sum(per_cell).astype(f32) / n_rows
+    tac[:, _T_MAKE_FOUR] = (clean & (mine == 3)).sum(per_cell).astype(f32) / n_rows
+    tac[:, _T_BLOCK_FIVE] = five_hits.astype(f32) / n_rows
+    tac[:, _T_BLOCK_FOUR] = blocks_four.sum(per_cell).astype(f32) / n_rows
+    tac[:, _T_FIVES_LEFT] = f32(min(fives_left, GLOBAL_THREAT_CAP)) / cap
+    tac[:, _T_FOURS_LEFT] = f32(min(fours_left, GLOBAL_THREAT_CAP)) / cap
+    tac[:, _T_BLOCKS_ALL_FIVES] = (fives_left > 0) & (five_hits == fives_left)
+    tac[:, _T_LIVE_ROWS] = live.sum(per_cell).astype(f32) / n_rows
+    return dict(
+        dec_cell=cell.astype(np.int64), dec_window=dec_window.astype(np.int64), dec_class=dec_class.astype(np.int64),
+        action_window_index=window.astype(np.int64), action_post1_class=placed.astype(np.int64),
+        action_pre_status=status.astype(np.int64), action_tactical=tac,
+    )
 
 
 def build(stone_qr, stone_owner, mover, legal_qr, moves_remaining) -> PositionGraph:
-    """One position's graph from the builder input list (reference builder.py:486-642).
+    """One position's graph from the builder input list: stones (q, r) with
+    their owners, the player to move, the legal cells in engine order and the
+    stones left this turn (reference builder.py:486-642).
 
-    Raises ``ValueError`` for a terminal position (no legal moves), a bad
-    ``moves_remaining``, duplicate stones, or legal cells that are occupied
-    or out of reach."""
-    stone_qr = np.asarray(stone_qr, dtype=np.int64).reshape(-1, 2)
-    stone_owner = np.asarray(stone_owner, dtype=np.int64).reshape(-1)
-    legal_qr = np.asarray(legal_qr, dtype=np.int64).reshape(-1, 2)
-    if len(legal_qr) == 0:
-        raise ValueError("terminal position: the builder refuses it")
+    Raises ``ValueError`` for a terminal position (no legal moves), a turn
+    that does not place one or two stones, two stones on one cell, or a
+    legal cell that holds a stone or lies beyond distance 8 of every stone."""
+    stones = np.asarray(stone_qr, dtype=np.int64).reshape(-1, 2)
+    owners = np.asarray(stone_owner, dtype=np.int64).reshape(-1)
+    cells = np.asarray(legal_qr, dtype=np.int64).reshape(-1, 2)
+    if len(cells) == 0:
+        raise ValueError(_MSG_TERMINAL)
     if moves_remaining not in (1, 2):
-        raise ValueError(f"moves_remaining must be 1 or 2, got {moves_remaining}")
-    n_s = len(stone_qr)
-    stone_own = (stone_owner != mover).astype(np.int64)
+        raise ValueError(f"a turn places one or two stones; got moves_remaining={moves_remaining}")
+    opponent = (owners != mover).astype(np.int64)  # stone_own: 0 the mover's, 1 the opponent's
 
-    legal_key = _pack(legal_qr)
-    legal_order = np.argsort(legal_key, kind="stable")
-    legal_sorted = legal_key[legal_order]
-    legal_rank = legal_order  # sorted slot -> legal row
-    cell_nodes = _cell_node_fields(stone_qr, stone_own, legal_qr, legal_key, legal_sorted, legal_rank)
+    cell_key = _pack(cells)
+    cell_order = np.argsort(cell_key, kind="stable")
+    node_fields = _cell_node_fields(stones, opponent, cells, cell_key, cell_key[cell_order], cell_order)
+    board = _Board(stones, opponent)
 
-    empty = np.empty(0, dtype=np.int64)
-    if n_s == 0:
-        actions = _action_tables(legal_qr, empty, empty, stone_own, empty)
-        return PositionGraph(
-            stone_own=stone_own, stone_qr=stone_qr,
-            window_feat=empty, window_id=np.empty((0, 3), dtype=np.int64),
-            inc_stone=empty, inc_window=empty, inc_class=empty,
-            n_legal=len(legal_qr), **cell_nodes,
-            dec_cell=empty, dec_window=empty, dec_class=empty,
-            moves_remaining=moves_remaining,
-            action_window_index=actions[0], action_post1_class=actions[1],
-            action_pre_status=actions[2], action_tactical=actions[3],
-        )
-
-    stone_key = _pack(stone_qr)
-    stone_order = np.argsort(stone_key, kind="stable")
-    stone_sorted = stone_key[stone_order]
-    if np.any(stone_sorted[1:] == stone_sorted[:-1]):
-        raise ValueError("duplicate stone coordinates")
-
-    ks = np.arange(WINDOW_LEN, dtype=np.int64)
-    # Every (axis, start) through some stone: 18 candidates per stone.
-    starts = stone_qr[:, None, None, :] - AXES[None, :, None, :] * ks[None, None, :, None]
-    axis_of = np.broadcast_to(np.arange(3)[None, :, None], starts.shape[:3])
-    cand_key = (_pack(starts) * 4 + axis_of).reshape(-1)
-    live_key, first = np.unique(cand_key, return_index=True)
-    w_start = starts.reshape(-1, 2)[first]
-    w_axis = axis_of.reshape(-1)[first].astype(np.int64)
-
-    wcells = w_start[:, None, :] + AXES[w_axis][:, None, :] * ks[None, :, None]
-    occ = _lookup(stone_sorted, _pack(wcells))
-    occupant = np.where(occ >= 0, stone_order[np.maximum(occ, 0)], -1)  # (n_w, 6)
-    own = stone_own[np.maximum(occupant, 0)]
-    digit = np.where(occupant >= 0, 1 + own, 0)
-    pattern = (digit * POW3[None, :]).sum(axis=1)
-    window_feat = TERN_RANK[pattern]
-    window_id = np.column_stack([w_axis, w_start[:, 0], w_start[:, 1]])
-
-    w_idx, slot = np.nonzero(occupant >= 0)
-    inc_stone = occupant[w_idx, slot]
-    inc_class = TERN_OCC_CLASS[pattern[w_idx], slot]
-    if inc_class.size and inc_class.min() < 0:
-        raise ValueError("incidence entry pairs a window with a slot it does not occupy")
-
-    c_starts = legal_qr[:, None, None, :] - AXES[None, :, None, :] * ks[None, None, :, None]
-    c_key = (_pack(c_starts) * 4 + np.arange(3)[None, :, None]).reshape(-1)
-    c_win = _lookup(live_key, c_key)
-    flat = np.nonzero(c_win >= 0)[0]
-    dec_cell = flat // (3 * WINDOW_LEN)
-    dec_window = c_win[flat]
-    dec_class = TERN_DEC_CLASS[pattern[dec_window], flat % WINDOW_LEN]
-    if dec_class.size and dec_class.min() < 0:
-        raise ValueError("decoder entry pairs a window with a slot it already occupies")
-
-    actions = _action_tables(legal_qr, stone_sorted, stone_order, stone_own, live_key)
+    axis, start, pattern, slots, win_key = _live_windows(board, stones)
+    win, slot = np.nonzero(slots >= 0)  # window-major, slot-minor
+    inc_class = TERN_OCC_CLASS[pattern[win], slot]
+    rows = _cell_rows(board, cells, win_key, pattern)
     return PositionGraph(
-        stone_own=stone_own, stone_qr=stone_qr,
-        window_feat=window_feat, window_id=window_id,
-        inc_stone=inc_stone.astype(np.int64), inc_window=w_idx.astype(np.int64),
-        inc_class=inc_class,
-        n_legal=len(legal_qr), **cell_nodes,
-        dec_cell=dec_cell.astype(np.int64), dec_window=dec_window.astype(np.int64),
-        dec_class=dec_class,
-        moves_remaining=moves_remaining,
-        action_window_index=actions[0], action_post1_class=actions[1],
-        action_pre_status=actions[2], action_tactical=actions[3],
+        stone_own=opponent, stone_qr=stones,
+        window_feat=TERN_RANK[pattern].astype(np.int64),
+        window_id=np.column_stack([axis, start[:, 0], start[:, 1]]).astype(np.int64).reshape(-1, 3),
+        inc_stone=slots[win, slot].astype(np.int64), inc_window=win.astype(np.int64),
+        inc_class=inc_class.astype(np.int64),
+        n_legal=len(cells), **node_fields,
+        moves_remaining=moves_remaining, **rows,
     )
 
 

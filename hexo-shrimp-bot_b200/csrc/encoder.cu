@@ -249,9 +249,9 @@ struct PosIn {
 // Builds one position; returns an empty string or the refusal message.
 std::string build_one(const PosIn& in, Graph& g) {
   const Tables& T = tables();
-  if (in.n_l == 0) return "terminal position: the builder refuses it";
+  if (in.n_l == 0) return "terminal position: no legal move left to evaluate";
   if (in.moves != 1 && in.moves != 2)
-    return "moves_remaining must be 1 or 2, got " + std::to_string(in.moves);
+    return "a turn places one or two stones; got moves_remaining=" + std::to_string(in.moves);
   const int64_t n_s = in.n_s, n_l = in.n_l;
   g.n_s = n_s;
   g.n_l = n_l;
@@ -310,7 +310,7 @@ std::string build_one(const PosIn& in, Graph& g) {
       for (int64_t s = 0; s < n_s; ++s) stones.insert(in.stone_qr[2 * s], in.stone_qr[2 * s + 1], s);
       for (int64_t c = 0; c < n_l && !bad; ++c) bad = stones.find(in.legal_qr[2 * c], in.legal_qr[2 * c + 1]) >= 0;
     }
-    if (bad) return "legal cells must be empty and within radius 8 of a stone";
+    if (bad) return "every legal cell must be empty and at most 8 steps from a stone";
     // stable counting sort by destination: sources stay ascending within a cell
     for (int64_t c = 0; c < n_l; ++c) cnt[c + 1] += cnt[c];
     g.radius.resize(hits.size());
@@ -344,7 +344,7 @@ std::string build_one(const PosIn& in, Graph& g) {
     std::vector<int64_t> keys(n_s);
     for (int64_t s = 0; s < n_s; ++s) keys[s] = pack(in.stone_qr[2 * s], in.stone_qr[2 * s + 1]);
     std::sort(keys.begin(), keys.end());
-    if (std::adjacent_find(keys.begin(), keys.end()) != keys.end()) return "duplicate stone coordinates";
+    if (std::adjacent_find(keys.begin(), keys.end()) != keys.end()) return "two stones occupy the same cell";
     for (int64_t s = 0; s < n_s; ++s) stones.insert(in.stone_qr[2 * s], in.stone_qr[2 * s + 1], s);
   }
   auto digit_at = [&](int64_t q, int64_t r) -> int {  // 0 empty, 1 own (mover's), 2 opponent's
@@ -390,7 +390,7 @@ std::string build_one(const PosIn& in, Graph& g) {
   }
   for (IncRow& e : g.inc) {
     const int cls = T.occ[pattern[e.window]][e.cls];
-    if (cls < 0) return "incidence entry pairs a window with a slot it does not occupy";
+    if (cls < 0) return "internal: an occupied slot has no incidence class";
     e.cls = (int16_t)cls;
   }
 
@@ -409,7 +409,7 @@ std::string build_one(const PosIn& in, Graph& g) {
       int line[2 * W - 1];
       for (int o = 0; o < 2 * W - 1; ++o)
         line[o] = digit_at(q0 + AX[a][0] * (o - (W - 1)), r0 + AX[a][1] * (o - (W - 1)));
-      if (line[W - 1] != 0) return "a legal action cell is occupied";
+      if (line[W - 1] != 0) return "a legal cell holds a stone";
       // The window starting k steps before the cell covers line[5 - k ..
       // 10 - k]; its pattern and counts slide from k = 5 down to k = 0.
       int pre_k[W], own_k[W], opp_k[W];
@@ -435,11 +435,11 @@ std::string build_one(const PosIn& in, Graph& g) {
       for (int k = 0; k < W; ++k) {
         const int pre = pre_k[k], own = own_k[k], opp = opp_k[k];
         const int post1 = T.post1[pre + T.pow3[k]][k];
-        if (post1 < 0) return "a post-placement row lost its own stone";
+        if (post1 < 0) return "internal: a placement slot has no post-placement class";
         const bool kept = own > 0 || opp > 0;
         // only a row holding a stone can name a live window
         const int64_t w = kept ? live[a].find(q0 - AX[a][0] * k, r0 - AX[a][1] * k) : -1;
-        if ((w >= 0) != kept) return "the kept-window set disagrees with the action-row walk";
+        if ((w >= 0) != kept) return "internal: a window through a stone is missing from the live set";
         max_own = std::max(max_own, own);
         max_opp = std::max(max_opp, opp);
         if (opp == 0 && own == W - 1) any_win = 1;
@@ -447,7 +447,7 @@ std::string build_one(const PosIn& in, Graph& g) {
         if (opp == 0 && own + 1 == 4) ++make4;
         if (kept) {
           const int cls = T.dec[pattern[w]][k];
-          if (cls < 0) return "decoder entry pairs a window with a slot it already occupies";
+          if (cls < 0) return "internal: an empty slot has no decoder class";
           g.dec.push_back({(int32_t)c, (int32_t)w, (int16_t)cls, (int16_t)post1});
           ++kept_rows;
           if (opp > 0 && own == 0) {
