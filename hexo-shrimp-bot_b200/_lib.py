@@ -56,6 +56,9 @@ SIGNATURES = {
     "mb_linear": "pilllpiplipilp",
     "mb_gemm_weight_image": "pllpp",
     "mb_gemm_rows": "pillppfppiplplp",
+    "mb_gemm_rows_ex": "pilllppfplpiplplplp",
+    "mb_gemm_rows_head": "pllplppllpppiplp",
+    "mb_gemm_set_plan": "ii",
     "mb_encode_positions": "lpppppppip",
     "mb_encoding_sizes": "pp",
     "mb_encoding_fill": "ppi",

@@ -4,17 +4,26 @@
 //
 //   prologue: LN      - fp32 rows -> LayerNorm (fp32 statistics) -> bf16
 //             COPY    - bf16 rows used as they are
+//             TMA     - bf16 rows loaded by the tensor memory accelerator, one
+//                       128-row x 64-column K-block per copy, already in the
+//                       MMA's swizzled layout, into a ring of K-block slots
 //             HEXMEAN - mean of the bf16 rows of a node's present hex
 //                       neighbours (six-slot int32 table, -1 = absent; fp32
 //                       sum, zero when none is present) -> bf16
-//   epilogue: STORE    - bf16 rows (optionally ReLU)
+//   epilogue: STORE    - bf16 rows (optionally ReLU, optionally plus an fp32
+//                        addend row)
 //             RESIDUAL - x_res[row] += result (fp32, in place)
 //             ADD_X    - out[row] = x[row] + result (bf16), the fused
 //                        message-passing update y = x + W mean(x[nbr]) + b
 //             RESID_LN - RESIDUAL, then up to three LayerNorms of each
 //                        updated row (bf16 outputs), from the same launch
+//             HEAD     - a decoder head's last two layers: per row
+//                        out[j] = b_out[j] + w_out[j] . relu(result +
+//                        tok[tok_idx[row]]), up to four outputs (fp32)
 //
-// K = 256 (one model width), N = 256 output columns per launch, M any.
+// K = 256 or 512 (the A tile is held whole in shared memory), N any multiple
+// of 128: a tile's N blocks (256 columns, the last one 128 when N is an odd
+// multiple of 128) run back to back on the same A tile; M any.
 // The op is HBM-bound (about 1.5-4 KB of row traffic per 131 kFLOP), so the
 // design is about keeping row bytes in flight and accesses coalesced.
 //
@@ -22,9 +31,10 @@
 // sub-partition, so every thread may hold 128 registers):
 //   warp 0      lane 0 streams pre-swizzled 64-wide K-blocks of W (32 KB,
 //               L2-resident) through a 1- or 2-stage ring with cp.async.bulk
-//               and issues the tcgen05.mma stream (M=128, N=256, K=16, bf16 x
-//               bf16 -> fp32) into a double-buffered TMEM accumulator,
-//               signalling with tcgen05.commit.
+//               and issues the tcgen05.mma stream (M=128, N=256 or 128, K=16,
+//               bf16 x bf16 -> fp32) into a double-buffered TMEM accumulator
+//               (one buffer per (tile, N block) work item), signalling with
+//               tcgen05.commit.
 //   warps 1-7   A producers (11 for the neighbour gather), three variants:
 //               staged (LayerNorm of contiguous fp32 rows): lane 1 of warp 0
 //                 bulk-copies 32-row groups (32 KB) into a 3-deep ring; warps
@@ -46,14 +56,14 @@
 //
 // Every mbarrier wait is bounded by a clock deadline; on expiry the CTA
 // records a device error, stops issuing work, and still frees its TMEM.
+#include <cuda.h>  // CUtensorMap and its encoding enums (the encoder is fetched through the runtime)
+
 #include "common.cuh"
 
 namespace mb {
 namespace sm100 {
 
 constexpr int BM = 128, BN = 256, BK = 64, KDIM = 256;
-constexpr int KBLOCKS = KDIM / BK;                 // 4
-constexpr int A_BYTES = BM * KDIM * 2;             // 64 KB
 constexpr int A_KB_BYTES = BM * BK * 2;            // 16 KB per K-block
 constexpr int W_KB_BYTES = BN * BK * 2;            // 32 KB per K-block
 constexpr int XG_ROWS = 32;                        // rows per staged group
@@ -65,12 +75,14 @@ constexpr int THREADS = 32 * 16;
 constexpr int RB = 8;                              // rows in flight per direct producer warp
 constexpr int BOX_FLOATS = 32 * 32;
 constexpr int OUT_BOX_BYTES = 32 * 32 * 2;          // 32 rows x 32 bf16 LayerNorm outputs
-constexpr int BAR_BYTES = 256;
+constexpr int BAR_BYTES = 512;
+constexpr int A_RING = 8;                          // A K-block slots of the tensor-map prologue
 constexpr long long kWaitCycles = 4000000000LL;   // ~2 s at 1.9 GHz
 
-enum Prologue { PRO_LN = 0, PRO_COPY = 1, PRO_HEXMEAN = 2 };
-enum Epilogue { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_ADD_X = 2, EPI_RESID_LN = 3 };
+enum Prologue { PRO_LN = 0, PRO_COPY = 1, PRO_HEXMEAN = 2, PRO_TMA = 3 };
+enum Epilogue { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_ADD_X = 2, EPI_RESID_LN = 3, EPI_HEAD = 4 };
 constexpr int MAX_LN = 3;
+constexpr int MAX_HEAD_OUT = 4;
 constexpr int HEX_SLOTS = 6;
 
 constexpr uint32_t ERR_TIMEOUT = 4;
@@ -118,6 +130,17 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
                : "memory");
 }
 
+// Tensor-map load of one (64-column, 128-row) box of a 2-D bf16 tensor into
+// shared memory (128-byte swizzle), completing on `bar`. Rows past the
+// tensor's end read as zero. x (the column) is a multiple of 64.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
 // 16-byte cp.async (L2 only) that zero-fills the destination when `live` is
 // false, and the group commit / wait that orders a warp's boxes.
 __device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, bool live) {
@@ -140,14 +163,16 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
 
 // Instruction descriptor, kind::f16: fp32 accumulate, bf16 A and B, both
 // K-major, N >> 3 at bit 17, M >> 4 at bit 24.
-constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                           ((uint32_t)(BM >> 4) << 24);
+__host__ __device__ constexpr uint32_t make_idesc(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
 
-__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                     uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accumulate)
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
@@ -189,7 +214,8 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-struct Params {
+struct alignas(64) Params {
+  CUtensorMap tmap_x;   // PRO_TMA: the (m, K) bf16 input rows, 64 x 128 boxes, 128-byte swizzle
   const void* x;        // prologue input rows (fp32 for LN, bf16 for COPY)
   int64_t ldx;
   const float* gamma;   // LN
@@ -212,43 +238,82 @@ struct Params {
   void* ln_out[MAX_LN];
   int ln_dtype[MAX_LN];
   int64_t ln_ld[MAX_LN];
+  // N blocks per tile (256 columns each; the last one n_last = 128 or 256)
+  int n_blocks;
+  int n_last;
+  // EPI_STORE: optional fp32 addend rows (add + row * ld_add + column)
+  const float* add;
+  int64_t ld_add;
+  // EPI_HEAD: per-row second operand tok[tok_idx[row]] (bf16 rows), the
+  // output layer w_out (n_out x N fp32, row-major), b_out, fp32 outputs
+  const __nv_bfloat16* tok;
+  int64_t ld_tok;
+  int64_t n_tok;
+  const int64_t* tok_idx;
+  const float* w_out;
+  const float* b_out;
+  int n_out;
+  float* head_out;
+  int64_t ld_head;
 };
 
 // Shared-memory plan of one variant (all region offsets 1024-byte aligned).
-template <int PRO, int EPI, bool XS>
+template <int PRO, int EPI, bool XS, int KB, bool WS>
 struct Plan {
   // The residual epilogues stream the residual through a shared-memory ring,
   // which takes the second A buffer's space (the epilogue, not the MMA,
-  // bounds these variants).
+  // bounds these variants). A K = 512 tile (128 KB) is single-buffered.
   static constexpr bool RESID = EPI == EPI_RESIDUAL || EPI == EPI_RESID_LN;
-  static constexpr int A_BUFS = (XS || RESID) ? 1 : 2;
+  static_assert(KB == 4 || KB == 8, "K must be 256 or 512");
+  static_assert(KB == 4 || ((PRO == PRO_COPY || PRO == PRO_TMA) && EPI != EPI_RESID_LN), "K = 512 takes bf16 rows");
+  static constexpr int A_BYTES = BM * BK * 2 * KB;
+  // Weight-stationary plan (WS): the CTA holds one whole N block of W (K =
+  // 256: 128 KB) and runs every one of its row tiles against it before the
+  // next N block, so W crosses from L2 once per CTA and N block instead of
+  // once per tile; its A tiles are re-read for each N block.
+  static_assert(!WS || (KB == 4 && !RESID && !XS && (PRO == PRO_TMA || PRO == PRO_LN)),
+                "the weight-stationary plan serves K = 256 bf16-output launches");
+  static constexpr int A_BUFS = (XS || RESID || KB > 4 || WS) ? 1 : 2;
+  // PRO_TMA keeps K-block slots in a ring instead of whole tiles: a slot is
+  // refilled as soon as the MMAs that read it finish.
+  static constexpr bool RING_A = PRO == PRO_TMA;
+  static constexpr int A_SLOTS = RING_A ? ((RESID || WS) ? KB : A_RING) : 0;
+  static_assert(!RING_A || A_SLOTS >= KB, "a tile's K-blocks must fit the ring");
+  static constexpr int A_SPACE = RING_A ? A_SLOTS * A_KB_BYTES : A_BUFS * A_BYTES;
+  // bf16-output epilogues stage 32 x 32 boxes for whole-segment stores
+  static constexpr bool OUT_BOXES = EPI == EPI_RESID_LN || EPI == EPI_STORE || EPI == EPI_ADD_X;
   // W K-blocks in flight. The residual epilogues are long enough to hide a
   // one-stage W stream; the freed 32 KB hold the output staging boxes.
   static constexpr int W_STAGES = RESID ? 1 : 2;
   // Residual boxes (32 rows x 32 fp32 columns, 4 KB) per epilogue warp.
-  static constexpr int RING = 3;
+  static constexpr int RING = KB > 4 ? 1 : 3;
   // Warps writing the A tile (1..PRODUCERS) and draining TMEM (the rest).
   // The neighbour-gather prologue is latency-bound, so it gets more warps and
   // the epilogue four (one per TMEM lane quadrant, all 256 columns each).
-  static constexpr int PRODUCERS = PRO == PRO_HEXMEAN ? 11 : 7;
+  static constexpr int PRODUCERS = PRO == PRO_HEXMEAN ? 11 : 7;  // idle under PRO_TMA
   static constexpr int EPI_WARPS = 16 - 1 - PRODUCERS;
   static constexpr int A_OFF = 0;
-  static constexpr int W_OFF = A_OFF + A_BUFS * A_BYTES;
-  static constexpr int X_OFF = W_OFF + W_STAGES * W_KB_BYTES;
-  static constexpr int E_OFF = X_OFF + (XS ? X_STAGES * XG_BYTES : 0);
+  static constexpr int W_OFF = A_OFF + A_SPACE;
+  static constexpr int X_OFF = W_OFF + (WS ? KB : W_STAGES) * W_KB_BYTES;
+  // staged LayerNorm rows: 32-row groups in flight (two when the output boxes
+  // need the space)
+  static constexpr int XSTAGES = OUT_BOXES ? 2 : X_STAGES;
+  static constexpr int E_OFF = X_OFF + (XS ? XSTAGES * XG_BYTES : 0);
   static constexpr int OUT_OFF = E_OFF + (RESID ? EPILOGUE * RING * BOX_FLOATS * 4 : 0);
   // bias and the LayerNorms' gamma / beta, copied once per CTA (uniform
   // reads in the epilogue, kept out of the busy L1 miss path)
-  static constexpr int PAR_OFF = OUT_OFF + (EPI == EPI_RESID_LN ? EPILOGUE * OUT_BOX_BYTES : 0);
+  static constexpr int PAR_OFF = OUT_OFF + (OUT_BOXES ? EPILOGUE * OUT_BOX_BYTES : 0);
   static constexpr int RED_OFF = PAR_OFF + (RESID ? (1 + 2 * MAX_LN) * BN * 4 : 0);
-  static constexpr int BAR_OFF = RED_OFF + (EPI == EPI_RESID_LN ? 4 * 64 * 4 : 0);
+  static constexpr int BAR_OFF = RED_OFF + (EPI == EPI_RESID_LN ? 4 * 64 * 4 : 0) +
+                                 (EPI == EPI_HEAD ? 4 * MAX_HEAD_OUT * 32 * 4 : 0);
   static constexpr int SMEM = BAR_OFF + BAR_BYTES + 1024 /*alignment slack*/;
   static_assert(SMEM <= 232448, "shared memory plan exceeds 227 KB");
+  static_assert(PRO != PRO_TMA || EPI != EPI_RESID_LN, "the LayerNorm epilogue keeps its cp.async producers");
 };
 
-template <int PRO, int EPI, bool XS>
-__global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
-  using L = Plan<PRO, EPI, XS>;
+template <int PRO, int EPI, bool XS, int KB = 4, bool WS = false>
+__global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const __grid_constant__ Params p) {
+  using L = Plan<PRO, EPI, XS, KB, WS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* a_smem = smem + L::A_OFF;
@@ -256,31 +321,39 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
   uint8_t* x_smem = smem + L::X_OFF;
   float* e_smem = reinterpret_cast<float*>(smem + L::E_OFF);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
-  uint64_t* a_full = bars;            // [2]
-  uint64_t* a_empty = bars + 2;       // [2]
-  uint64_t* w_full = bars + 4;        // [2]
-  uint64_t* w_empty = bars + 6;       // [2]
-  uint64_t* t_full = bars + 8;        // [2]
-  uint64_t* t_empty = bars + 10;      // [2]
-  uint64_t* x_full = bars + 12;       // [3]
-  uint64_t* x_empty = bars + 15;      // [3]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
-  volatile int* abort = reinterpret_cast<volatile int*>(bars + 19);
+  uint64_t* a_full = bars;            // [A_RING]: tiles (2) or K-block slots
+  uint64_t* a_empty = bars + 8;       // [A_RING]
+  uint64_t* w_full = bars + 16;       // [2]
+  uint64_t* w_empty = bars + 18;      // [2]
+  uint64_t* t_full = bars + 20;       // [2]
+  uint64_t* t_empty = bars + 22;      // [2]
+  uint64_t* x_full = bars + 24;       // [3]
+  uint64_t* x_empty = bars + 27;      // [3]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 30);
+  volatile int* abort = reinterpret_cast<volatile int*>(bars + 31);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n_tiles = (p.m + BM - 1) / BM;
   const int64_t my_tiles = n_tiles > blockIdx.x ? (n_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  // A units: the A tiles the producers write, in MMA order. Without WS one per
+  // tile, shared by its N blocks (work items t * n_blocks + nb); with WS one
+  // per work item, N-block-major (item nb * my_tiles + t).
+  const int nbn = p.n_blocks;
+  const int64_t n_units = WS ? my_tiles * nbn : my_tiles;
+  auto unit_tile = [&](int64_t u) -> int64_t { return WS ? u % my_tiles : u; };
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(smem_u32(&a_full[i]), L::PRODUCERS);
+    for (int i = 0; i < A_RING; ++i) {
+      mbar_init(smem_u32(&a_full[i]), L::RING_A ? 1 : L::PRODUCERS);
       mbar_init(smem_u32(&a_empty[i]), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&w_full[i]), 1);
       mbar_init(smem_u32(&w_empty[i]), 1);
       mbar_init(smem_u32(&t_full[i]), 1);
       mbar_init(smem_u32(&t_empty[i]), L::EPI_WARPS);
     }
-    for (int i = 0; i < X_STAGES; ++i) {
+    for (int i = 0; i < L::XSTAGES; ++i) {
       mbar_init(smem_u32(&x_full[i]), 1);
       mbar_init(smem_u32(&x_empty[i]), L::PRODUCERS);
     }
@@ -313,50 +386,120 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
   if (warp == 0) {
     // ------------------------------------- W stream + MMA issuer (1 lane)
     if (lane == 0) {
-      const uint64_t total_kb = (uint64_t)my_tiles * KBLOCKS;
+      const uint64_t total_kb = WS ? 0 : (uint64_t)my_tiles * nbn * KB;
+      const uint8_t* wimg = reinterpret_cast<const uint8_t*>(p.w_img);
       uint64_t issued = 0;
       auto issue_w = [&](uint64_t upto) -> bool {
         for (; issued < upto && issued < total_kb; ++issued) {
           const uint32_t s = issued % L::W_STAGES, ph = (issued / L::W_STAGES) & 1;
           if (!mbar_wait(smem_u32(&w_empty[s]), ph ^ 1, abort)) return false;
-          mbar_expect_tx(smem_u32(&w_full[s]), W_KB_BYTES);
-          bulk_g2s(smem_u32(w_smem + s * W_KB_BYTES),
-                   reinterpret_cast<const uint8_t*>(p.w_img) + (size_t)(issued % KBLOCKS) * W_KB_BYTES, W_KB_BYTES,
+          const int nb = (int)((issued / KB) % nbn), kb = (int)(issued % KB);
+          const uint32_t bytes = (uint32_t)(nb == nbn - 1 ? p.n_last : BN) * 128u;
+          mbar_expect_tx(smem_u32(&w_full[s]), bytes);
+          bulk_g2s(smem_u32(w_smem + s * W_KB_BYTES), wimg + (size_t)nb * BN * KB * 128 + (size_t)kb * bytes, bytes,
                    smem_u32(&w_full[s]));
         }
         return true;
       };
-      bool ok = issue_w(L::W_STAGES);
-      uint64_t used = 0;
-      for (int64_t t = 0; ok && t < my_tiles && !*abort; ++t) {
-        const uint32_t tb = t & 1, tph = (t >> 1) & 1;
-        const uint32_t ab = t % L::A_BUFS, aph = (t / L::A_BUFS) & 1;
-        if (!mbar_wait(smem_u32(&t_empty[tb]), tph ^ 1, abort)) break;
-        if (!mbar_wait(smem_u32(&a_full[ab]), aph, abort)) break;
+      // WS: the whole N block nb into shared memory once the previous block's
+      // MMAs are done with it
+      auto load_block = [&](int nb) -> bool {
+        if (nb > 0 && !mbar_wait(smem_u32(&w_empty[0]), (nb - 1) & 1, abort)) return false;
+        const uint32_t kb_bytes = (uint32_t)(nb == nbn - 1 ? p.n_last : BN) * 128u;
+        mbar_expect_tx(smem_u32(&w_full[0]), kb_bytes * KB);
+        for (int kb = 0; kb < KB; ++kb)
+          bulk_g2s(smem_u32(w_smem + kb * kb_bytes), wimg + (size_t)nb * BN * KB * 128 + (size_t)kb * kb_bytes,
+                   kb_bytes, smem_u32(&w_full[0]));
+        if (!mbar_wait(smem_u32(&w_full[0]), nb & 1, abort)) return false;
         tc_fence_after();
-        const uint32_t d = tmem_base + tb * BN;
-        for (int kb = 0; kb < KBLOCKS; ++kb, ++used) {
-          const uint32_t s = used % L::W_STAGES, ph = (used / L::W_STAGES) & 1;
-          if (!mbar_wait(smem_u32(&w_full[s]), ph, abort)) { ok = false; break; }
+        return true;
+      };
+      bool ok = WS ? true : issue_w(L::W_STAGES);
+      uint64_t used = 0;
+      for (int64_t u = 0; ok && u < n_units && !*abort; ++u) {
+        const int64_t t = unit_tile(u);
+        const uint32_t ab = u % L::A_BUFS, aph = (u / L::A_BUFS) & 1;
+        const int nb0 = WS ? (int)(u / my_tiles) : 0, nb1 = WS ? nb0 + 1 : nbn;
+        if constexpr (WS) {
+          if (t == 0 && !load_block(nb0)) break;
+        }
+        if constexpr (!L::RING_A) {
+          if (!mbar_wait(smem_u32(&a_full[ab]), aph, abort)) break;
           tc_fence_after();
-          const uint32_t a0 = smem_u32(a_smem + ab * A_BYTES + kb * A_KB_BYTES);
-          const uint32_t b0 = smem_u32(w_smem + s * W_KB_BYTES);
+        }
+        for (int nb = nb0; ok && nb < nb1; ++nb) {
+          const int64_t item = WS ? u : t * nbn + nb;
+          const uint32_t tb = item & 1, tph = (item >> 1) & 1;
+          if (!mbar_wait(smem_u32(&t_empty[tb]), tph ^ 1, abort)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d = tmem_base + tb * BN;
+          const int rows = nb == nbn - 1 ? p.n_last : BN;
+          const uint32_t idesc = make_idesc(rows);
+          for (int kb = 0; kb < KB; ++kb, ++used) {
+            const uint32_t s = used % L::W_STAGES, ph = (used / L::W_STAGES) & 1;
+            uint32_t a0;
+            uint64_t aseq = 0;
+            if constexpr (L::RING_A) {
+              aseq = (uint64_t)u * KB + kb;  // this K-block's slot in the ring
+              if (nb == nb0 && !mbar_wait(smem_u32(&a_full[aseq % L::A_SLOTS]), (aseq / L::A_SLOTS) & 1, abort)) {
+                ok = false;
+                break;
+              }
+              a0 = smem_u32(a_smem + (aseq % L::A_SLOTS) * A_KB_BYTES);
+            } else {
+              a0 = smem_u32(a_smem + ab * L::A_BYTES + kb * A_KB_BYTES);
+            }
+            uint32_t b0;
+            if constexpr (WS) {
+              tc_fence_after();
+              b0 = smem_u32(w_smem + kb * rows * 128);
+            } else {
+              if (!mbar_wait(smem_u32(&w_full[s]), ph, abort)) { ok = false; break; }
+              tc_fence_after();
+              b0 = smem_u32(w_smem + s * W_KB_BYTES);
+            }
 #pragma unroll
-          for (int j = 0; j < BK / 16; ++j)
-            umma(d, smem_desc(a0 + j * 32), smem_desc(b0 + j * 32), (kb | j) != 0);
-          umma_commit(smem_u32(&w_empty[s]));  // frees the W stage once these MMAs finish
-          // request block used + 1: with two stages it refills the stage the
-          // previous block used (its MMAs are older, so the wait rarely
-          // blocks); with one stage it waits for these MMAs
-          if (!issue_w(used + 2)) { ok = false; break; }
+            for (int j = 0; j < BK / 16; ++j)
+              umma(d, smem_desc(a0 + j * 32), smem_desc(b0 + j * 32), idesc, (kb | j) != 0);
+            if constexpr (!WS) umma_commit(smem_u32(&w_empty[s]));  // frees the W stage once these MMAs finish
+            if constexpr (L::RING_A) {
+              if (nb == nb1 - 1) umma_commit(smem_u32(&a_empty[aseq % L::A_SLOTS]));  // the slot may be refilled
+            }
+            // request block used + 1: with two stages it refills the stage the
+            // previous block used (its MMAs are older, so the wait rarely
+            // blocks); with one stage it waits for these MMAs
+            if (!WS && !issue_w(used + 2)) { ok = false; break; }
+          }
+          if (!ok) break;
+          umma_commit(smem_u32(&t_full[tb]));
         }
         if (!ok) break;
-        umma_commit(smem_u32(&a_empty[ab]));  // the A tile may be rewritten once these MMAs finish
-        umma_commit(smem_u32(&t_full[tb]));
+        if constexpr (!L::RING_A) umma_commit(smem_u32(&a_empty[ab]));  // the A tile may be rewritten
+        if constexpr (WS) {
+          if (t == my_tiles - 1) umma_commit(smem_u32(&w_empty[0]));  // this N block's W may be replaced
+        }
       }
     }
   }
-  if (XS && warp == 0) {
+  if (L::RING_A && warp == 0) {
+    // ------------------------ tensor-map A loads: K-blocks into the ring (lane 1)
+    if (lane == 1) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tmap_x)) : "memory");
+      for (int64_t u = 0; u < n_units && !*abort; ++u) {
+        const int64_t tile = blockIdx.x + unit_tile(u) * gridDim.x;
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb) {
+          const uint64_t aseq = (uint64_t)u * KB + kb;
+          const uint32_t slot = aseq % L::A_SLOTS;
+          if (!mbar_wait(smem_u32(&a_empty[slot]), ((aseq / L::A_SLOTS) & 1) ^ 1, abort)) { ok = false; break; }
+          mbar_expect_tx(smem_u32(&a_full[slot]), A_KB_BYTES);
+          tma_load_2d(smem_u32(a_smem + slot * A_KB_BYTES), &p.tmap_x, kb * BK, (int)(tile * BM),
+                      smem_u32(&a_full[slot]));
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (XS && warp == 0) {
     // ----------------------- staged rows: bulk-copy loader (warp 0, lane 1)
     if (lane == 1) {
       const float* x = reinterpret_cast<const float*>(p.x);
@@ -365,7 +508,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
         bool ok = true;
         for (int grp = 0; grp < BM / XG_ROWS; ++grp) {
           const uint64_t seq = (uint64_t)t * (BM / XG_ROWS) + grp;
-          const uint32_t s = seq % X_STAGES, ph = (seq / X_STAGES) & 1;
+          const uint32_t s = seq % L::XSTAGES, ph = (seq / L::XSTAGES) & 1;
           if (!mbar_wait(smem_u32(&x_empty[s]), ph ^ 1, abort)) { ok = false; break; }
           const int64_t row0 = tile * BM + grp * XG_ROWS;
           int64_t rows = p.m - row0;
@@ -378,7 +521,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
         if (!ok) break;
       }
     }
-  } else if (warp >= 1 && warp < 1 + L::PRODUCERS) {
+  } else if (!L::RING_A && warp >= 1 && warp < 1 + L::PRODUCERS) {
     // ------------------------------------------------------ A producers
     const int kb = lane >> 3, chunk = lane & 7;  // lane owns columns [8*lane, 8*lane+8)
     // LayerNorm of NR rows at once: the NR warp reductions are interleaved so
@@ -429,7 +572,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
         bool ok = true;
         for (int grp = 0; grp < BM / XG_ROWS; ++grp) {
           const uint64_t seq = (uint64_t)t * (BM / XG_ROWS) + grp;
-          const uint32_t s = seq % X_STAGES, ph = (seq / X_STAGES) & 1;
+          const uint32_t s = seq % L::XSTAGES, ph = (seq / L::XSTAGES) & 1;
           if (!mbar_wait(smem_u32(&x_full[s]), ph, abort)) { ok = false; break; }
           if (grp == 0 && !mbar_wait(smem_u32(&a_empty[0]), (t & 1) ^ 1, abort)) { ok = false; break; }
           const float* stage = reinterpret_cast<const float*>(x_smem + s * XG_BYTES);
@@ -464,10 +607,10 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
       }
     } else {
       const int pw = warp - 1;  // rows pw, pw + PRODUCERS, ... of each tile
-      for (int64_t t = 0; t < my_tiles && !*abort; ++t) {
-        const int64_t tile = blockIdx.x + t * gridDim.x;
-        const uint32_t ab = t % L::A_BUFS, aph = (t / L::A_BUFS) & 1;
-        uint8_t* abuf = a_smem + ab * A_BYTES;
+      for (int64_t u = 0; u < n_units && !*abort; ++u) {
+        const int64_t tile = blockIdx.x + unit_tile(u) * gridDim.x;
+        const uint32_t ab = u % L::A_BUFS, aph = (u / L::A_BUFS) & 1;
+        uint8_t* abuf = a_smem + ab * L::A_BYTES;
         if constexpr (PRO == PRO_COPY) {
           // bf16 rows need no arithmetic: each lane cp.asyncs its 16-byte
           // chunk of every row of the warp straight into the swizzled slot
@@ -479,8 +622,10 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
           for (int r = pw; r < BM; r += L::PRODUCERS) {
             const int64_t row = tile * BM + r;
             const bool live = row < p.m;
-            cp_async16_zfill(smem_u32(abuf + kb * A_KB_BYTES + r * 128 + ((chunk ^ (r & 7)) << 4)),
-                             xb + (live ? row : 0) * p.ldx + lane * 8, live);
+#pragma unroll
+            for (int i = 0; i < KB / 4; ++i)  // K-blocks kb, kb + 4: 64-column strips of the row
+              cp_async16_zfill(smem_u32(abuf + (kb + 4 * i) * A_KB_BYTES + r * 128 + ((chunk ^ (r & 7)) << 4)),
+                               xb + (live ? row : 0) * p.ldx + (kb + 4 * i) * BK + chunk * 8, live);
           }
           cp_async_commit();
           cp_async_wait<0>();
@@ -619,9 +764,11 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
     if constexpr (L::RESID) {
       for (int64_t k = 0; k < RING; ++k) issue_box(k);
     }
-    for (int64_t t = 0; t < my_tiles && !*abort; ++t) {
+    for (int64_t it = 0; it < my_tiles * nbn && !*abort; ++it) {  // nbn = 1 for the residual epilogues
+      const int64_t t = WS ? it % my_tiles : it / nbn;
+      const int nb = (int)(WS ? it / my_tiles : it % nbn);
       const int64_t tile = blockIdx.x + t * gridDim.x;
-      const uint32_t tb = t & 1, tph = (t >> 1) & 1;
+      const uint32_t tb = it & 1, tph = (it >> 1) & 1;
       if (!mbar_wait(smem_u32(&t_full[tb]), tph, abort)) break;
       tc_fence_after();
       const int64_t row0 = tile * BM + q * 32;  // this warp's 32 rows
@@ -746,16 +893,97 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&t_empty[tb]));
-      } else {
+      } else if constexpr (EPI == EPI_HEAD) {
+        // One N block of width cols (128 or 256): each column half takes
+        // cols / 2 columns of its rows, v = relu(acc + bias + tok[tok_idx[row]]),
+        // and its partial dot products with the output layer's rows; the
+        // halves meet in shared memory and half 0 writes the outputs.
+        const int cols = p.n_last;
+        const int span = cols / 2;
+        const int cbeg = half * span;
+        float part[MAX_HEAD_OUT] = {};
+        int64_t trow = -1;
+        if (row < p.m) {
+          trow = p.tok_idx[row];
+          if (trow < 0 || trow >= p.n_tok) {
+            report(ERR_INDEX);
+            trow = -1;
+          }
+        }
 #pragma unroll 1
-      for (int c0 = half * (BN / PARTS); c0 < (half + 1) * (BN / PARTS); c0 += 32) {
+        for (int c0 = cbeg; c0 < cbeg + span; c0 += 32) {
+          float v[32];
+          tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + tb * BN + c0, v);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 bb = p.bias ? __ldg(reinterpret_cast<const float4*>(p.bias + c0) + i) : make_float4(0, 0, 0, 0);
+            v[4 * i] += bb.x; v[4 * i + 1] += bb.y; v[4 * i + 2] += bb.z; v[4 * i + 3] += bb.w;
+          }
+          if (trow >= 0) {
+            const __nv_bfloat16* tr = p.tok + trow * p.ld_tok + c0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              float a[8];
+              load_vec<8>(tr + 8 * i, a);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) v[8 * i + j] += a[j];
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i], 0.f);
+#pragma unroll
+          for (int o = 0; o < MAX_HEAD_OUT; ++o) {
+            if (o >= p.n_out) break;
+            const float4* w4 = reinterpret_cast<const float4*>(p.w_out + (int64_t)o * cols + c0);
+            float acc = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 w = __ldg(w4 + i);
+              acc += v[4 * i] * w.x + v[4 * i + 1] * w.y + v[4 * i + 2] * w.z + v[4 * i + 3] * w.w;
+            }
+            part[o] += acc;
+          }
+        }
+        float* red = reinterpret_cast<float*>(smem + L::RED_OFF) + q * (MAX_HEAD_OUT * 32);
+        if (half == 1) {
+#pragma unroll
+          for (int o = 0; o < MAX_HEAD_OUT; ++o) red[o * 32 + lane] = part[o];
+        }
+        asm volatile("bar.sync %0, 64;" ::"r"(1 + q) : "memory");
+        if (half == 0 && row < p.m) {
+#pragma unroll
+          for (int o = 0; o < MAX_HEAD_OUT; ++o)
+            if (o < p.n_out) p.head_out[row * p.ld_head + o] = part[o] + red[o * 32 + lane] + p.b_out[o];
+        }
+        asm volatile("bar.sync %0, 64;" ::"r"(1 + q) : "memory");  // the partials are read before the next tile
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&t_empty[tb]));
+      } else {
+      const int cols = nb == nbn - 1 ? p.n_last : BN;
+      const int cend = (half + 1) * (BN / PARTS) < cols ? (half + 1) * (BN / PARTS) : cols;
+      const int nr = (int)(p.m - row0 < 32 ? (p.m - row0 < 0 ? 0 : p.m - row0) : 32);  // live rows of the warp
+      uint4* sb = reinterpret_cast<uint4*>(smem + L::OUT_OFF + ew * OUT_BOX_BYTES);
+#pragma unroll 1
+      for (int c0 = half * (BN / PARTS); c0 < cend; c0 += 32) {
         float v[32];
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + tb * BN + c0, v);
+        const int oc = nb * BN + c0;  // output column
         if (p.bias) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + c0) + i);
+            const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + oc) + i);
             v[4 * i] += bb.x; v[4 * i + 1] += bb.y; v[4 * i + 2] += bb.z; v[4 * i + 3] += bb.w;
+          }
+        }
+        if constexpr (EPI == EPI_STORE) {
+          if (p.add && row < p.m) {
+            const float4* ar = reinterpret_cast<const float4*>(p.add + row * p.ld_add + oc);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 a4 = __ldg(ar + i);
+              v[4 * i] += a4.x; v[4 * i + 1] += a4.y; v[4 * i + 2] += a4.z; v[4 * i + 3] += a4.w;
+            }
           }
         }
         if (p.relu) {
@@ -763,8 +991,8 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
           for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i], 0.f);
         }
         if constexpr (EPI == EPI_STORE || EPI == EPI_ADD_X) {
-          if (row < p.m) {
-            if constexpr (EPI == EPI_ADD_X) {
+          if constexpr (EPI == EPI_ADD_X) {
+            if (row < p.m) {
               const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(p.x) + row * p.ldx + c0;
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
@@ -774,9 +1002,28 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
                 for (int j = 0; j < 8; ++j) v[8 * i + j] += a[j];
               }
             }
-            __nv_bfloat16* o = p.out + row * p.ldo + c0;
+          }
+          // Through the warp's staging box (32 rows of 64 bytes, 16-byte piece
+          // j of row r at j ^ ((r >> 1) & 3): the row-wise writes and the
+          // piece-wise reads are both conflict-free), so that each store
+          // writes whole 64-byte row segments, 8 rows at a time.
+          __syncwarp();  // the previous chunk's reads of the box are done
 #pragma unroll
-            for (int i = 0; i < 4; ++i) store_vec<8>(o + 8 * i, v + 8 * i);
+          for (int j = 0; j < 4; ++j) {
+            const float* x = v + 8 * j;
+            uint4 w;
+            __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+            sb[lane * 4 + (j ^ ((lane >> 1) & 3))] = w;
+          }
+          __syncwarp();
+          __nv_bfloat16* d = p.out + row0 * p.ldo + oc + (lane & 3) * 8;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int r = 8 * i + (lane >> 2);
+            const uint4 w = sb[r * 4 + ((lane & 3) ^ ((r >> 1) & 3))];
+            if (r < nr) *reinterpret_cast<uint4*>(d + r * p.ldo) = w;
           }
         }
       }
@@ -798,8 +1045,10 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const Params p) {
 }
 
 // Pre-swizzle W (N x K row-major bf16) into the image the kernel streams:
-// K-block kb holds rows n = 0..BN-1, 128 bytes each, 16-byte chunk c of row n
-// stored at chunk c ^ (n % 8).
+// N block nb (rows nb * 256 onwards, 256 of them or 128 for a short last
+// block) holds its K-blocks one after another, K-block kb holding the
+// block's rows, 128 bytes each, 16-byte chunk c of row r stored at chunk
+// c ^ (r % 8).
 __global__ void swizzle_weight_kernel(const __nv_bfloat16* __restrict__ w, int64_t n, int64_t k,
                                       __nv_bfloat16* __restrict__ img) {
   const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;  // one 16-byte chunk
@@ -807,12 +1056,82 @@ __global__ void swizzle_weight_kernel(const __nv_bfloat16* __restrict__ w, int64
   if (idx >= chunks) return;
   const int64_t row = idx / (k / 8), kc = idx % (k / 8);
   const int64_t kb = kc / 8, c = kc % 8;
+  const int64_t nb = row / BN, r = row % BN;
+  const int64_t rows_in_block = n - nb * BN < BN ? n - nb * BN : BN;
   const uint4 val = reinterpret_cast<const uint4*>(w + row * k)[kc];
-  uint8_t* dst = reinterpret_cast<uint8_t*>(img) + kb * (n * 128) + row * 128 + ((c ^ (row & 7)) << 4);
+  uint8_t* dst = reinterpret_cast<uint8_t*>(img) + nb * BN * k * 2 + kb * (rows_in_block * 128) + r * 128 +
+                 ((c ^ (r & 7)) << 4);
   *reinterpret_cast<uint4*>(dst) = val;
 }
 
 static int g_num_sms = 0;
+
+static int num_sms() {
+  if (g_num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_num_sms <= 0) g_num_sms = 148;
+  }
+  return g_num_sms;
+}
+
+// cuTensorMapEncodeTiled, fetched once through the runtime (no link-time
+// dependency on the driver library).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<EncodeTiledFn>(f);
+  }();
+  return fn;
+}
+
+// The (m, k) bf16 rows at x (leading dim ldx) as a tensor map of 64-column x
+// 128-row boxes in the MMA's 128-byte-swizzled K-major layout.
+static bool encode_rows_map(CUtensorMap* map, const void* x, int64_t m, int64_t k, int64_t ldx) {
+  EncodeTiledFn encode = encode_tiled();
+  if (!encode) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
+  const cuuint64_t strides[1] = {(cuuint64_t)(ldx * 2)};
+  const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)BM};
+  const cuuint32_t elem[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, elem,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// One persistent CTA per SM (or per tile when there are fewer tiles).
+template <int PRO, int EPI, bool XS, int KB, bool WS = false>
+static int launch_rowgemm(const Params& prm, cudaStream_t s, const char* what) {
+  constexpr int smem_bytes = Plan<PRO, EPI, XS, KB, WS>::SMEM;
+  auto kern = rowgemm_kernel<PRO, EPI, XS, KB, WS>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+  const int64_t tiles = cdiv(prm.m, BM);
+  const int grid = (int)(tiles < num_sms() ? tiles : num_sms());
+  kern<<<grid, THREADS, smem_bytes, s>>>(prm);
+  return launch_status(what);
+}
+
+// Plan choices of the bf16-output launches: 0 = weights streamed per tile,
+// 1 = weight-stationary (the default for the plain projections), 2 (LayerNorm
+// prologue only) = per-row loads instead of staged 32-row groups.
+static int g_store_plan = 1;
+static int g_ln_plan = 2;
+
+static Params base_params() {
+  Params prm{};
+  prm.n_blocks = 1;
+  prm.n_last = BN;
+  return prm;
+}
 
 }  // namespace sm100
 }  // namespace mb
@@ -823,8 +1142,9 @@ extern "C" {
 
 int mb_gemm_weight_image(const void* w, int64_t n, int64_t k, void* image, void* stream) {
   MB_REQUIRE(w && image, "gemm_weight_image: null pointer");
-  MB_REQUIRE(n == sm100::BN && k == sm100::KDIM, "gemm_weight_image: supports N=%d, K=%d (got %lld x %lld)",
-             sm100::BN, sm100::KDIM, (long long)n, (long long)k);
+  MB_REQUIRE(n >= 128 && n % 128 == 0 && (k == 256 || k == 512),
+             "gemm_weight_image: supports N a multiple of 128 and K 256 or 512 (got %lld x %lld)", (long long)n,
+             (long long)k);
   MB_REQUIRE(aligned(w, 16) && aligned(image, 16), "gemm_weight_image: pointers must be 16-byte aligned");
   const int64_t chunks = n * k / 8;
   sm100::swizzle_weight_kernel<<<(unsigned)cdiv(chunks, 256), 256, 0, as_stream(stream)>>>(
@@ -832,51 +1152,120 @@ int mb_gemm_weight_image(const void* w, int64_t n, int64_t k, void* image, void*
   return launch_status("gemm_weight_image");
 }
 
-int mb_gemm_rows(const void* x, int x_dtype, int64_t ldx, int64_t m, const float* gamma, const float* beta, float eps,
-                 const void* w_image, const float* bias, int relu, void* out, int64_t ldo, float* residual,
-                 int64_t ldr, void* stream) {
+int mb_gemm_rows_ex(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k, const float* gamma,
+                    const float* beta, float eps, const void* w_image, int64_t n, const float* bias, int relu,
+                    const float* add, int64_t ld_add, void* out, int64_t ldo, float* residual, int64_t ldr,
+                    void* stream) {
   using namespace sm100;
   MB_REQUIRE(valid_dtype(x_dtype), "gemm_rows: bad dtype");
   MB_REQUIRE(m >= 0, "gemm_rows: negative m");
+  MB_REQUIRE(k == 256 || k == 512, "gemm_rows: K must be 256 or 512 (got %lld)", (long long)k);
+  MB_REQUIRE(n >= 128 && n % 128 == 0, "gemm_rows: N must be a positive multiple of 128 (got %lld)", (long long)n);
   if (m == 0) return MB_OK;
   MB_REQUIRE(x && w_image, "gemm_rows: null pointer");
   const bool ln = gamma != nullptr;
-  MB_REQUIRE(!ln || (x_dtype == MB_F32 && beta), "gemm_rows: the LayerNorm prologue takes fp32 rows and beta");
+  MB_REQUIRE(!ln || (x_dtype == MB_F32 && beta && k == KDIM),
+             "gemm_rows: the LayerNorm prologue takes fp32 rows of width 256 and beta");
   MB_REQUIRE(ln || x_dtype == MB_BF16, "gemm_rows: without LayerNorm the rows must be bf16");
   MB_REQUIRE((out != nullptr) != (residual != nullptr), "gemm_rows: exactly one of out / residual");
-  MB_REQUIRE(aligned(x, 16) && (ldx * dtype_size(x_dtype)) % 16 == 0, "gemm_rows: x rows must be 16-byte aligned");
-  MB_REQUIRE(!out || (aligned(out, 16) && (ldo * 2) % 16 == 0), "gemm_rows: out rows must be 16-byte aligned");
-  MB_REQUIRE(!residual || (aligned(residual, 16) && (ldr * 4) % 16 == 0),
-             "gemm_rows: residual rows must be 16-byte aligned");
+  MB_REQUIRE(ldx >= k && aligned(x, 16) && (ldx * dtype_size(x_dtype)) % 16 == 0,
+             "gemm_rows: x rows must be 16-byte aligned");
+  MB_REQUIRE(!out || (ldo >= n && aligned(out, 16) && (ldo * 2) % 16 == 0),
+             "gemm_rows: out rows must be 16-byte aligned");
+  MB_REQUIRE(!residual || (n == BN && ldr >= BN && aligned(residual, 16) && (ldr * 4) % 16 == 0),
+             "gemm_rows: the residual update takes N = 256 and 16-byte aligned fp32 rows");
+  MB_REQUIRE(!add || (out && ld_add >= n && aligned(add, 16) && (ld_add * 4) % 16 == 0),
+             "gemm_rows: the addend takes a bf16 output and 16-byte aligned fp32 rows");
+  MB_REQUIRE(!(ln && residual), "gemm_rows: the LayerNorm prologue writes a bf16 output");
   MB_REQUIRE(aligned(w_image, 16), "gemm_rows: weight image must be 16-byte aligned");
   MB_REQUIRE(!bias || aligned(bias, 16), "gemm_rows: bias must be 16-byte aligned");
-  if (g_num_sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (g_num_sms <= 0) g_num_sms = 148;
-  }
-  Params prm{x, ldx, gamma, beta, eps, (const __nv_bfloat16*)w_image, bias, m, relu, (__nv_bfloat16*)out, ldo,
-             residual, ldr};
-  const int64_t tiles = cdiv(m, BM);
-  const int grid = (int)(tiles < g_num_sms ? tiles : g_num_sms);
+  Params prm = base_params();
+  prm.x = x;
+  prm.ldx = ldx;
+  prm.gamma = gamma;
+  prm.beta = beta;
+  prm.eps = eps;
+  prm.w_img = (const __nv_bfloat16*)w_image;
+  prm.bias = bias;
+  prm.m = m;
+  prm.relu = relu;
+  prm.out = (__nv_bfloat16*)out;
+  prm.ldo = ldo;
+  prm.res = residual;
+  prm.ldr = ldr;
+  prm.add = add;
+  prm.ld_add = ld_add;
+  prm.n_blocks = (int)cdiv(n, BN);
+  prm.n_last = (int)(n - (int64_t)(prm.n_blocks - 1) * BN);
   cudaStream_t s = as_stream(stream);
-  auto launch = [&](auto kern, int smem_bytes) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
-    kern<<<grid, THREADS, smem_bytes, s>>>(prm);
-  };
-  // Contiguous fp32 rows take the bulk-copy staged path (rows are copied as
-  // one block per 32-row group).
-  const bool staged = ln && ldx == KDIM;
   if (ln) {
-    MB_REQUIRE(out != nullptr, "gemm_rows: the LayerNorm prologue writes a bf16 output");
-    if (staged) launch(rowgemm_kernel<PRO_LN, EPI_STORE, true>, Plan<PRO_LN, EPI_STORE, true>::SMEM);
-    else launch(rowgemm_kernel<PRO_LN, EPI_STORE, false>, Plan<PRO_LN, EPI_STORE, false>::SMEM);
-  } else {
-    if (out) launch(rowgemm_kernel<PRO_COPY, EPI_STORE, false>, Plan<PRO_COPY, EPI_STORE, false>::SMEM);
-    else launch(rowgemm_kernel<PRO_COPY, EPI_RESIDUAL, false>, Plan<PRO_COPY, EPI_RESIDUAL, false>::SMEM);
+    if (g_ln_plan == 1) return launch_rowgemm<PRO_LN, EPI_STORE, false, 4, true>(prm, s, "gemm_rows");
+    // contiguous fp32 rows take the bulk-copy staged path (one block per 32-row group)
+    if (ldx == KDIM && g_ln_plan == 0) return launch_rowgemm<PRO_LN, EPI_STORE, true, 4>(prm, s, "gemm_rows");
+    return launch_rowgemm<PRO_LN, EPI_STORE, false, 4>(prm, s, "gemm_rows");
   }
-  return launch_status("gemm_rows");
+  // bf16 rows: tensor-map loads of A K-blocks
+  MB_REQUIRE(m < (int64_t(1) << 31), "gemm_rows: at most 2^31 - 1 rows per call");
+  if (!encode_rows_map(&prm.tmap_x, x, m, k, ldx))
+    return ::mb::fail(MB_LAUNCH_FAILED, "gemm_rows: could not encode the input tensor map");
+  if (out) {
+    if (k == 512) return launch_rowgemm<PRO_TMA, EPI_STORE, false, 8>(prm, s, "gemm_rows");
+    if (g_store_plan == 1) return launch_rowgemm<PRO_TMA, EPI_STORE, false, 4, true>(prm, s, "gemm_rows");
+    return launch_rowgemm<PRO_TMA, EPI_STORE, false, 4>(prm, s, "gemm_rows");
+  }
+  if (k == 512) return launch_rowgemm<PRO_TMA, EPI_RESIDUAL, false, 8>(prm, s, "gemm_rows");
+  return launch_rowgemm<PRO_TMA, EPI_RESIDUAL, false, 4>(prm, s, "gemm_rows");
+}
+
+int mb_gemm_set_plan(int store_plan, int ln_plan) {
+  MB_REQUIRE(store_plan >= 0 && store_plan <= 1 && ln_plan >= 0 && ln_plan <= 2, "gemm_set_plan: unknown plan");
+  sm100::g_store_plan = store_plan;
+  sm100::g_ln_plan = ln_plan;
+  return MB_OK;
+}
+
+int mb_gemm_rows(const void* x, int x_dtype, int64_t ldx, int64_t m, const float* gamma, const float* beta, float eps,
+                 const void* w_image, const float* bias, int relu, void* out, int64_t ldo, float* residual,
+                 int64_t ldr, void* stream) {
+  return mb_gemm_rows_ex(x, x_dtype, ldx, m, sm100::KDIM, gamma, beta, eps, w_image, sm100::BN, bias, relu, nullptr,
+                         0, out, ldo, residual, ldr, stream);
+}
+
+int mb_gemm_rows_head(const void* x, int64_t ldx, int64_t m, const void* w_image, int64_t n, const float* bias,
+                      const void* tok, int64_t ld_tok, int64_t n_tok, const int64_t* tok_idx, const float* w_out,
+                      const float* b_out, int n_out, float* out, int64_t ldo, void* stream) {
+  using namespace sm100;
+  MB_REQUIRE(m >= 0, "gemm_rows_head: negative m");
+  MB_REQUIRE(n == 128 || n == 256, "gemm_rows_head: the hidden width must be 128 or 256 (got %lld)", (long long)n);
+  MB_REQUIRE(n_out >= 1 && n_out <= MAX_HEAD_OUT, "gemm_rows_head: 1 to %d outputs (got %d)", MAX_HEAD_OUT, n_out);
+  if (m == 0) return MB_OK;
+  MB_REQUIRE(x && w_image && tok && tok_idx && w_out && b_out && out, "gemm_rows_head: null pointer");
+  MB_REQUIRE(ldx >= KDIM && aligned(x, 16) && (ldx * 2) % 16 == 0, "gemm_rows_head: x rows must be 16-byte aligned");
+  MB_REQUIRE(ld_tok >= n && aligned(tok, 16) && (ld_tok * 2) % 16 == 0,
+             "gemm_rows_head: tok rows must be 16-byte aligned");
+  MB_REQUIRE(aligned(w_out, 16) && aligned(w_image, 16) && (!bias || aligned(bias, 16)),
+             "gemm_rows_head: misaligned weights or bias");
+  MB_REQUIRE(ldo >= n_out, "gemm_rows_head: ldo must hold the outputs");
+  Params prm = base_params();
+  prm.x = x;
+  prm.ldx = ldx;
+  prm.w_img = (const __nv_bfloat16*)w_image;
+  prm.bias = bias;
+  prm.m = m;
+  prm.n_last = (int)n;
+  prm.tok = (const __nv_bfloat16*)tok;
+  prm.ld_tok = ld_tok;
+  prm.n_tok = n_tok;
+  prm.tok_idx = tok_idx;
+  prm.w_out = w_out;
+  prm.b_out = b_out;
+  prm.n_out = n_out;
+  prm.head_out = out;
+  prm.ld_head = ldo;
+  MB_REQUIRE(m < (int64_t(1) << 31), "gemm_rows_head: at most 2^31 - 1 rows per call");
+  if (!encode_rows_map(&prm.tmap_x, x, m, KDIM, ldx))
+    return ::mb::fail(MB_LAUNCH_FAILED, "gemm_rows_head: could not encode the input tensor map");
+  return launch_rowgemm<PRO_TMA, EPI_HEAD, false, 4, true>(prm, as_stream(stream), "gemm_rows_head");
 }
 
 int mb_gemm_rows_ln(const void* a, int64_t lda, int64_t m, const void* w_image, const float* bias, float* residual,
@@ -890,8 +1279,14 @@ int mb_gemm_rows_ln(const void* a, int64_t lda, int64_t m, const void* w_image, 
   MB_REQUIRE(aligned(a, 16) && (lda * 2) % 16 == 0 && lda >= KDIM, "gemm_rows_ln: a rows must be 16-byte aligned");
   MB_REQUIRE(aligned(residual, 16) && ldr % 4 == 0 && ldr >= BN, "gemm_rows_ln: residual rows must be 16-byte aligned");
   MB_REQUIRE(aligned(w_image, 16) && (!bias || aligned(bias, 16)), "gemm_rows_ln: misaligned weight image or bias");
-  Params prm{a, lda, nullptr, nullptr, 0.f, (const __nv_bfloat16*)w_image, bias, m, 0, nullptr, 0, residual, ldr,
-             nullptr};
+  Params prm = base_params();
+  prm.x = a;
+  prm.ldx = lda;
+  prm.w_img = (const __nv_bfloat16*)w_image;
+  prm.bias = bias;
+  prm.m = m;
+  prm.res = residual;
+  prm.ldr = ldr;
   const float* gs[MAX_LN] = {g0, g1, g2};
   const float* bs[MAX_LN] = {b0, b1, b2};
   void* os[MAX_LN] = {o0, o1, o2};
@@ -913,19 +1308,7 @@ int mb_gemm_rows_ln(const void* a, int64_t lda, int64_t m, const void* w_image, 
     prm.n_ln = j + 1;
   }
   for (int j = prm.n_ln; j < MAX_LN; ++j) MB_REQUIRE(!os[j], "gemm_rows_ln: outputs must be given in order");
-  if (g_num_sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (g_num_sms <= 0) g_num_sms = 148;
-  }
-  const int64_t tiles = cdiv(m, BM);
-  const int grid = (int)(tiles < g_num_sms ? tiles : g_num_sms);
-  auto kern = rowgemm_kernel<PRO_COPY, EPI_RESID_LN, false>;
-  const int smem_bytes = Plan<PRO_COPY, EPI_RESID_LN, false>::SMEM;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
-  kern<<<grid, THREADS, smem_bytes, as_stream(stream)>>>(prm);
-  return launch_status("gemm_rows_ln");
+  return launch_rowgemm<PRO_COPY, EPI_RESID_LN, false, 4>(prm, as_stream(stream), "gemm_rows_ln");
 }
 
 int mb_hex_message_pass(const void* x, int64_t ldx, int64_t n, const int32_t* nbr, const void* w_image,
@@ -939,21 +1322,16 @@ int mb_hex_message_pass(const void* x, int64_t ldx, int64_t n, const int32_t* nb
   MB_REQUIRE(aligned(out, 16) && (ldo * 2) % 16 == 0 && ldo >= BN, "hex_message_pass: out rows must be 16-byte aligned");
   MB_REQUIRE(aligned(nbr, 4) && aligned(w_image, 16) && (!bias || aligned(bias, 16)),
              "hex_message_pass: misaligned table, weight image or bias");
-  if (g_num_sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (g_num_sms <= 0) g_num_sms = 148;
-  }
-  Params prm{x, ldx, nullptr, nullptr, 0.f, (const __nv_bfloat16*)w_image, bias, n, 0, (__nv_bfloat16*)out, ldo,
-             nullptr, 0, nbr};
-  const int64_t tiles = cdiv(n, BM);
-  const int grid = (int)(tiles < g_num_sms ? tiles : g_num_sms);
-  auto kern = rowgemm_kernel<PRO_HEXMEAN, EPI_ADD_X, false>;
-  const int smem_bytes = Plan<PRO_HEXMEAN, EPI_ADD_X, false>::SMEM;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
-  kern<<<grid, THREADS, smem_bytes, as_stream(stream)>>>(prm);
-  return launch_status("hex_message_pass");
+  Params prm = base_params();
+  prm.x = x;
+  prm.ldx = ldx;
+  prm.w_img = (const __nv_bfloat16*)w_image;
+  prm.bias = bias;
+  prm.m = n;
+  prm.out = (__nv_bfloat16*)out;
+  prm.ldo = ldo;
+  prm.nbr = nbr;
+  return launch_rowgemm<PRO_HEXMEAN, EPI_ADD_X, false, 4>(prm, as_stream(stream), "hex_message_pass");
 }
 
 }  // extern "C"

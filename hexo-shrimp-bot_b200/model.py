@@ -305,20 +305,25 @@ def _f32(t: Tensor) -> Tensor:
 
 class _Lin:
     """A prepared projection: weight in the compute dtype, bias fp32 (or in
-    the compute dtype for cuBLAS epilogues). In bf16 mode a 256-wide input
-    with a multiple of 256 outputs also carries the swizzled weight images of
-    the tcgen05 row GEMM, one per 256-row block of W."""
+    the compute dtype for cuBLAS epilogues). In bf16 mode a weight with a
+    multiple of 128 outputs also carries the swizzled image of the tcgen05
+    row GEMM (``img``, K = 256 or 512), or for K a multiple of 512 one image
+    per 512-column slice of K (``kparts``, summed by successive residual
+    launches)."""
 
-    __slots__ = ("w", "b", "b_cd", "n", "k", "imgs")
+    __slots__ = ("w", "b", "b_cd", "n", "k", "img", "kparts")
 
     def __init__(self, w: Tensor, b: Tensor | None, cd: torch.dtype):
         self.w = w.detach().to(cd).contiguous()
         self.b = _f32(b) if b is not None else None
         self.b_cd = self.b.to(cd) if b is not None else None
         self.n, self.k = self.w.shape
-        self.imgs = None
-        if cd == torch.bfloat16 and self.k == ops.GEMM_K and self.n % ops.GEMM_N == 0 and self.w.is_cuda:
-            self.imgs = [ops.weight_image(self.w[j:j + ops.GEMM_N]) for j in range(0, self.n, ops.GEMM_N)]
+        self.img = self.kparts = None
+        if cd == torch.bfloat16 and self.w.is_cuda and self.n % 128 == 0:
+            if self.k in ops.GEMM_KS:
+                self.img = ops.weight_image(self.w)
+            elif self.k % 512 == 0:
+                self.kparts = [ops.weight_image(self.w[:, j:j + 512]) for j in range(0, self.k, 512)]
 
 
 def _cat_lin(parts, cd) -> _Lin:
@@ -396,22 +401,26 @@ class _Tables:
 class Engine:
     """Prepared weights plus the forward schedule over the kernels."""
 
-    GEMM_MODES = ("tcgen05", "tcgen05-res", "tcgen05-ln", "cublas", "native")
+    GEMM_MODES = ("tcgen05-ln", "cublas", "native")
 
     def __init__(self, model: MantisNet, dtype: torch.dtype, gemm: str = "tcgen05-ln"):
-        """``gemm`` picks the dense-projection path: ``tcgen05`` (the fused
-        LayerNorm-prologue and residual-epilogue row GEMMs of the library
-        wherever the shape is 256 x 256, cuBLAS elsewhere), ``tcgen05-res``
-        (only the residual-epilogue fusion), ``tcgen05-ln`` (the projections
-        that feed a residual update emit the update and the next LayerNorms
-        from the GEMM epilogue; cuBLAS elsewhere; the default, and in fp32
-        the same as ``cublas``), ``cublas`` (separate
-        LayerNorm / cuBLAS / residual kernels) or ``native`` (the CUDA-core
-        fp32 GEMM, the fp32 parity mode)."""
+        """``gemm`` picks the dense-projection path:
+
+        - ``tcgen05-ln`` (the default): every projection is a kernel of the
+          library. In bf16 they run on the tcgen05 row GEMM: LayerNorm
+          prologues fused where a LayerNorm feeds the projection, the
+          projections that feed a residual update emit the update and the
+          next LayerNorms from the same launch, and each decoder head's last
+          two layers are one launch. In fp32 (the parity mode, which tensor
+          -core formats cannot meet at 1e-4) they run on the CUDA-core fp32
+          GEMM.
+        - ``native``: the CUDA-core fp32-accumulating GEMM for every
+          projection, with separate LayerNorm and residual kernels.
+        - ``cublas``: the projections through torch (cuBLAS), with separate
+          LayerNorm and residual kernels; a comparison path only."""
         if dtype not in (torch.float32, torch.bfloat16):
             raise ValueError("dtype must be torch.float32 or torch.bfloat16")
-        if gemm == "torch":
-            gemm = "cublas"
+        gemm = {"torch": "cublas", "tcgen05": "tcgen05-ln"}.get(gemm, gemm)
         if gemm not in self.GEMM_MODES:
             raise ValueError(f"gemm must be one of {self.GEMM_MODES}")
         self.cfg = cfg = model.cfg
@@ -464,6 +473,9 @@ class Engine:
             self.q_lin_a = _Lin(m.mlp_q.lin_a.weight, m.mlp_q.lin_a.bias, cd)
             self.p_out = _Lin(m.mlp_p.out.weight, m.mlp_p.out.bias, cd)
             self.q_out = _Lin(m.mlp_q.out.weight, m.mlp_q.out.bias, cd)
+            # fp32 output layers for the fused head launch
+            self.head_out32 = [(_f32(m.mlp_p.out.weight), _f32(m.mlp_p.out.bias)),
+                               (_f32(m.mlp_q.out.weight), _f32(m.mlp_q.out.bias))]
             if cfg.action_tactical:
                 self.tactical_a = _Lin(m.tactical_a.weight, m.tactical_a.bias, cd)
                 self.tactical_out = _Lin(m.tactical_out.weight, m.tactical_out.bias, cd)
@@ -531,20 +543,40 @@ class Engine:
         return d
 
     # ----------------------------------------------------------- primitives
-    def linear(self, x: Tensor, lin: _Lin, relu: bool = False, out: Tensor | None = None) -> Tensor:
-        """act(x @ W^T + b) in the compute dtype, fp32 accumulation."""
-        if self.gemm == "native":
-            return ops.linear_native(x, lin.w, lin.b, relu=relu, out_dtype=self.cd, out=out)
+    def _tc(self, lin: _Lin, x: Tensor) -> bool:
+        """Whether act(x @ W^T) runs on the tcgen05 row GEMM."""
+        return (self.gemm == "tcgen05-ln" and lin.img is not None and x.dtype == torch.bfloat16 and x.dim() == 2
+                and x.stride(1) == 1 and x.shape[1] == lin.k)
+
+    def linear(self, x: Tensor, lin: _Lin, relu: bool = False, out: Tensor | None = None,
+               add: Tensor | None = None) -> Tensor:
+        """act(x @ W^T + b (+ add)) in the compute dtype, fp32 accumulation;
+        ``add`` is an fp32 addend of the output's shape."""
+        if self._tc(lin, x):
+            return ops.gemm_rows(x, lin.img, bias=lin.b, relu=relu, out=out, add=add)
+        if self.gemm != "cublas":
+            if add is None:
+                return ops.linear_native(x, lin.w, lin.b, relu=relu, out_dtype=self.cd, out=out)
+            y = ops.linear_native(x, lin.w, lin.b, out_dtype=torch.float32)
+            ops.residual_add(y, add)
+            if relu:
+                y.relu_()
+            if out is None:
+                return y.to(self.cd)
+            out.copy_(y)
+            return out
         if lin.b_cd is None:
             y = torch.matmul(x, lin.w.t(), out=out) if out is not None else torch.matmul(x, lin.w.t())
-        elif relu:
+        elif relu and add is None:
             y = torch._addmm_activation(lin.b_cd, x, lin.w.t(), use_gelu=False)
             if out is not None:
                 out.copy_(y)
                 y = out
         else:
             y = torch.addmm(lin.b_cd, x, lin.w.t(), out=out) if out is not None else torch.addmm(lin.b_cd, x, lin.w.t())
-        if relu and lin.b_cd is None:
+        if add is not None:
+            y.copy_(y.float() + add)
+        if relu and (lin.b_cd is None or add is not None):
             y.relu_()
         return y
 
@@ -563,39 +595,20 @@ class Engine:
     def ln(self, x: Tensor, p: _LN, out: Tensor | None = None, dtype=None) -> Tensor:
         return ops.layer_norm(x, p.g, p.b, out_dtype=dtype or self.cd, out=out)
 
-    def _fused(self, lin: _Lin, ln: bool = False) -> bool:
-        if lin.imgs is None:
-            return False
-        return self.gemm == "tcgen05" or (self.gemm == "tcgen05-res" and not ln)
-
     def ln_linear(self, x: Tensor, p: _LN, lin: _Lin, relu: bool = False) -> Tensor:
-        """act(LN(x) @ W^T + b): one tcgen05 launch per 256 output columns
-        with the LayerNorm in the prologue (x fp32), else LN then GEMM."""
-        if self._fused(lin, ln=True) and x.dtype == torch.float32:
-            out = torch.empty(x.shape[0], lin.n, dtype=torch.bfloat16, device=x.device)
-            for j, img in enumerate(lin.imgs):
-                c = slice(j * ops.GEMM_N, (j + 1) * ops.GEMM_N)
-                ops.gemm_rows(x, img, bias=lin.b[c] if lin.b is not None else None, gamma=p.g, beta=p.b,
-                              relu=relu, out=out[:, c])
-            return out
+        """act(LN(x) @ W^T + b): one tcgen05 launch with the LayerNorm in the
+        prologue (x fp32, width 256, any multiple of 128 outputs), else LN
+        then GEMM."""
+        if (self.gemm == "tcgen05-ln" and lin.img is not None and lin.k == ops.GEMM_K and x.dtype == torch.float32
+                and self.cd == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1):
+            return ops.gemm_rows(x, lin.img, bias=lin.b, gamma=p.g, beta=p.b, relu=relu)
         return self.linear(self.ln(x, p), lin, relu=relu)
-
-    def linear_cd(self, a: Tensor, lin: _Lin, relu: bool = False) -> Tensor:
-        """act(a @ W^T + b) for compute-dtype rows a."""
-        if self.gemm == "tcgen05" and lin.imgs is not None and a.dtype == torch.bfloat16:
-            out = torch.empty(a.shape[0], lin.n, dtype=torch.bfloat16, device=a.device)
-            for j, img in enumerate(lin.imgs):
-                c = slice(j * ops.GEMM_N, (j + 1) * ops.GEMM_N)
-                ops.gemm_rows(a, img, bias=lin.b[c] if lin.b is not None else None, relu=relu, out=out[:, c])
-            return out
-        return self.linear(a, lin, relu=relu)
 
     def linear_update(self, a: Tensor, lin: _Lin, x: Tensor, lns) -> list[Tensor]:
         """x += a @ W^T + b, then the LayerNorms ``lns`` of the updated rows
         (as ``update``): one tcgen05 launch in ``tcgen05-ln`` mode."""
-        if (self.gemm == "tcgen05-ln" and lin.imgs is not None and lin.n == ops.GEMM_N and 1 <= len(lns) <= 3
-                and a.dtype == torch.bfloat16 and a.stride(1) == 1 and x.dtype == torch.float32 and x.stride(1) == 1
-                and self.cd == torch.bfloat16
+        if (self._tc(lin, a) and lin.n == ops.GEMM_N and lin.k == ops.GEMM_K and 1 <= len(lns) <= 3
+                and x.dtype == torch.float32 and x.stride(1) == 1
                 and all(not isinstance(e, tuple) or e[1] is None or e[1].dtype == torch.bfloat16 for e in lns)):
             outs = []
             for e in lns:
@@ -606,14 +619,21 @@ class Engine:
             if self.probe is not None:  # algorithmic bytes of the launch: a, residual in + out, outputs
                 self.probe.setdefault("resid_ln_bytes", []).append(x.shape[0] * (512 + 2048 + 512 * len(outs)))
             with self.timed("resid_ln"):
-                return ops.gemm_rows_ln(a, lin.imgs[0], lin.b, x, outs)
+                return ops.gemm_rows_ln(a, lin.img, lin.b, x, outs)
         return self.update(x, self.linear(a, lin), lns)
 
     def linear_residual(self, a: Tensor, lin: _Lin, x: Tensor) -> None:
-        """x += a @ W^T + b with the residual add in the GEMM epilogue."""
-        if self._fused(lin) and lin.n == ops.GEMM_N and a.dtype == torch.bfloat16 and x.dtype == torch.float32:
-            ops.gemm_rows(a, lin.imgs[0], bias=lin.b, residual=x)
-            return
+        """x += a @ W^T + b with the residual add in the GEMM epilogue (a
+        K wider than 512 is summed over 512-column slices, one launch each)."""
+        if (self.gemm == "tcgen05-ln" and lin.n == ops.GEMM_N and a.dtype == torch.bfloat16 and a.stride(1) == 1
+                and x.dtype == torch.float32 and x.stride(1) == 1 and a.shape[1] == lin.k):
+            if lin.img is not None:
+                ops.gemm_rows(a, lin.img, bias=lin.b, residual=x)
+                return
+            if lin.kparts is not None:
+                for j, img in enumerate(lin.kparts):
+                    ops.gemm_rows(a[:, j * 512:(j + 1) * 512], img, bias=lin.b if j == 0 else None, residual=x)
+                return
         ops.residual_add(x, self.linear(a, lin))
 
     def pair_mlp_residual(self, x: Tensor, a_ln: _LN, agg_writer, mlp) -> None:
@@ -752,7 +772,7 @@ class Engine:
         qkv = self.ln_linear(tok, blk["ln_attn"], blk["qkv"])
         if update_stones:
             att = ops.stone_attention_ragged(qkv, T.tok_off, cfg.heads, T.max_t)
-            ops.tokens_scatter_add(g, s, T.stone_off, T.tok_off, self.linear_cd(att, blk["wo"]), update_stones=True)
+            ops.tokens_scatter_add(g, s, T.stone_off, T.tok_off, self.linear(att, blk["wo"]), update_stones=True)
         else:
             att = ops.stone_attention_ragged(qkv, T.tok_off, cfg.heads, T.max_t, max_queries=GLOBAL_ROWS,
                                              out_dtype=cd)
@@ -777,7 +797,7 @@ class Engine:
         # FFN (row-wise; the stone half is skipped in the last block)
         for x_ in ((s, g) if update_stones else (g,)):
             hid = self.ln_linear(x_, blk["ln_ffn"], blk["ffn0"], relu=True)
-            ops.residual_add(x_, self.linear(hid, blk["ffn2"]))
+            self.linear_residual(hid, blk["ffn2"], x_)
         return s, w, g, c, buf_w, zc, w_out, cells
 
     def _cell_stage(self, blk, nxt, s, c, T: _Tables, zc_cr, zw_cr, zw_wr):
@@ -830,13 +850,13 @@ class Engine:
             if cfg.cell_structure:
                 mlp = blk["mlp_c"]
                 buf = torch.cat([zstate, reads], 1)
-                ops.residual_add(c, self.linear(self.linear(buf, mlp[0], relu=True), mlp[1]))
+                self.linear_residual(self.linear(buf, mlp[0], relu=True), mlp[1], c)
             if cfg.cell_adjacency:
                 q = self.ln_linear(c, blk["ln_adj_q"], blk["adj_wq"])
                 kv = self.ln_linear(c, blk["ln_adj_k"], blk["adj_kv"])
                 read = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["adj_bias"], blk["adj_vclass"], T.a_ptr,
                                              T.a_src, T.a_cls, skip_ptr=T.skip, out_dtype=cd)
-                ops.residual_add(c, self.linear(read, blk["adj_wo"]))
+                self.linear_residual(read, blk["adj_wo"], c)
             zc_wr, zc_out = self.update(c, None, [blk["ln_wr_c"], exit_ln])
         q = self.linear(zw_wr, blk["wr_wq"])
         kv = self.linear(zc_wr, blk["wr_kv"])
@@ -854,7 +874,7 @@ class Engine:
         if T is None or T.N_c != b.cell_pos.shape[0]:
             T = _Tables(cfg, b)
         n_c = T.N_c
-        pre = self.linear_cd(w.to(cd), self.act_proj)
+        pre = self.linear(w.to(cd), self.act_proj)
         # decoder input [cells | action rows]; the evaluate path's trunk has
         # already written cells into the left half of its buffer
         head_buf = getattr(self, "_head_buf", None)
@@ -866,8 +886,8 @@ class Engine:
         if cfg.action_tactical:
             acts = ops.row_encode(pre, self.act_table, T.dec_window, T.act_class, T.cell_ptr, n_c,
                                   out_dtype=torch.float32, **enc)
-            t = self.linear(self.linear(b.act_tactical.to(cd), self.tactical_a, relu=True), self.tactical_out)
-            ops.residual_add(acts, t)
+            t = self.linear(b.act_tactical.to(cd), self.tactical_a, relu=True)
+            self.linear_residual(t, self.tactical_out, acts)
             buf[:, h:].copy_(acts)
         else:
             ops.row_encode(pre, self.act_table, T.dec_window, T.act_class, T.cell_ptr, n_c, out=buf[:, h:], **enc)
@@ -876,15 +896,22 @@ class Engine:
                 buf[:, :h].copy_(cells)
             else:
                 ops.run_reduce(w, T.dec_window, T.cell_ptr, n_c, out=buf[:, :h])
-        base = self.linear(buf, self.dec_pq)  # (N_c, 2H): [p-head | q-head]
+        # (N_c, 2H): [p-head | q-head] = [cells | acts] @ W_dec^T + sum of the
+        # cell's decoder class rows
         extra = ops.run_reduce(self.e_pq, T.dec_class, T.cell_ptr, n_c)
-        ops.residual_add(base, extra)
+        base = self.linear(buf, self.dec_pq, add=extra)
         gh = self.linear(g.to(cd), self.lin_b_pq)  # (P, 2 * P_H)
         ph = cfg.policy_hidden
         outs = []
         for j, (lin_a, out_lin) in enumerate(((self.p_lin_a, self.p_out), (self.q_lin_a, self.q_out))):
-            pre_j = self.linear(base[:, j * h:(j + 1) * h], lin_a)
-            ops.add_gather(pre_j, gh[:, j * ph:(j + 1) * ph].contiguous(), b.cell_pos, relu=True)
+            x_j = base[:, j * h:(j + 1) * h]
+            t_j = gh[:, j * ph:(j + 1) * ph]
+            if self._tc(lin_a, x_j) and lin_a.n in (128, 256) and out_lin.n <= 4:
+                w_out, b_out = self.head_out32[j]
+                outs.append(ops.gemm_head(x_j, lin_a.img, lin_a.b, t_j, b.cell_pos, w_out, b_out))
+                continue
+            pre_j = self.linear(x_j, lin_a)
+            ops.add_gather(pre_j, t_j.contiguous(), b.cell_pos, relu=True)
             outs.append(self.linear(pre_j, out_lin))
         return outs[0].float().reshape(-1), outs[1].float()
 

@@ -658,34 +658,75 @@ def fused_attention(q, k, v, seq_lens):
 # ============================================ tcgen05 fused row GEMM (sm_100a)
 
 GEMM_K = GEMM_N = 256
+GEMM_KS = (256, 512)  # the K widths the tensor-core row GEMM holds whole in shared memory
 
 
 def weight_image(w: torch.Tensor) -> torch.Tensor:
-    """The pre-swizzled bf16 image of a (256, 256) weight for ``gemm_rows``."""
+    """The pre-swizzled bf16 image of an (N, K) weight for ``gemm_rows``:
+    N a multiple of 128, K 256 or 512."""
     _cuda(w)
     w = w.detach().to(torch.bfloat16).contiguous()
-    if tuple(w.shape) != (GEMM_N, GEMM_K):
-        raise ValueError(f"gemm weight must be ({GEMM_N}, {GEMM_K}), got {tuple(w.shape)}")
+    n, k = w.shape
+    if n % 128 or n == 0 or k not in GEMM_KS:
+        raise ValueError(f"gemm weight must be (N, K) with N a multiple of 128 and K in {GEMM_KS}, got {(n, k)}")
     img = torch.empty_like(w)
-    call("mb_gemm_weight_image", ptr(w), w.shape[0], w.shape[1], ptr(img), stream_of(w.device))
+    call("mb_gemm_weight_image", ptr(w), n, k, ptr(img), stream_of(w.device))
     return img
 
 
-def gemm_rows(x, w_img, bias=None, gamma=None, beta=None, relu=False, out=None, residual=None, eps=1e-5):
-    """act(prologue(x) @ W^T + bias) on tcgen05: LayerNorm prologue when
-    ``gamma`` is given (x fp32), else x bf16. Writes ``out`` (bf16, allocated
-    when neither out nor residual is given) or adds into ``residual`` (fp32)."""
-    _rowmajor(x, "x")
-    if x.shape[1] != GEMM_K:
-        raise ValueError(f"gemm_rows takes rows of width {GEMM_K}")
-    m = x.shape[0]
+def gemm_rows(x, w_img, bias=None, gamma=None, beta=None, relu=False, out=None, residual=None, eps=1e-5, add=None):
+    """act(prologue(x) @ W^T + bias (+ add)) on tcgen05: LayerNorm prologue
+    when ``gamma`` is given (x fp32, width 256), else x bf16 (width 256 or
+    512). ``w_img`` is ``weight_image(W)`` of W (N, K); N is read from it.
+    Writes ``out`` (bf16, allocated when neither out nor residual is given),
+    optionally plus fp32 addend rows ``add``, or adds into ``residual``
+    (fp32, N = 256)."""
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("x must be 2-D with unit column stride")
+    m, k = x.shape
+    n = w_img.shape[0]
+    if w_img.shape[1] != k:
+        raise ValueError(f"x width {k} does not match the weight's K {w_img.shape[1]}")
     if out is None and residual is None:
-        out = torch.empty(m, GEMM_N, dtype=torch.bfloat16, device=x.device)
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
+    if out is not None and (out.dtype != torch.bfloat16 or out.shape != (m, n) or out.stride(1) != 1):
+        raise ValueError("out must be (m, N) bf16 with unit column stride")
+    if add is not None and (add.dtype != torch.float32 or add.shape != (m, n) or add.stride(1) != 1):
+        raise ValueError("add must be (m, N) fp32 with unit column stride")
     b = bias.float().contiguous() if bias is not None else None
-    call("mb_gemm_rows", ptr(x), dtype_code(x.dtype), x.stride(0), m, ptr(gamma), ptr(beta), float(eps), ptr(w_img),
-         ptr(b), int(relu), ptr(out), out.stride(0) if out is not None else 0, ptr(residual),
-         residual.stride(0) if residual is not None else 0, stream_of(x.device))
+    call("mb_gemm_rows_ex", ptr(x), dtype_code(x.dtype), x.stride(0), m, k, ptr(gamma), ptr(beta), float(eps),
+         ptr(w_img), n, ptr(b), int(relu), ptr(add), add.stride(0) if add is not None else 0, ptr(out),
+         out.stride(0) if out is not None else 0, ptr(residual), residual.stride(0) if residual is not None else 0,
+         stream_of(x.device))
     return out if out is not None else residual
+
+
+def gemm_head(x, w_img, bias, tok, tok_idx, w_out, b_out, out=None):
+    """A decoder head's hidden and output layers in one tensor-core launch
+    (reference _PairMlp over a per-cell row and its position's row,
+    model.py:246-260, 1031-1139):
+        out[r] = relu(x[r] @ W^T + bias + tok[tok_idx[r]]) @ w_out^T + b_out
+    x (m, 256) bf16; W (N, 256) with N 128 or 256; tok (P, N) bf16 rows (the
+    position half lin_b(g), already projected); w_out (n_out, N) fp32 with
+    n_out <= 4; out (m, n_out) fp32."""
+    _rowmajor(x, "x")
+    _rowmajor(tok, "tok")
+    n = w_img.shape[0]
+    n_out = w_out.shape[0]
+    if x.dtype != torch.bfloat16 or tok.dtype != torch.bfloat16 or tok.shape[1] != n:
+        raise ValueError("gemm_head takes bf16 x and bf16 tok rows of the hidden width")
+    if out is None:
+        out = torch.empty(x.shape[0], n_out, dtype=torch.float32, device=x.device)
+    _i64(tok_idx, "tok_idx")
+    if tok_idx.shape != (x.shape[0],):
+        raise ValueError("tok_idx must hold one position per row")
+    wo = w_out if (w_out.dtype == torch.float32 and w_out.is_contiguous()) else w_out.float().contiguous()
+    bo = b_out if (b_out.dtype == torch.float32 and b_out.is_contiguous()) else b_out.float().contiguous()
+    if out.dtype != torch.float32 or out.shape != (x.shape[0], n_out) or out.stride(1) != 1:
+        raise ValueError("out must be (m, n_out) fp32 rows")
+    call("mb_gemm_rows_head", ptr(x), x.stride(0), x.shape[0], ptr(w_img), n, ptr(bias), ptr(tok), tok.stride(0),
+         tok.shape[0], ptr(tok_idx), ptr(wo), ptr(bo), n_out, ptr(out), out.stride(0), stream_of(x.device))
+    return out
 
 
 def gemm_rows_ln(a, w_img, bias, residual, outs, eps=1e-5):

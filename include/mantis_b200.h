@@ -252,7 +252,8 @@ int mb_compose_q(const float* critic, int64_t ld_critic, const int64_t* offsets,
 int mb_linear(const void* a, int a_dtype, int64_t lda, int64_t m, int64_t k, const void* w, int w_dtype,
               const float* bias, int64_t n, int relu, void* out, int out_dtype, int64_t ldo, void* stream);
 
-/* Fused row GEMM on tcgen05 tensor cores (sm_100a), K = N = 256:
+/* Fused row GEMM on tcgen05 tensor cores (sm_100a), K = N = 256 (see
+ * mb_gemm_rows_ex for the other shapes):
  *   out[r] = act(LN(x[r]) @ W^T + bias)            (gamma != NULL: x fp32, LayerNorm prologue)
  *   out[r] = act(x[r] @ W^T + bias)                (gamma == NULL: x bf16)
  * with either a bf16 output (out, ldo) or an in-place fp32 residual update
@@ -264,6 +265,41 @@ int mb_gemm_weight_image(const void* w, int64_t n, int64_t k, void* image, void*
 int mb_gemm_rows(const void* x, int x_dtype, int64_t ldx, int64_t m, const float* gamma, const float* beta, float eps,
                  const void* w_image, const float* bias, int relu, void* out, int64_t ldo, float* residual,
                  int64_t ldr, void* stream);
+
+/* The row GEMM above for every projection shape of the model: K = 256 or
+ * 512 (bf16 rows; the LayerNorm prologue takes K = 256), N any multiple of
+ * 128 (a row tile's N blocks run back to back on the tile held in shared
+ * memory), w_image = mb_gemm_weight_image of the (N, K) weight. With `out`
+ * (bf16, ldo >= n) an optional fp32 addend `add` (ld_add) is summed before the
+ * activation; `residual` (fp32, N = 256) takes the in-place update instead.
+ * Replaces every nn.Linear of the trunk and the decoder (model.py:246-260,
+ * 425-692 Q / K|V / FFN / PairMlp projections, 1031-1139 decoder GEMMs),
+ * which the reference runs through cuBLAS under autocast. */
+int mb_gemm_rows_ex(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k, const float* gamma,
+                    const float* beta, float eps, const void* w_image, int64_t n, const float* bias, int relu,
+                    const float* add, int64_t ld_add, void* out, int64_t ldo, float* residual, int64_t ldr,
+                    void* stream);
+
+/* Launch plan of the bf16-output row GEMMs (a measurement knob; the
+ * defaults are the measured best): store_plan 0 streams W K-blocks per row
+ * tile, 1 holds a whole N block of W in shared memory per CTA (K = 256);
+ * ln_plan 0 stages the LayerNorm prologue's fp32 rows in 32-row groups, 1
+ * weight-stationary with per-row loads, 2 per-row loads with W streamed.
+ * Process-wide; not for use while launches are being issued from other
+ * threads. No counterpart in the reference. */
+int mb_gemm_set_plan(int store_plan, int ln_plan);
+
+/* A decoder head's last two layers in one launch (the reference's _PairMlp
+ * on a cell row and its position's row, model.py:246-260 called from
+ * _cell_scores, model.py:1031-1139):
+ *   out[r, j] = b_out[j] + sum_c w_out[j, c] * relu(x[r] W^T + bias + tok[tok_idx[r]])[c]
+ * x (m, 256) bf16; W (N, 256), N = 128 or 256, as mb_gemm_weight_image;
+ * tok (n_tok, N) bf16 rows (the position half, already projected);
+ * tok_idx (m) int64 position of each row; w_out (n_out, N) fp32 row-major,
+ * 1 <= n_out <= 4; out (m, n_out) fp32 with leading dim ldo. */
+int mb_gemm_rows_head(const void* x, int64_t ldx, int64_t m, const void* w_image, int64_t n, const float* bias,
+                      const void* tok, int64_t ld_tok, int64_t n_tok, const int64_t* tok_idx, const float* w_out,
+                      const float* b_out, int n_out, float* out, int64_t ldo, void* stream);
 
 /* Fused projection + residual update + LayerNorms on the tensor cores:
  *   x[r] += a[r] W^T + bias;  out_j[r] = LN_j(x[r])  for each given output j,

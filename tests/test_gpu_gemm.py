@@ -104,3 +104,94 @@ def test_residual_layernorm_rejects_fp32_outputs():
     one, zero = torch.ones(256, device=DEV), torch.zeros(256, device=DEV)
     with pytest.raises(ValueError):
         ops.gemm_rows_ln(a, w, None, x, [(one, zero, torch.empty(64, 256, device=DEV))])
+
+
+# ------------------------------------------------ every projection shape
+@pytest.mark.parametrize("k,n", [(256, 128), (256, 384), (256, 512), (256, 768), (256, 1024), (512, 256),
+                                 (512, 512), (512, 128), (512, 640)])
+@pytest.mark.parametrize("m", [1, 129, 5000, 60000])
+def test_copy_prologue_store_shapes(k, n, m):
+    """bf16 rows of width K = 256 / 512 times an (N, K) weight, N a multiple
+    of 128 (several N blocks on one A tile, a 128-wide last block), with
+    bias, ReLU and the fp32 addend; strided input and output rows."""
+    g = torch.Generator(device="cpu").manual_seed(m * 7 + k + n)
+    xs = torch.randn(m, k + 64, generator=g).to(torch.bfloat16).to(DEV)
+    x = xs[:, 32:32 + k]
+    w = (torch.randn(n, k, generator=g) / (k ** 0.5)).to(DEV)
+    b = torch.randn(n, generator=g).to(DEV)
+    add = torch.randn(m, n, generator=g).to(DEV)
+    img = ops.weight_image(w)
+    ref = x.float() @ w.to(torch.bfloat16).float().t() + b
+    out = torch.empty(m, n + 64, dtype=torch.bfloat16, device=DEV)[:, 64:]
+    ops.gemm_rows(x, img, bias=b, out=out)
+    torch.cuda.synchronize()
+    _close(out, ref)
+    _close(ops.gemm_rows(x, img, bias=b, relu=True, add=add), (ref + add).relu())
+    mb._lib.check_device_error()
+
+
+@pytest.mark.parametrize("n", [256, 512, 768, 1024])
+@pytest.mark.parametrize("m", [3, 4000])
+def test_ln_prologue_wide(n, m):
+    g = torch.Generator(device="cpu").manual_seed(n + m)
+    x = (torch.randn(m, 256, generator=g) * 3 - 1).to(DEV)
+    w = (torch.randn(n, 256, generator=g) / 16).to(DEV)
+    b = torch.randn(n, generator=g).to(DEV)
+    gam, bet = torch.randn(256, generator=g).to(DEV), torch.randn(256, generator=g).to(DEV)
+    out = ops.gemm_rows(x, ops.weight_image(w), bias=b, gamma=gam, beta=bet, relu=True)
+    z = F.layer_norm(x, (256,), gam, bet).to(torch.bfloat16).float()
+    torch.cuda.synchronize()
+    _close(out, (z @ w.to(torch.bfloat16).float().t() + b).relu())
+
+
+@pytest.mark.parametrize("m", [7, 9000])
+def test_k512_residual_and_k1024_split(m):
+    """residual += a @ W^T + b for K = 512 in one launch and K = 1024 as two
+    launches over 512-column slices (the FFN's down-projection)."""
+    g = torch.Generator(device="cpu").manual_seed(m)
+    a = torch.randn(m, 1024, generator=g).to(torch.bfloat16).to(DEV)
+    w = (torch.randn(256, 1024, generator=g) / 32).to(DEV)
+    b = torch.randn(256, generator=g).to(DEV)
+    res0 = torch.randn(m, 256, generator=g).to(DEV)
+    res = res0.clone()
+    ops.gemm_rows(a[:, :512], ops.weight_image(w[:, :512]), bias=b, residual=res)
+    _close(res, res0 + a[:, :512].float() @ w[:, :512].to(torch.bfloat16).float().t() + b)
+    ops.gemm_rows(a[:, 512:], ops.weight_image(w[:, 512:]), residual=res)
+    torch.cuda.synchronize()
+    _close(res, res0 + a.float() @ w.to(torch.bfloat16).float().t() + b)
+    mb._lib.check_device_error()
+
+
+@pytest.mark.parametrize("n,n_out", [(128, 1), (128, 3), (256, 3), (256, 4)])
+@pytest.mark.parametrize("m", [1, 130, 20000])
+def test_head_epilogue(n, n_out, m):
+    """out = relu(x W^T + b + tok[pos]) @ w_out^T + b_out (the decoder head's
+    hidden and output layers in one launch) against fp32 torch."""
+    g = torch.Generator(device="cpu").manual_seed(n * 11 + n_out + m)
+    p = 37
+    x = torch.randn(m, 256, generator=g).to(torch.bfloat16).to(DEV)
+    w = (torch.randn(n, 256, generator=g) / 16).to(DEV)
+    b = torch.randn(n, generator=g).to(DEV)
+    tok_all = torch.randn(p, 2 * n, generator=g).to(torch.bfloat16).to(DEV)
+    tok = tok_all[:, n:]  # strided view, as the engine passes one head's half
+    pos = torch.randint(0, p, (m,), generator=g).to(DEV)
+    w_out = torch.randn(n_out, n, generator=g).to(DEV) / 8
+    b_out = torch.randn(n_out, generator=g).to(DEV)
+    got = ops.gemm_head(x, ops.weight_image(w), b, tok, pos, w_out, b_out)
+    hid = (x.float() @ w.to(torch.bfloat16).float().t() + b + tok.float()[pos]).relu()
+    want = hid @ w_out.t() + b_out
+    torch.cuda.synchronize()
+    err = (got - want).abs().max().item()
+    assert err <= 1e-3 * want.abs().max().item() + 1e-3, err
+    mb._lib.check_device_error()
+
+
+def test_head_refuses_bad_shapes():
+    x = torch.zeros(4, 256, dtype=torch.bfloat16, device=DEV)
+    img = ops.weight_image(torch.zeros(384, 256, device=DEV))
+    tok = torch.zeros(2, 384, dtype=torch.bfloat16, device=DEV)
+    pos = torch.zeros(4, dtype=torch.long, device=DEV)
+    with pytest.raises(ValueError, match="hidden width"):
+        ops.gemm_head(x, img, None, tok, pos, torch.zeros(1, 384, device=DEV), torch.zeros(1, device=DEV))
+    with pytest.raises(ValueError):
+        ops.weight_image(torch.zeros(200, 256, device=DEV))

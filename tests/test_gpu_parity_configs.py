@@ -161,3 +161,24 @@ def test_config5_fp32_matches_oracle(config5):
     _rel(critic, ref["critic_logits"], 1e-4, "critic")
     _rel(q_values, ref["q_values"], 1e-4, "q_values")
     _rel(value, ref["value"], 1e-4, "value")
+
+
+def test_evaluate_path_runs_no_library_gemm(config5):
+    """Every projection of the bf16 evaluate path is a kernel of the
+    library: a profiled forward over late positions launches no cuBLAS /
+    CUTLASS GEMM (nvjet, xmma, cutlass kernels)."""
+    net, batch, lone, ref = config5
+    eng = net.engine(torch.bfloat16)
+    b = lone.to(DEV)
+    eng.evaluate(b)  # warm (weight images, allocator)
+    torch.cuda.synchronize()
+    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+        eng.evaluate(b)
+        torch.cuda.synchronize()
+    names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    ours = [n for n in names if "mb::" in n]
+    others = sorted({n for n in names if "mb::" not in n})
+    print("library kernels:", len(ours), "other kernels:", others)
+    assert ours, "no library kernel seen"
+    bad = [n for n in others if any(t in n.lower() for t in ("nvjet", "xmma", "cutlass", "gemm", "cublas"))]
+    assert not bad, bad
