@@ -268,10 +268,13 @@ def run_ours(args, rank, world, local_rank):
     # timed region): the fused projection launches or the radius read.
     roof = None
     if rank == 0:
-        radius = radius_roofline(probe, tables, cfg)
-        if radius is not None:
-            radius["total_ms"] = radius["launch_ms"] * radius["launches_timed"]
-        roof = dominant_roofline([resid_ln_roofline(probe), radius])
+        n_dec = int(tables.dec_window.numel())
+        roof = dominant_roofline([
+            resid_ln_roofline(probe), radius_roofline(probe, tables, cfg),
+            segment_roofline(probe, "cell_read", "segment_attention_kernel (cells<-windows, class rows)", tables.N_c,
+                             tables.N_w, n_dec, cfg, 726),
+            segment_roofline(probe, "window_read", "segment_attention_kernel (windows<-cells)", tables.N_w,
+                             tables.N_c, n_dec, cfg, 726)])
 
     # p50 batch-64 latency (config-4 distribution: 40-150 stones), end to end
     p50 = None
@@ -326,19 +329,19 @@ def run_ours(args, rank, world, local_rank):
 
 def radius_read_bytes(T, cfg):
     """Algorithmic HBM bytes of one radius read (cells <- stones): per cell its
-    bf16 query row in and output row out plus its run bound; per edge the int64
-    source and class; each stone's bf16 K and V rows once; the bf16 class value
-    rows and fp32 bias rows once."""
+    bf16 query row in and output row out, its run bound and its slot in the
+    edge-count order; per edge the packed int32 stone | class; each stone's
+    bf16 K and V rows once; the bf16 class value rows and fp32 bias rows once."""
     h, n_cls = cfg.h, 192
-    return (T.N_c * h * 2 * 2 + (T.N_c + 1) * 8 + int(T.r_src.numel()) * 16 + T.N_s * 2 * h * 2
+    return (T.N_c * h * 2 * 2 + (T.N_c + 1) * 8 + T.N_c * 8 + int(T.r_src.numel()) * 4 + T.N_s * 2 * h * 2
             + n_cls * h * 2 + cfg.heads * n_cls * 4)
 
 
 # DRAM bytes per cell of one radius read, from an ncu capture of the same
-# kernel (dram__bytes_read.sum + dram__bytes_write.sum = 486.8 MB over 438,658
-# cells; profiles/segment_attention_radius_and_incidence_reads_64pos.md), scaled
-# to the timed launch by its cell count.
-RADIUS_DRAM_BYTES_PER_CELL = 486_827_264 / 438_658
+# kernel (dram__bytes_read.sum + dram__bytes_write.sum = 450.1 MB over 438,658
+# cells; profiles/radius_read_64pos.md), scaled to the timed launch by its
+# cell count.
+RADIUS_DRAM_BYTES_PER_CELL = 450_067_712 / 438_658
 
 
 def radius_roofline(probe, T, cfg):
@@ -352,13 +355,31 @@ def radius_roofline(probe, T, cfg):
     algo = radius_read_bytes(T, cfg)
     pk, kind = peaks()
     achieved = algo / sec / 1e9
-    cell_ms = [s.elapsed_time(e) for s, e in probe.get("cell_read", [])]
-    return {"kernel": "segment_attention_grouped (radius read, cells<-stones)", "bound": "hbm",
+    return {"kernel": "radius_read_kernel (packed edges, cells<-stones)", "bound": "hbm",
             "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
             "traffic": RADIUS_DRAM_BYTES_PER_CELL * T.N_c, "traffic_source": "ncu capture at 64 positions, scaled by cells",
             "peak_kind": kind, "algorithmic_bytes": algo, "launch_ms": sec * 1000.0,
-            "launches_timed": len(ms), "edges": int(T.r_src.numel()),
-            "cell_read_launch_ms": statistics.mean(cell_ms) if cell_ms else None}
+            "launches_timed": len(ms), "edges": int(T.r_src.numel()), "total_ms": sum(ms)}
+
+
+def segment_roofline(probe, name, kernel, n_q, n_src, n_edges, cfg, n_cls):
+    """A generic segment attention's launches inside the timed region:
+    algorithmic bytes per launch (per query row its bf16 query and output
+    rows and run bound, per edge the int64 source and class, each source's
+    bf16 K and V rows once, class value rows and bias once) over the mean
+    CUDA-event duration."""
+    ev = probe.get(name, [])
+    if not ev:
+        return None
+    h = cfg.h
+    algo = (n_q * (2 * h * 2 + 8) + n_edges * 16 + n_src * 2 * h * 2 + n_cls * (h * 2 + cfg.heads * 4))
+    ms = [s.elapsed_time(e) for s, e in ev]
+    sec = statistics.mean(ms) / 1000.0
+    pk, kind = peaks()
+    achieved = algo / sec / 1e9
+    return {"kernel": kernel, "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": achieved / pk["hbm_gbs"], "traffic": None, "peak_kind": kind, "algorithmic_bytes": algo,
+            "launch_ms": sec * 1000.0, "launches_timed": len(ms), "edges": n_edges, "total_ms": sum(ms)}
 
 
 # DRAM bytes (read + write) over algorithmic bytes of the fused projection +
@@ -397,6 +418,8 @@ def dominant_roofline(cands):
     roof = dict(cands[0])
     if len(cands) > 1:
         roof["next"] = cands[1]
+    if len(cands) > 2:
+        roof["others"] = cands[2:]
     return roof
 
 
@@ -445,6 +468,30 @@ def run_op(args):
                 "unit": "rows/s", "ms_per_step": ms,
                 "config": {"workload": f"{m} rows x 256, bf16 input, fp32 residual, {n_out} bf16 LayerNorm outputs"},
                 "roofline": {"kernel": "rowgemm_kernel<COPY, RESID_LN>", "bound": "hbm", "achieved": algo / ms / 1e6,
+                             "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": algo / ms / 1e6 / pk["hbm_gbs"],
+                             "peak_kind": kind, "algorithmic_bytes": algo}}
+    elif args.op == "radius":
+        # the radius read of one trunk block over encoder-built late positions
+        # (tables derived as the engine derives them, packed edges shared)
+        specs = make_specs(min(p, 256), args.lo, args.hi, seed=1000)
+        host = mb.encoder.encode((specs * math.ceil(p / len(specs)))[:p])
+        cfg = mb.MantisConfig(**ARCH)
+        b = mb.evaluator.to_device(host, dev, mb.evaluator.needed_fields(cfg))
+        T = mb.model._Tables(cfg, b, torch.bfloat16)
+        q = torch.randn(T.N_c, cfg.h, device=dev, generator=g).to(torch.bfloat16)
+        kv = torch.randn(T.N_s, 2 * cfg.h, device=dev, generator=g).to(torch.bfloat16)
+        bias = torch.randn(cfg.heads, 192, device=dev, generator=g) * 0.02
+        vcls = (torch.randn(192, cfg.h, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        h, stage = cfg.h, T.max_t - 4
+        out = torch.empty_like(q)
+        ms = _time_launches(lambda: ops.radius_read(q, kv[:, :h], kv[:, h:], bias, vcls, T.r_ptr, T.r_pack, T.cell_off,
+                                                    T.stone_off, stage, order=T.r_order, out=out),
+                            args.steps, args.warmup)
+        algo = radius_read_bytes(T, cfg)
+        line = {"metric": "radius read cells/s", "value": T.N_c / (ms / 1000.0), "unit": "cells/s", "ms_per_step": ms,
+                "config": {"workload": f"radius read of {p} late positions ({args.lo}-{args.hi} stones)",
+                           "cells": T.N_c, "edges": int(T.r_src.numel())},
+                "roofline": {"kernel": "radius_read_kernel", "bound": "hbm", "achieved": algo / ms / 1e6,
                              "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": algo / ms / 1e6 / pk["hbm_gbs"],
                              "peak_kind": kind, "algorithmic_bytes": algo}}
     elif args.op == "hex":
@@ -503,7 +550,7 @@ def main():
     ap.add_argument("--ref-sample", type=int, default=4)
     ap.add_argument("--latency", type=int, default=1)
     ap.add_argument("--gemm", default="tcgen05-ln", help="dense projection path (see model.Engine)")
-    ap.add_argument("--op", default=None, choices=["hex", "axial", "resid_ln"],
+    ap.add_argument("--op", default=None, choices=["hex", "axial", "resid_ln", "radius"],
                     help="time one isolated-op workload instead of the evaluator (config 3 / config 2 / the "
                          "fused projection + residual + LayerNorm launch)")
     ap.add_argument("--rows", type=int, default=1814720, help="rows of --op resid_ln (default: one chunk's windows)")

@@ -39,6 +39,8 @@ SIGNATURES = {
     "mb_hex_message_pass": "pllpppplp",
     "mb_gemm_rows_ln": "pllppplfpppilpppilpppilp",
     "mb_axial_attention": "pppliillllpppplllp",
+    "mb_radius_pack_edges": "ppppplllllpp",
+    "mb_radius_read": "plppllliiplpppppppllpilp",
     "mb_stone_attention": "pppiliilllplplipilllp",
     "mb_window_latent_read": "plpplilliipppippp",
     "mb_window_latent_broadcast": "plpplilliippippp",

@@ -4,6 +4,7 @@
 #include "tables.cu"
 #include "rows.cu"
 #include "attention.cu"
+#include "radius.cu"
 #include "gemm_simt.cu"
 #include "gemm_sm100.cu"
 #include "attention_sm100.cu"

@@ -351,7 +351,7 @@ class _Tables:
     by every block (the reference recomputes them in the trunk prologue,
     model.py:914-936)."""
 
-    def __init__(self, cfg: MantisConfig, b: Batch):
+    def __init__(self, cfg: MantisConfig, b: Batch, cd: torch.dtype = torch.bfloat16):
         dev = b.stone_own.device
         self.P = int(b.attn_valid.shape[0])
         self.N_s = int(b.stone_own.shape[0])
@@ -391,6 +391,16 @@ class _Tables:
             self.r_ptr = ops.csr(r_sorted, self.N_c)
             self.cell_off = ops.csr(b.cell_pos, self.P)  # cells are laid out position by position
             self.skip = self.cell_ptr if cfg.cell_node_scope == "uncovered" else None
+            self.r_pack = self.r_order = None
+            if ops.radius_supported(cfg.heads, cfg.h, cd):
+                # shared by every block's radius read: packed edges, and each
+                # position's cells ordered by edge count
+                self.r_pack = ops.radius_pack(self.r_src, self.r_cls, self.r_ptr, self.cell_off, self.stone_off,
+                                              self.N_s, RADIUS_CLASSES)
+                deg = (self.r_ptr[1:] - self.r_ptr[:-1]).clamp(max=63)
+                if self.skip is not None:
+                    deg = deg * (self.skip[1:] == self.skip[:-1])
+                _, self.r_order = ops.argsort(b.cell_pos * 64 + deg, self.P * 64)
         if cfg.cell_adjacency:
             a_sorted, aorder = ops.argsort(b.adjacency_dst, self.N_c)
             self.a_src = ops.gather_i64(b.adjacency_src, aorder)
@@ -675,7 +685,7 @@ class Engine:
         buffer; the values are the same rows rounded where the reference's
         autocast GEMMs round them."""
         cfg, cd, h = self.cfg, self.cd, self.h
-        T = _Tables(cfg, b)
+        T = _Tables(cfg, b, cd)
         self.tables = T
         dev = b.stone_own.device
         direct = for_heads and cfg.uses_cell_state and cfg.cell_nodes
@@ -824,8 +834,13 @@ class Engine:
                 (zc_rad,) = self.update(c, reads, [blk["ln_radius_c"]])
             q = self.linear(zc_rad, blk["radius_wq"])
             kv = self.ln_linear(s, blk["ln_radius_s"], blk["radius_kv"])
+            stage = self.radius_stage_rows if self.radius_stage_rows is not None else T.max_t - GLOBAL_ROWS
             with self.timed("radius_read"):
-                if ops.grouped_supported(cfg.heads, h, cd):
+                if T.r_pack is not None:
+                    read = ops.radius_read(q, kv[:, :h], kv[:, h:], blk["radius_bias"], blk["radius_vclass"], T.r_ptr,
+                                           T.r_pack, T.cell_off, T.stone_off, stage, order=T.r_order,
+                                           skip_ptr=T.skip, out_dtype=cd)
+                elif ops.grouped_supported(cfg.heads, h, cd):
                     # block-diagonal: position p's cells read only position p's stones
                     read = ops.segment_attention_grouped(
                         q, kv[:, :h], kv[:, h:], blk["radius_bias"], blk["radius_vclass"], T.r_ptr, T.r_src,
@@ -860,8 +875,9 @@ class Engine:
             zc_wr, zc_out = self.update(c, None, [blk["ln_wr_c"], exit_ln])
         q = self.linear(zw_wr, blk["wr_wq"])
         kv = self.linear(zc_wr, blk["wr_kv"])
-        back = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["wr_bias"], None, T.win_ptr, T.edge_wcell,
-                                     T.edge_wclass, out_dtype=cd)
+        with self.timed("window_read"):
+            back = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["wr_bias"], None, T.win_ptr, T.edge_wcell,
+                                         T.edge_wclass, out_dtype=cd)
         if nxt is not None:
             return back, c, zc_out, None
         return back, c, None, zc_out
@@ -872,7 +888,7 @@ class Engine:
         cfg, cd, h = self.cfg, self.cd, self.h
         T = getattr(self, "tables", None)
         if T is None or T.N_c != b.cell_pos.shape[0]:
-            T = _Tables(cfg, b)
+            T = _Tables(cfg, b, cd)
         n_c = T.N_c
         pre = self.linear(w.to(cd), self.act_proj)
         # decoder input [cells | action rows]; the evaluate path's trunk has

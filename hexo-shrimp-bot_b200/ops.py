@@ -197,6 +197,51 @@ def segment_attention_grouped(q, k, v, bias, vcls, seg_ptr, src, cls, q_off, s_o
     return out
 
 
+def radius_pack(src, cls, seg_ptr, q_off, s_off, n_src: int, n_cls: int) -> torch.Tensor:
+    """int32 packed radius edges (local stone << 11 | class) for
+    ``radius_read``; computed once per forward, shared by every block."""
+    _cuda(src, cls, seg_ptr, q_off, s_off)
+    for t, n in ((src, "src"), (cls, "cls"), (seg_ptr, "seg_ptr"), (q_off, "q_off"), (s_off, "s_off")):
+        _i64(t, n)
+    packed = torch.empty(src.shape[0], dtype=torch.int32, device=src.device)
+    call("mb_radius_pack_edges", ptr(src), ptr(cls), ptr(seg_ptr), ptr(q_off), ptr(s_off), q_off.shape[0] - 1,
+         seg_ptr.shape[0] - 1, src.shape[0], n_src, n_cls, ptr(packed), stream_of(src.device))
+    return packed
+
+
+def radius_read(q, k, v, bias, vcls, seg_ptr, packed, q_off, s_off, stage_rows, order=None, skip_ptr=None, out=None,
+                out_dtype=torch.bfloat16):
+    """The radius read on packed edges: same result as
+    ``segment_attention_grouped`` up to float rounding. head_dim 32, bf16
+    q/k/v (and class value rows)."""
+    _cuda(q, k, v, bias, seg_ptr, packed, q_off, s_off)
+    for t, n in ((q, "q"), (k, "k"), (v, "v")):
+        _rowmajor(t, n)
+    if k.stride(0) != v.stride(0):
+        raise ValueError("k and v must share a row stride")
+    if not (q.dtype == k.dtype == v.dtype == torch.bfloat16):
+        raise ValueError("radius_read needs bf16 q, k and v")
+    if packed.dtype != torch.int32:
+        raise ValueError("packed edges must be int32 (radius_pack)")
+    heads = bias.shape[0]
+    n_q, width = q.shape
+    if out is None:
+        out = torch.empty(n_q, width, dtype=out_dtype, device=q.device)
+    bias32 = bias if (bias.dtype == torch.float32 and bias.is_contiguous()) else bias.float().contiguous()
+    if vcls is not None and not (vcls.dtype == torch.bfloat16 and vcls.is_contiguous()):
+        vcls = vcls.to(torch.bfloat16).contiguous()
+    call("mb_radius_read", ptr(q), q.stride(0), ptr(k), ptr(v), k.stride(0), n_q, k.shape[0], heads, width // heads,
+         ptr(bias32), bias32.shape[1], ptr(vcls), ptr(seg_ptr), ptr(packed), ptr(skip_ptr), ptr(q_off), ptr(s_off),
+         ptr(order), q_off.shape[0] - 1, max(int(stage_rows), 1), ptr(out), dtype_code(out.dtype), out.stride(0),
+         stream_of(q.device))
+    return out
+
+
+def radius_supported(heads: int, width: int, dtype) -> bool:
+    """Whether ``radius_read`` takes this shape."""
+    return dtype == torch.bfloat16 and width == heads * 32 and width % 64 == 0
+
+
 def grouped_supported(heads: int, width: int, dtype) -> bool:
     """Whether ``segment_attention_grouped`` takes this shape."""
     hd = width // heads

@@ -151,6 +151,27 @@ int mb_segment_attention_grouped(const void* q, int64_t ldq, const void* k, cons
                                  int64_t n_groups, int64_t stage_rows, void* out, int out_dtype, int64_t ldo,
                                  void* stream);
 
+/* The radius read (cells <- stones within distance 8) in two steps, for the
+ * trunk's blocks to share the first (model.py:439-451 with the radius tables
+ * of model.py:864-875; kernel cell_latents.py:213-285).
+ * mb_radius_pack_edges: packed[e] = (src[e] - s_off[g]) << 11 | cls[e] for
+ * every edge of group g's rows [q_off[g], q_off[g+1]) (edges [seg_ptr[q_off[g]],
+ * seg_ptr[q_off[g+1]])), -1 (and a device error) where the stone is not one
+ * of the group's [s_off[g], s_off[g+1]) or the class is not below n_cls
+ * (n_cls <= 2048, fewer than 2^20 stones per group).
+ * mb_radius_read: the result of mb_segment_attention_grouped on the packed
+ * edges (head_dim 32, bf16 q/k/v and class rows, fp32 bias), rows of each
+ * group visited in the order `order` gives (a permutation of the group's own
+ * rows, NULL = ascending; the engine orders them by edge count). */
+int mb_radius_pack_edges(const int64_t* src, const int64_t* cls, const int64_t* seg_ptr, const int64_t* q_off,
+                         const int64_t* s_off, int64_t n_groups, int64_t n_q, int64_t n_edges, int64_t n_src,
+                         int64_t n_cls, int32_t* packed, void* stream);
+int mb_radius_read(const void* q, int64_t ldq, const void* k, const void* v, int64_t ldkv, int64_t n_q, int64_t n_src,
+                   int heads, int head_dim, const float* bias, int64_t n_cls, const void* vcls,
+                   const int64_t* seg_ptr, const int32_t* packed, const int64_t* skip_ptr, const int64_t* q_off,
+                   const int64_t* s_off, const int64_t* order, int64_t n_groups, int64_t stage_rows, void* out,
+                   int out_dtype, int64_t ldo, void* stream);
+
 /* Block-diagonal stone attention over [4 latents; stones] per position.
  * Padded mode (tok_off == NULL): q/k/v/out element (p, a, t, d) at
  * p*s_pos + a*s_head + t*s_row + d, keys t < seq_lens[p] live, query rows

@@ -313,3 +313,61 @@ def test_native_linear(dtype):
     got = ops.linear_native(a.to(DEV), w.to(DEV), b.to(DEV), relu=True, out_dtype=torch.float32)
     want = torch.relu(a.float() @ w.float().t() + b)
     torch.testing.assert_close(got.cpu(), want, rtol=1e-4, atol=1e-4)
+
+
+# ------------------------------------------------ radius read on packed edges
+def _degree_order(seg_ptr, q_off):
+    """Each group's rows by ascending run length (the engine's order)."""
+    runs = seg_ptr[1:] - seg_ptr[:-1]
+    grp = torch.repeat_interleave(torch.arange(q_off.numel() - 1, device=seg_ptr.device), q_off[1:] - q_off[:-1])
+    return torch.argsort(grp * 4096 + runs, stable=True)
+
+
+@pytest.mark.parametrize("heads", [8, 2])
+@pytest.mark.parametrize("vdt", [None, torch.bfloat16])
+@pytest.mark.parametrize("odt", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("ordered", [False, True])
+def test_radius_read_matches_generic(heads, vdt, odt, ordered):
+    q, kv, bias, vcls, seg_ptr, src, cls, q_off, s_off, runs = (
+        x.to(DEV) for x in _grouped_case(heads, 32, heads * 77 + 5))
+    h = heads * 32
+    vc = None if vdt is None else vcls.to(vdt)
+    packed = ops.radius_pack(src, cls, seg_ptr, q_off, s_off, kv.shape[0], bias.shape[1])
+    order = _degree_order(seg_ptr, q_off) if ordered else None
+    want = ops.segment_attention(q, kv[:, :h], kv[:, h:], bias, vc, seg_ptr, src, cls, out_dtype=torch.float32)
+    for stage in (1024, 64, 1):  # all staged; the 400-source group from global memory; every group from global
+        got = ops.radius_read(q, kv[:, :h], kv[:, h:], bias, vc, seg_ptr, packed, q_off, s_off, stage, order=order,
+                              out_dtype=odt)
+        torch.cuda.synchronize()
+        tol = 1e-5 if odt == torch.float32 else 8e-3
+        torch.testing.assert_close(got.float(), want, rtol=tol, atol=tol, msg=f"stage_rows={stage}")
+    skip = torch.cat([torch.zeros(1, dtype=torch.long, device=DEV),
+                      (torch.arange(q.shape[0], device=DEV) % 3 == 0).long().cumsum(0)])
+    want = ops.segment_attention(q, kv[:, :h], kv[:, h:], bias, vc, seg_ptr, src, cls, skip_ptr=skip,
+                                 out_dtype=torch.float32)
+    got = ops.radius_read(q, kv[:, :h], kv[:, h:], bias, vc, seg_ptr, packed, q_off, s_off, 1024, order=order,
+                          skip_ptr=skip, out_dtype=odt)
+    tol = 1e-5 if odt == torch.float32 else 8e-3
+    torch.testing.assert_close(got.float(), want, rtol=tol, atol=tol, msg="skip")
+    mb._lib.check_device_error()
+
+
+def test_radius_read_against_oracle_and_bad_edge():
+    q, kv, bias, vcls, seg_ptr, src, cls, q_off, s_off, runs = _grouped_case(8, 32, 11)
+    qid = torch.repeat_interleave(torch.arange(q.shape[0]), runs)
+    d = [x.to(DEV) for x in (q, kv, bias, vcls, seg_ptr, src, cls, q_off, s_off)]
+    packed = ops.radius_pack(d[5], d[6], d[4], d[7], d[8], kv.shape[0], 192)
+    got = ops.radius_read(d[0], d[1][:, :256], d[1][:, 256:], d[2], d[3].to(torch.bfloat16), d[4], packed, d[7],
+                          d[8], 1024, order=_degree_order(d[4], d[7]), out_dtype=torch.float32)
+    want = O.segment_attention(q.float().view(-1, 8, 32), kv[:, :256].float().view(-1, 8, 32),
+                               kv[:, 256:].float().view(-1, 8, 32), bias, vcls.to(torch.bfloat16).float(), src, cls,
+                               qid)
+    torch.testing.assert_close(got.view(-1, 8, 32).cpu(), want, rtol=1e-5, atol=2e-5)
+    mb._lib.check_device_error()
+    bad = d[5].clone()
+    bad[0] = int(s_off[3])  # a row of group 0 naming a stone of group 3: refused when packing
+    packed = ops.radius_pack(bad, d[6], d[4], d[7], d[8], kv.shape[0], 192)
+    assert int(packed[0]) == -1
+    with pytest.raises(ValueError, match="out of range"):
+        mb._lib.check_device_error()
+    mb._lib.check_device_error()  # cleared
