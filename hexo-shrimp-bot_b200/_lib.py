@@ -41,6 +41,7 @@ SIGNATURES = {
     "mb_axial_attention": "pppliillllpppplllp",
     "mb_radius_pack_edges": "ppppplllllpp",
     "mb_radius_read": "plppllliiplpppppppllpilp",
+    "mb_stone_attention_engine": "i",
     "mb_stone_attention": "pppiliilllplplipilllp",
     "mb_window_latent_read": "plpplilliipppippp",
     "mb_window_latent_broadcast": "plpplilliippippp",

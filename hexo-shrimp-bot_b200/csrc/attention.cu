@@ -442,6 +442,9 @@ __global__ void __launch_bounds__(kGrpWarps * 32, 2) segment_attention_grouped_k
 }
 
 // --------------------------------------------------------- stone attention
+// Whether mb_stone_attention takes the tensor-core kernel for the shapes it
+// serves (1, the default) or always the CUDA-core kernel below (0).
+static int g_stone_tc = 1;
 constexpr int kStoneThreads = 128;
 constexpr int kKeyTile = 64;
 
@@ -915,6 +918,17 @@ int mb_segment_attention_grouped(const void* q, int64_t ldq, const void* k, cons
   return launch_status("segment_attention_grouped");
 }
 
+}  // extern "C"
+
+// Defined with the tcgen05 kernels (stone_sm100.cu): the tensor-core path of
+// mb_stone_attention, -1 when it does not take the shape.
+static int stone_attention_tc(const void* q, const void* k, const void* v, int dtype, int64_t n_pos, int heads,
+                              int head_dim, int64_t s_pos, int64_t s_head, int64_t s_row, const int32_t* seq_lens,
+                              int64_t t_pad, const int64_t* tok_off, int64_t max_tokens, int max_queries, void* out,
+                              int out_dtype, int64_t o_pos, int64_t o_head, int64_t o_row, cudaStream_t s);
+
+extern "C" {
+
 int mb_stone_attention(const void* q, const void* k, const void* v, int dtype, int64_t n_pos, int heads, int head_dim,
                        int64_t s_pos, int64_t s_head, int64_t s_row, const int32_t* seq_lens, int64_t t_pad,
                        const int64_t* tok_off, int64_t max_tokens, int max_queries, void* out, int out_dtype,
@@ -927,6 +941,13 @@ int mb_stone_attention(const void* q, const void* k, const void* v, int dtype, i
   MB_REQUIRE(n_pos <= 65535 && heads <= 65535, "stone_attention: grid too large");
   const int64_t rows = tok_off ? (max_queries >= 0 ? max_queries : max_tokens) : t_pad;
   if (rows <= 0) return MB_OK;
+  // bf16, head_dim 32, at most 320 keys: QK^T and PV on the tensor cores
+  if (g_stone_tc) {
+    const int rc = stone_attention_tc(q, k, v, dtype, n_pos, heads, head_dim, s_pos, s_head, s_row, seq_lens, t_pad,
+                                      tok_off, max_tokens, max_queries, out, out_dtype, o_pos, o_head, o_row,
+                                      as_stream(stream));
+    if (rc >= 0) return rc;
+  }
   dim3 grid((unsigned)cdiv(rows, kStoneThreads), (unsigned)n_pos, (unsigned)heads);
   const float scale = 1.f / sqrtf((float)head_dim);
   cudaStream_t s = as_stream(stream);
@@ -947,6 +968,12 @@ int mb_stone_attention(const void* q, const void* k, const void* v, int dtype, i
 }
 
 static int latent_vec(int heads, int head_dim) { return attn_vec(heads, head_dim); }
+
+int mb_stone_attention_engine(int tensor_cores) {
+  MB_REQUIRE(tensor_cores == 0 || tensor_cores == 1, "stone_attention_engine: 0 or 1");
+  g_stone_tc = tensor_cores;
+  return MB_OK;
+}
 
 int mb_window_latent_read(const void* q, int64_t ldq, const void* k, const void* v, int64_t ldkv, int dtype,
                           int64_t n_pos, int64_t n_windows, int heads, int head_dim, const int64_t* offsets,

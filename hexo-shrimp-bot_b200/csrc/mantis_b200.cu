@@ -8,6 +8,7 @@
 #include "gemm_simt.cu"
 #include "gemm_sm100.cu"
 #include "attention_sm100.cu"
+#include "stone_sm100.cu"
 #include "noalloc.cu"
 #include "encoder.cu"
 #include "klent.cu"

@@ -187,6 +187,13 @@ int mb_stone_attention(const void* q, const void* k, const void* v, int dtype, i
                        const int64_t* tok_off, int64_t max_tokens, int max_queries,
                        void* out, int out_dtype, int64_t o_pos, int64_t o_head, int64_t o_row, void* stream);
 
+/* Engine of mb_stone_attention: 1 (the default) runs bf16 head_dim-32
+ * calls with at most 320 keys per position on the tensor cores (S = Q K^T
+ * and P V with tcgen05.mma, fp32 softmax, P rounded to bf16 for the second
+ * product), 0 keeps every call on the CUDA-core kernel (fp32 P). Process-wide,
+ * a measurement knob. No counterpart in the reference. */
+int mb_stone_attention_engine(int tensor_cores);
+
 /* Window-latent read: four latent queries per position attend over the
  * position's windows (order[offsets[p]..offsets[p+1]]). q (P, 4, H), k/v
  * (N_w, H), out (P, 4, H). m/l (P, 4, heads) may be NULL.

@@ -371,3 +371,65 @@ def test_radius_read_against_oracle_and_bad_edge():
     with pytest.raises(ValueError, match="out of range"):
         mb._lib.check_device_error()
     mb._lib.check_device_error()  # cleared
+
+
+# ------------------------------------------------ stone attention on tcgen05
+def _ragged_tokens(lengths, heads, seed):
+    g = torch.Generator().manual_seed(seed)
+    tok_off = torch.tensor([0] + list(lengths)).cumsum(0)
+    qkv = (torch.randn(int(tok_off[-1]), 3 * heads * 32, generator=g) * 1.5).to(torch.bfloat16)
+    return qkv, tok_off
+
+
+def _ragged_oracle(qkv, tok_off, heads, max_queries=-1):
+    h = heads * 32
+    outs = []
+    for p in range(tok_off.numel() - 1):
+        a, b = int(tok_off[p]), int(tok_off[p + 1])
+        x = qkv[a:b].float()
+        q, k, v = (x[:, i * h:(i + 1) * h].view(b - a, heads, 32).transpose(0, 1) for i in range(3))
+        o = torch.softmax(q @ k.transpose(1, 2) / 32 ** 0.5, -1) @ v
+        o = o.transpose(0, 1).reshape(b - a, h)
+        outs.append(o[:max_queries] if max_queries >= 0 else o)
+    return torch.cat(outs)
+
+
+@pytest.mark.parametrize("lengths", [[4, 5, 37, 128, 129, 200], [304, 4, 257, 320, 300], [64, 63, 65, 256]])
+@pytest.mark.parametrize("engine", [1, 0])
+def test_stone_attention_ragged_tensor_cores(lengths, engine):
+    """[latents; stones] attention on the ragged token layout at the lengths
+    of late positions (T up to 320 keys, past one 256-column MMA and two
+    128-query tiles), on the tensor cores (engine 1) and on the CUDA cores
+    (engine 0), against fp32 attention on the same bf16 rows; the latent-only
+    read of the last block (max_queries = 4, compact output) too."""
+    heads = 8
+    qkv, tok_off = _ragged_tokens(lengths, heads, sum(lengths))
+    mb._lib.call("mb_stone_attention_engine", engine)
+    try:
+        d = qkv.to(DEV)
+        to = tok_off.to(DEV)
+        got = ops.stone_attention_ragged(d, to, heads, max(lengths))
+        lat = ops.stone_attention_ragged(d, to, heads, max(lengths), max_queries=4, out_dtype=torch.float32)
+        torch.cuda.synchronize()
+    finally:
+        mb._lib.call("mb_stone_attention_engine", 1)
+    want = _ragged_oracle(qkv, tok_off, heads)
+    torch.testing.assert_close(got.float().cpu(), want, rtol=2e-2, atol=2e-2)
+    want4 = _ragged_oracle(qkv, tok_off, heads, 4)
+    torch.testing.assert_close(lat.cpu(), want4, rtol=1e-2, atol=1e-2)
+    mb._lib.check_device_error()
+
+
+def test_stone_attention_padded_tensor_cores_zero_pad_rows():
+    """The padded (P, A, T, D) entry (mantisnet::fused_attention) on the
+    tensor cores: rows past seq_lens read zero, a position with one key."""
+    g = torch.Generator().manual_seed(9)
+    p, t = 4, 300
+    base = torch.randn(3, p, t, 8, 32, generator=g).to(torch.bfloat16)
+    q, k, v = (base[i].to(DEV).transpose(1, 2) for i in range(3))
+    seq = torch.tensor([300, 1, 129, 64], dtype=torch.int32)
+    out = ops.fused_attention(q, k, v, seq.to(DEV))
+    want = O.stone_attention(q.float().cpu(), k.float().cpu(), v.float().cpu(), seq.long())
+    torch.testing.assert_close(out.float().cpu(), want, rtol=2e-2, atol=2e-2)
+    assert torch.count_nonzero(out[1, :, 1:]) == 0 and torch.count_nonzero(out[2, :, 129:]) == 0
+    mb._lib.check_device_error()
