@@ -55,6 +55,7 @@ SIGNATURES = {
     "mb_tokens_gather": "ppppllpp",
     "mb_tokens_scatter_add": "ppppllpiip",
     "mb_latent_mean": "pllpp",
+    "mb_value_head": "ppillpppplllppfpippippippppp",
     "mb_compose_q": "plplfppp",
     "mb_linear": "pilllpiplipilp",
     "mb_gemm_weight_image": "pllpp",

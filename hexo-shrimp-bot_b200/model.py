@@ -937,19 +937,12 @@ class Engine:
         return self.heads(w, g, cells, b)
 
     def value_head(self, w: Tensor, g: Tensor, b: Batch):
-        """model.py:1160-1183 (full forward only; KLENT skips it)."""
-        cfg, h = self.cfg, self.h
-        p, max_w = g.shape[0], b.value_valid.shape[1]
-        rows = torch.zeros(p * max_w, h, dtype=torch.float32, device=g.device)
-        rows[torch.arange(p, device=g.device) * max_w] = self.ln(g.float().contiguous(), self.ln_value,
-                                                                 dtype=torch.float32)
-        if b.window_slot.numel():
-            rows[b.window_slot] = self.ln(w.float().contiguous(), self.ln_value, dtype=torch.float32)
-        kv = rows.view(p, max_w, h)
-        sc = torch.einsum("qh,pth->pqt", self.value_queries, kv) / math.sqrt(h)
-        sc = sc.masked_fill(~b.value_valid[:, None, :], torch.finfo(sc.dtype).min)
-        r = torch.einsum("pqt,pth->pqh", sc.softmax(-1), kv)
-        hid = F.relu(F.linear(r.reshape(p, -1), *self.mlp_v0))
-        logits = F.linear(hid, *self.mlp_v2)
-        dist = logits.softmax(-1)
-        return dist @ self.bin_centers, dist, logits
+        """model.py:1160-1183 (full forward only; KLENT skips it): one kernel
+        per batch (ops.value_head)."""
+        T = getattr(self, "tables", None)
+        if T is None or T.N_w != b.window_feat.shape[0] or T.P != g.shape[0]:
+            T = _Tables(self.cfg, b, self.cd)
+        w = w if w.stride(1) == 1 else w.contiguous()
+        return ops.value_head(g.float().contiguous(), w, T.wl_off, T.wl_order, b.window_slot, b.value_valid,
+                              self.ln_value.g, self.ln_value.b, self.value_queries, self.mlp_v0[0], self.mlp_v0[1],
+                              self.mlp_v2[0], self.mlp_v2[1], self.bin_centers)

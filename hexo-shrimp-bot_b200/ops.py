@@ -398,6 +398,36 @@ def latent_mean(g_ln, n_pos):
     return out
 
 
+def value_head(g, w, win_off, win_order, window_slot, value_valid, ln_g, ln_b, queries, w1, b1, w2, b2, centers,
+               eps=1e-5):
+    """(value (P,), value_dist (P, bins), value_logits (P, bins)) of the
+    full forward's value readout (reference model.py:1160-1183) in one
+    kernel: g (P, h) fp32 token rows, w (N_w, h) window rows (fp32 or bf16),
+    the windows of position p at win_order[win_off[p]:win_off[p+1]]."""
+    _cuda(g, w, win_off, window_slot, value_valid, queries, w1, w2)
+    _rowmajor(g, "g")
+    _rowmajor(w, "w")
+    for t, n in ((win_off, "win_off"), (window_slot, "window_slot")):
+        _i64(t, n)
+    if win_order is not None:
+        _i64(win_order, "win_order")
+    p, h = g.shape
+    nq = queries.shape[0]
+    vh, bins = w1.shape[0], w2.shape[0]
+    if w1.shape[1] != nq * h or w2.shape[1] != vh:
+        raise ValueError("value head weights do not match the queries and width")
+    f = lambda t: t.float().contiguous()
+    vv = value_valid.to(torch.bool).contiguous()
+    value = torch.empty(p, dtype=torch.float32, device=g.device)
+    dist = torch.empty(p, bins, dtype=torch.float32, device=g.device)
+    logits = torch.empty(p, bins, dtype=torch.float32, device=g.device)
+    call("mb_value_head", ptr(g), ptr(w), dtype_code(w.dtype), w.stride(0), w.shape[0], ptr(win_off), ptr(win_order),
+         ptr(window_slot), ptr(vv), p, vv.shape[1], h, ptr(f(ln_g)), ptr(f(ln_b)), float(eps), ptr(f(queries)), nq,
+         ptr(f(w1)), ptr(f(b1)), vh, ptr(f(w2)), ptr(f(b2)), bins, ptr(f(centers)), ptr(value), ptr(dist),
+         ptr(logits), stream_of(g.device))
+    return value, dist, logits
+
+
 def compose(critic, offsets, mass_floor):
     """(q_score, q_values) from (N, 3) fp32 logits (model.py:177-220)."""
     critic = critic.float()

@@ -267,6 +267,22 @@ int mb_tokens_scatter_add(float* g, float* s, const int64_t* stone_off, const in
 /* Mean of ln(g) over the 4 latent rows: out (P, h) fp32 (model.py:973). */
 int mb_latent_mean(const float* g_ln, int64_t n_pos, int64_t h, float* out, void* stream);
 
+/* Value head (model.py:1160-1183): per position p the rows [g[p]; its
+ * windows (win_order[win_off[p] .. win_off[p+1]), NULL order = identity)],
+ * each LayerNorm'd with (ln_g, ln_b, eps), are read by nq <= 4 queries
+ * (queries (nq, h) fp32) with one head of width h, scores scaled by
+ * 1/sqrt(h) and slots (window_slot - p * max_w; 0 for g[p]) that value_valid
+ * (n_pos, max_w) marks invalid left out; the nq read rows, concatenated,
+ * go through relu(w1 x + b1) (w1 (vh, nq * h)) and w2 x + b2 (w2 (bins, vh))
+ * to logits, whose softmax is dist and whose expectation over centers is
+ * value. g (n_pos, h) fp32, w (n_windows, ldw) f32 or bf16; all fp32 math.
+ * h in {32, 64, 128, 256, 512}, vh and bins <= 256. */
+int mb_value_head(const float* g, const void* w, int w_dtype, int64_t ldw, int64_t n_windows, const int64_t* win_off,
+                  const int64_t* win_order, const int64_t* window_slot, const uint8_t* value_valid, int64_t n_pos,
+                  int64_t max_w, int64_t h, const float* ln_g, const float* ln_b, float eps, const float* queries,
+                  int nq, const float* w1, const float* b1, int vh, const float* w2, const float* b2, int bins,
+                  const float* centers, float* value, float* dist, float* logits, void* stream);
+
 /* Q composition (model.py:177-220, segments.py:24-31): per cell
  * p = softmax(critic[c, 0:3]); q_values = p0 - p1;
  * q_score = q_values / max(max over the position's cells of (p0 + p1), floor). */
