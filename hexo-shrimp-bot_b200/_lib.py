@@ -42,7 +42,7 @@ SIGNATURES = {
     "mb_radius_pack_edges": "ppppplllllpp",
     "mb_radius_read": "plppllliiplpppppppllpilp",
     "mb_stone_attention_engine": "i",
-    "mb_stone_attention": "pppiliilllplplipilllp",
+    "mb_stone_attention": "pppiliilllplplipilllpp",
     "mb_window_latent_read": "plpplilliipppippp",
     "mb_window_latent_broadcast": "plpplilliippippp",
     "mb_latent_mix": "pppliliipip",

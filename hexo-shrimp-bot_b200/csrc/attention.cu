@@ -452,7 +452,8 @@ template <typename T, typename TO, int D>
 __global__ void __launch_bounds__(kStoneThreads) stone_attention_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v, int64_t s_pos, int64_t s_head,
     int64_t s_row, const int32_t* __restrict__ seq_lens, int64_t t_pad, const int64_t* __restrict__ tok_off,
-    int max_queries, TO* __restrict__ out, int64_t o_pos, int64_t o_head, int64_t o_row, float scale) {
+    int max_queries, TO* __restrict__ out, int64_t o_pos, int64_t o_head, int64_t o_row, float* __restrict__ lse,
+    int heads, float scale) {
   __shared__ float ks[kKeyTile][D];
   __shared__ float vs[kKeyTile][D];
   const int64_t p = blockIdx.y;
@@ -535,6 +536,8 @@ __global__ void __launch_bounds__(kStoneThreads) stone_attention_kernel(
 #pragma unroll
     for (int i = 0; i < D; ++i) acc[i] *= inv;
     store_vec<D>(out + base_out + t * o_row, acc);
+    // log-sum-exp of the scaled scores (0 for a padded query row), padded layout (P, heads, t_pad)
+    if (lse && !tok_off) lse[(p * heads + a) * t_pad + t] = (active && l > 0.f) ? m + logf(l) : 0.f;
   }
 }
 
@@ -925,15 +928,17 @@ int mb_segment_attention_grouped(const void* q, int64_t ldq, const void* k, cons
 static int stone_attention_tc(const void* q, const void* k, const void* v, int dtype, int64_t n_pos, int heads,
                               int head_dim, int64_t s_pos, int64_t s_head, int64_t s_row, const int32_t* seq_lens,
                               int64_t t_pad, const int64_t* tok_off, int64_t max_tokens, int max_queries, void* out,
-                              int out_dtype, int64_t o_pos, int64_t o_head, int64_t o_row, cudaStream_t s);
+                              int out_dtype, int64_t o_pos, int64_t o_head, int64_t o_row, float* lse,
+                              cudaStream_t s);
 
 extern "C" {
 
 int mb_stone_attention(const void* q, const void* k, const void* v, int dtype, int64_t n_pos, int heads, int head_dim,
                        int64_t s_pos, int64_t s_head, int64_t s_row, const int32_t* seq_lens, int64_t t_pad,
                        const int64_t* tok_off, int64_t max_tokens, int max_queries, void* out, int out_dtype,
-                       int64_t o_pos, int64_t o_head, int64_t o_row, void* stream) {
+                       int64_t o_pos, int64_t o_head, int64_t o_row, float* lse, void* stream) {
   MB_REQUIRE(valid_dtype(dtype) && valid_dtype(out_dtype), "stone_attention: bad dtype");
+  MB_REQUIRE(!lse || !tok_off, "stone_attention: the log-sum-exp output takes the padded layout");
   MB_REQUIRE(head_dim == 16 || head_dim == 32 || head_dim == 64, "stone_attention: head_dim %d unsupported", head_dim);
   if (n_pos == 0) return MB_OK;
   MB_REQUIRE(q && k && v && out, "stone_attention: null pointer");
@@ -944,7 +949,7 @@ int mb_stone_attention(const void* q, const void* k, const void* v, int dtype, i
   // bf16, head_dim 32, at most 320 keys: QK^T and PV on the tensor cores
   if (g_stone_tc) {
     const int rc = stone_attention_tc(q, k, v, dtype, n_pos, heads, head_dim, s_pos, s_head, s_row, seq_lens, t_pad,
-                                      tok_off, max_tokens, max_queries, out, out_dtype, o_pos, o_head, o_row,
+                                      tok_off, max_tokens, max_queries, out, out_dtype, o_pos, o_head, o_row, lse,
                                       as_stream(stream));
     if (rc >= 0) return rc;
   }
@@ -957,7 +962,7 @@ int mb_stone_attention(const void* q, const void* k, const void* v, int dtype, i
         constexpr int D = decltype(dtag)::value;
         stone_attention_kernel<T, TO, D><<<grid, kStoneThreads, 0, s>>>(
             (const T*)q, (const T*)k, (const T*)v, s_pos, s_head, s_row, seq_lens, t_pad, tok_off, max_queries,
-            (TO*)out, o_pos, o_head, o_row, scale);
+            (TO*)out, o_pos, o_head, o_row, lse, heads, scale);
       };
       if (head_dim == 16) go(std::integral_constant<int, 16>{});
       else if (head_dim == 32) go(std::integral_constant<int, 32>{});

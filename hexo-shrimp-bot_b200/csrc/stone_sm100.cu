@@ -43,7 +43,8 @@ template <typename TO>
 __global__ void __launch_bounds__(ST_THREADS, 1) stone_attention_tc_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v, int64_t s_pos, int64_t s_head,
     int64_t s_row, const int32_t* __restrict__ seq_lens, int64_t t_pad, const int64_t* __restrict__ tok_off,
-    int max_queries, int heads, TO* __restrict__ out, int64_t o_pos, int64_t o_head, int64_t o_row, float scale) {
+    int max_queries, int heads, TO* __restrict__ out, int64_t o_pos, int64_t o_head, int64_t o_row,
+    float* __restrict__ lse, float scale) {
   extern __shared__ uint8_t st_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(st_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* qs = smem + ST_Q_OFF;
@@ -216,13 +217,17 @@ __global__ void __launch_bounds__(ST_THREADS, 1) stone_attention_tc_kernel(
       const int64_t row = (int64_t)t * 128 + rl;
       ok = ok && mbar_wait(smem_u32(o_done), t & 1, abort);
       tc_fence_after();
+      float row_lse = 0.f;
       if (ok) {
         tmem_ld32(taddr + ST_O_COL, o);
         const float tot = red[rl] + red[128 + rl];
         const float inv = tot > 0.f ? 1.f / tot : 0.f;
 #pragma unroll
         for (int i = 0; i < ST_D; ++i) o[i] *= inv;
+        if (tot > 0.f) row_lse = m + logf(tot);
       }
+      // log-sum-exp of the scaled scores (0 for a padded query row), padded layout (P, heads, t_pad)
+      if (lse && !tok_off && row < n_rows) lse[(p * heads + a) * t_pad + row] = row < nk ? row_lse : 0.f;
       if (row < n_rows) {
         if (row >= nk) {  // padded query rows read zero
 #pragma unroll
@@ -264,7 +269,8 @@ using namespace mb;
 static int stone_attention_tc(const void* q, const void* k, const void* v, int dtype, int64_t n_pos, int heads,
                               int head_dim, int64_t s_pos, int64_t s_head, int64_t s_row, const int32_t* seq_lens,
                               int64_t t_pad, const int64_t* tok_off, int64_t max_tokens, int max_queries, void* out,
-                              int out_dtype, int64_t o_pos, int64_t o_head, int64_t o_row, cudaStream_t s) {
+                              int out_dtype, int64_t o_pos, int64_t o_head, int64_t o_row, float* lse,
+                              cudaStream_t s) {
   using namespace sm100;
   const int64_t keys = tok_off ? max_tokens : t_pad;
   if (dtype != MB_BF16 || head_dim != ST_D || keys > ST_KEYS || n_pos * heads > INT32_MAX) return -1;
@@ -281,7 +287,7 @@ static int stone_attention_tc(const void* q, const void* k, const void* v, int d
     }
     kern<<<(unsigned)(n_pos * heads), ST_THREADS, ST_SMEM, s>>>(
         (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, s_pos, s_head, s_row, seq_lens,
-        t_pad, tok_off, max_queries, heads, (TO*)out, o_pos, o_head, o_row, scale);
+        t_pad, tok_off, max_queries, heads, (TO*)out, o_pos, o_head, o_row, lse, scale);
   });
   if (rc != MB_OK) return rc;
   return launch_status("stone_attention");

@@ -265,7 +265,7 @@ def stone_attention_ragged(qkv, tok_off, heads, max_tokens, max_queries=-1, out=
     call("mb_stone_attention", ptr(qkv), qkv.data_ptr() + h * es, qkv.data_ptr() + 2 * h * es,
          dtype_code(qkv.dtype), n_pos, heads, hd, 0, hd, qkv.stride(0), None, 0, ptr(tok_off), max_tokens,
          max_queries, ptr(out), dtype_code(out.dtype), max_queries * out.stride(0) if compact else 0, hd,
-         out.stride(0), stream_of(qkv.device))
+         out.stride(0), None, stream_of(qkv.device))
     return out
 
 
@@ -707,10 +707,12 @@ def cell_pass(x, emb, cell_ptr, edge_window, edge_class, win_ptr, edge_wcell, cl
     return out
 
 
-def fused_attention(q, k, v, seq_lens):
+def fused_attention(q, k, v, seq_lens, with_lse: bool = False):
     """attention.py:892-904: block-diagonal attention over (P, A, T, D)
     (strided views allowed, inner stride 1); keys >= seq_lens[p] masked, pad
-    query rows zero. Output preserves q's strides like ``empty_like``."""
+    query rows zero. Output preserves q's strides like ``empty_like``. With
+    ``with_lse`` also the per-row log-sum-exp of the scaled scores (P, A, T)
+    fp32, 0 on pad rows (the op's auxiliary output, attention.py:155-162)."""
     if q.ndim != 4 or q.shape != k.shape or q.shape != v.shape:
         raise ValueError("q, k, and v must have the same (P, A, T, D) shape")
     p, heads, t, d = q.shape
@@ -722,12 +724,13 @@ def fused_attention(q, k, v, seq_lens):
     if not (q.stride() == k.stride() == v.stride()) or q.stride(3) != 1:
         q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
     out = torch.empty_like(q)
+    lse = torch.empty(p, heads, t, dtype=torch.float32, device=q.device) if with_lse else None
     sp, sa, st, _ = q.stride()
     op, oa, ot, _ = out.stride()
     call("mb_stone_attention", ptr(q), ptr(k), ptr(v), dtype_code(q.dtype), p, heads, d, sp, sa, st,
-         ptr(seq_lens.contiguous()), t, None, 0, -1, ptr(out), dtype_code(out.dtype), op, oa, ot,
+         ptr(seq_lens.contiguous()), t, None, 0, -1, ptr(out), dtype_code(out.dtype), op, oa, ot, ptr(lse),
          stream_of(q.device))
-    return out
+    return (out, lse) if with_lse else out
 
 
 # ============================================ tcgen05 fused row GEMM (sm_100a)

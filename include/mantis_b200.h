@@ -181,11 +181,15 @@ int mb_radius_read(const void* q, int64_t ldq, const void* k, const void* v, int
  * only the first `max_queries` rows of each position are queries (4 = the
  * last block's latent-only read, model.py:647-669; -1 = all). In ragged mode
  * o_pos > 0 writes position p's rows at p*o_pos (a compact output), else at
- * the token rows themselves. */
+ * the token rows themselves. Padded mode may also write lse (P, heads, t_pad)
+ * fp32: m + log(l) of each query row's scaled scores, 0 for a padded row
+ * (the auxiliary output of mantisnet::fused_attention, attention.py:155-162);
+ * NULL skips it. */
 int mb_stone_attention(const void* q, const void* k, const void* v, int dtype, int64_t n_pos, int heads, int head_dim,
                        int64_t s_pos, int64_t s_head, int64_t s_row, const int32_t* seq_lens, int64_t t_pad,
                        const int64_t* tok_off, int64_t max_tokens, int max_queries,
-                       void* out, int out_dtype, int64_t o_pos, int64_t o_head, int64_t o_row, void* stream);
+                       void* out, int out_dtype, int64_t o_pos, int64_t o_head, int64_t o_row, float* lse,
+                       void* stream);
 
 /* Engine of mb_stone_attention: 1 (the default) runs bf16 head_dim-32
  * calls with at most 320 keys per position on the tensor cores (S = Q K^T

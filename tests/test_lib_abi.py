@@ -55,7 +55,7 @@ def test_host_side_validation_without_gpu():
         _lib.call("mb_run_reduce", None, 7, 0, 0, None, None, 1, 32, None, 0, None, 0, None, 0, 0, None)
     with pytest.raises(ValueError, match="head_dim"):
         _lib.call("mb_stone_attention", None, None, None, 0, 1, 1, 24, 0, 0, 0, None, 0, None, 0, -1, None, 0, 0, 0,
-                  0, None)
+                  0, None, None)
     with pytest.raises(ValueError, match="must be bf16"):
         _lib.call("mb_segment_attention_grouped", None, 256, None, None, 512, 0, 1, 1, 8, 32, None, 192, None, 0,
                   None, None, None, None, None, None, 1, 300, None, 1, 256, None)
