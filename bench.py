@@ -291,6 +291,14 @@ def run_ours(args, rank, world, local_rank):
                 times.append(dt * 1000.0)
         p50 = statistics.median(times)
 
+    # The reference's own GPU path on the same chunk (its KLENT evaluator,
+    # Triton kernels JIT-compiled for this GPU, bf16 autocast, host batch in
+    # and CPU outputs back, as network_evaluate does), when the reference is
+    # installed in baseline/_ref.
+    ref_gpu = None
+    if rank == 0 and world == 1 and args.ref_gpu:
+        ref_gpu = reference_gpu_rate(host, n_chunks, device)
+
     cpu = None
     if rank == 0 and world == 1 and args.cpu_sample > 0:
         threads = os.cpu_count() or 1
@@ -320,11 +328,53 @@ def run_ours(args, rank, world, local_rank):
             "clocks": clocks.summary(),
             "p50_batch64_ms": p50,
             "encoder": encoder,
+            "reference_gpu": ref_gpu,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def reference_gpu_rate(host, n_chunks, device, repeats=3):
+    """Positions/s of the reference's KLENT evaluator (klent/train.py:100-120)
+    on one chunk of the benchmark's batch (the same arrays, as the
+    reference's Batch), on this GPU: its Triton kernels JIT-compile on the
+    first call (untimed); the median of ``repeats`` timed calls. None when
+    the reference is not installed in baseline/_ref."""
+    sys.path.insert(0, str(Path(__file__).resolve().parent / "tests"))
+    try:
+        import reference_pkg
+    except ImportError:
+        return None
+    if not reference_pkg.available():
+        return None
+    import importlib
+    import torch
+
+    mn = reference_pkg.load()
+    train = importlib.import_module("mantisnet.klent.train")
+    batch = mn.builder.Batch(**vars(host))
+    torch.manual_seed(0)
+    net = mn.MantisNet(mn.MantisConfig(**ARCH))
+    with torch.no_grad():
+        for head in (net.mlp_p, net.mlp_q):
+            head.out.weight.normal_(std=0.02)
+            head.out.bias.normal_(std=0.02)
+    net = net.to(device).eval()
+    ev = train.network_evaluate(net, train.KlentConfig(device=str(device), autocast=True, mass_floor=0.2))
+    ev(batch)  # JIT compilation and autotuning
+    times = []
+    for _ in range(repeats):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        ev(batch)
+        torch.cuda.synchronize()
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    return {"value": host.n_pos / sec, "unit": "positions/s", "ms_per_chunk": sec * 1000.0,
+            "impl": "reference mantisnet network_evaluate (Triton kernels for this GPU, bf16 autocast, host batch "
+                    "in, CPU outputs out)", "positions": host.n_pos, "timed_calls": repeats}
 
 
 def radius_read_bytes(T, cfg):
@@ -554,6 +604,8 @@ def main():
                     help="time one isolated-op workload instead of the evaluator (config 3 / config 2 / the "
                          "fused projection + residual + LayerNorm launch)")
     ap.add_argument("--rows", type=int, default=1814720, help="rows of --op resid_ln (default: one chunk's windows)")
+    ap.add_argument("--ref-gpu", type=int, default=1,
+                    help="also time the reference's own GPU evaluator on one chunk (needs baseline/_ref)")
     ap.add_argument("--ln-outputs", type=int, default=2, help="LayerNorm outputs of --op resid_ln (1-3)")
     args = ap.parse_args()
     if args.op:

@@ -46,6 +46,11 @@ SIGNATURES = {
     "mb_window_latent_read": "plpplilliipppippp",
     "mb_window_latent_broadcast": "plpplilliippippp",
     "mb_latent_mix": "pppliliipip",
+    "mb_segment_attention_backward": "pppilliiplpippppppplpppppppppppp",
+    "mb_stone_attention_backward": "pppppiliilllplpppppp",
+    "mb_window_latent_read_backward": "pppippppppplliipppp",
+    "mb_window_latent_broadcast_backward": "pppipppppplliipppppp",
+    "mb_row_encode_backward": "pilplppplpllppppppp",
     "mb_layer_norm": "pilpllppfpilp",
     "mb_add_ln": "plpilpllfpppilpppilpppilp",
     "mb_embed": "plpplpllpp",

@@ -925,3 +925,129 @@ def improved_policy(policy_logits, q_score, q_value, offsets, tau, lam, uniforms
          ptr(draw.pi_chosen) if draw else None, stream_of(dev))
     imp = ImprovedPolicy(probs, v_hat, kl, ne)
     return (imp, draw) if draw is not None else imp
+
+
+# ============================================================ backward
+# Deterministic gradients of the data-dependent ops (no atomics): the edge
+# permutations by source / class / window come from the stable device sort.
+def _perm_csr(keys, bound):
+    """(stable order of ``keys``, CSR of the sorted keys over [0, bound))."""
+    sk, order = argsort(keys, max(int(bound), 1))
+    return order, csr(sk, bound)
+
+
+def segment_attention_backward(q, k, v, bias, vcls, seg_ptr, src, cls, m, l, grad_out, qid=None):
+    """Gradients of ``segment_attention`` (typed segment attention; the
+    reference's cell_attention_backward, cell_latents.py:869-990): q (n_q, H)
+    or (n_q, A, d) rows, k / v likewise, m / l (n_q, A) from the forward,
+    grad_out like the output. Returns (dq, dk, dv, dbias, dvcls or None) in
+    the dtypes of q, k, v, bias, vcls."""
+    _cuda(q, k, v, bias, seg_ptr, src, cls, m, l, grad_out)
+    heads = bias.shape[0]
+    n_q, n_src = q.shape[0], k.shape[0]
+    H = q[0].numel() if n_q else k[0].numel()
+    hd = H // heads
+    n_cls = bias.shape[1]
+    qc, kc, vc = (t.reshape(t.shape[0], H).contiguous() for t in (q, k, v))
+    if not (qc.dtype == kc.dtype == vc.dtype):
+        raise ValueError("q, k and v must have one dtype")
+    go = grad_out.reshape(n_q, H).float().contiguous()
+    e = src.shape[0]
+    if qid is None:
+        qid = torch.repeat_interleave(torch.arange(n_q, device=q.device), seg_ptr[1:] - seg_ptr[:-1])
+    src_perm, src_ptr = _perm_csr(src, n_src)
+    cls_perm, cls_ptr = _perm_csr(cls, n_cls)
+    ws_a = torch.empty(max(e, 1), heads, dtype=torch.float32, device=q.device)
+    ws_d = torch.empty_like(ws_a)
+    dq = torch.empty(n_q, H, dtype=torch.float32, device=q.device)
+    dk = torch.empty(n_src, H, dtype=torch.float32, device=q.device)
+    dv = torch.empty_like(dk)
+    dbias = torch.empty(heads, n_cls, dtype=torch.float32, device=q.device)
+    vcl = None if vcls is None else vcls.reshape(n_cls, H).contiguous()
+    dvcls = None if vcls is None else torch.empty(n_cls, H, dtype=torch.float32, device=q.device)
+    b32 = bias.float().contiguous()
+    call("mb_segment_attention_backward", ptr(qc), ptr(kc), ptr(vc), dtype_code(qc.dtype), n_q, n_src, heads, hd,
+         ptr(b32), n_cls, ptr(vcl), dtype_code(vcl.dtype) if vcl is not None else 0, ptr(seg_ptr), ptr(src),
+         ptr(cls), ptr(qid.contiguous()), ptr(m.float().contiguous()), ptr(l.float().contiguous()), ptr(go), e,
+         ptr(src_perm), ptr(src_ptr), ptr(cls_perm), ptr(cls_ptr), ptr(ws_a), ptr(ws_d), ptr(dq), ptr(dk), ptr(dv),
+         ptr(dbias), ptr(dvcls), stream_of(q.device))
+    out = (dq.view(q.shape).to(q.dtype), dk.view(k.shape).to(k.dtype), dv.view(v.shape).to(v.dtype),
+           dbias.to(bias.dtype), None if vcls is None else dvcls.view(vcls.shape).to(vcls.dtype))
+    return out
+
+
+def stone_attention_backward(q, k, v, seq_lens, out, lse, grad_out):
+    """Gradients of ``fused_attention`` (the reference's
+    fused_attention_backward, attention.py:823-890) on the padded (P, A, T, D)
+    layout with the forward's ``lse``: (dq, dk, dv) in q's dtype."""
+    _cuda(q, k, v, seq_lens, out, lse, grad_out)
+    p, heads, t, d = q.shape
+    tens = [q, k, v, out, grad_out.to(q.dtype)]
+    if not all(x.stride() == q.stride() for x in tens) or q.stride(3) != 1:
+        tens = [x.contiguous() for x in tens]
+    q_, k_, v_, o_, g_ = tens
+    sp, sa, st, _ = q_.stride()
+    dsum = torch.empty(p, heads, t, dtype=torch.float32, device=q.device)
+    grads = [torch.empty(p, heads, t, d, dtype=torch.float32, device=q.device) for _ in range(3)]
+    call("mb_stone_attention_backward", ptr(q_), ptr(k_), ptr(v_), ptr(o_), ptr(g_), dtype_code(q_.dtype), p, heads,
+         d, sp, sa, st, ptr(seq_lens.contiguous()), t, ptr(lse.float().contiguous()), ptr(dsum), *map(ptr, grads),
+         stream_of(q.device))
+    return tuple(g.to(q.dtype) for g in grads)
+
+
+def window_latent_read_backward(q, k, v, offsets, order, window_pos, out, m, l, grad_out):
+    """Gradients of the window-latent read (reference
+    window_latent_read_backward, window_latents.py:589-640): q (P, 4, A, d),
+    k / v (N_w, A, d), out / m / l from the forward."""
+    _cuda(q, k, v, offsets, window_pos, out, m, l, grad_out)
+    p, _, heads, hd = q.shape
+    n_w = k.shape[0]
+    H = heads * hd
+    qc, kc, vc = q.reshape(p * 4, H).contiguous(), k.reshape(n_w, H).contiguous(), v.reshape(n_w, H).contiguous()
+    dq = torch.empty(p * 4, H, dtype=torch.float32, device=q.device)
+    dk = torch.empty(n_w, H, dtype=torch.float32, device=q.device)
+    dv = torch.empty_like(dk)
+    call("mb_window_latent_read_backward", ptr(qc), ptr(kc), ptr(vc), dtype_code(qc.dtype),
+         ptr(out.reshape(p * 4, H).float().contiguous()), ptr(m.float().contiguous()), ptr(l.float().contiguous()),
+         ptr(grad_out.reshape(p * 4, H).float().contiguous()), ptr(window_pos.contiguous()), ptr(offsets),
+         ptr(order), p, n_w, heads, hd, ptr(dq), ptr(dk), ptr(dv), stream_of(q.device))
+    return dq.view(q.shape).to(q.dtype), dk.view(k.shape).to(k.dtype), dv.view(v.shape).to(v.dtype)
+
+
+def window_latent_broadcast_backward(q, k, v, offsets, order, window_pos, m, l, grad_out):
+    """Gradients of the window-latent broadcast (reference
+    window_latent_broadcast_backward, window_latents.py:666-700): q (N_w, A,
+    d), k / v (P, 4, A, d), m / l from the forward."""
+    _cuda(q, k, v, offsets, window_pos, m, l, grad_out)
+    n_w, heads, hd = q.shape
+    p = k.shape[0]
+    H = heads * hd
+    qc, kc, vc = q.reshape(n_w, H).contiguous(), k.reshape(p * 4, H).contiguous(), v.reshape(p * 4, H).contiguous()
+    ws = [torch.empty(max(n_w, 1), 4, heads, dtype=torch.float32, device=q.device) for _ in range(2)]
+    dq = torch.empty(n_w, H, dtype=torch.float32, device=q.device)
+    dk = torch.empty(p * 4, H, dtype=torch.float32, device=q.device)
+    dv = torch.empty_like(dk)
+    call("mb_window_latent_broadcast_backward", ptr(qc), ptr(kc), ptr(vc), dtype_code(qc.dtype),
+         ptr(m.float().contiguous()), ptr(l.float().contiguous()), ptr(grad_out.reshape(n_w, H).float().contiguous()),
+         ptr(window_pos.contiguous()), ptr(offsets), ptr(order), p, n_w, heads, hd, ptr(ws[0]), ptr(ws[1]), ptr(dq),
+         ptr(dk), ptr(dv), stream_of(q.device))
+    return dq.view(q.shape).to(q.dtype), dk.view(k.shape).to(k.dtype), dv.view(v.shape).to(v.dtype)
+
+
+def encode_rows_backward(pre_w, table, edge_window, edge_class, edge_cell, grad_out):
+    """Gradients of ``encode_rows`` (the action-row encoder,
+    row_encoder.py:114-207): (grad_pre_w, grad_table) in their dtypes."""
+    _cuda(pre_w, table, edge_window, edge_class, edge_cell, grad_out)
+    n_pre, h = pre_w.shape
+    n_table = table.shape[0]
+    pc = pre_w.contiguous()
+    t32 = table.float().contiguous()
+    win_perm, win_ptr = _perm_csr(edge_window, n_pre)
+    cls_perm, cls_ptr = _perm_csr(edge_class, n_table)
+    gp = torch.empty(n_pre, h, dtype=torch.float32, device=pre_w.device)
+    gt = torch.empty(n_table, h, dtype=torch.float32, device=pre_w.device)
+    call("mb_row_encode_backward", ptr(pc), dtype_code(pc.dtype), n_pre, ptr(t32), n_table, ptr(edge_window),
+         ptr(edge_class), ptr(edge_cell), edge_window.shape[0], ptr(grad_out.float().contiguous()),
+         grad_out.shape[0], h, ptr(win_perm), ptr(win_ptr), ptr(cls_perm), ptr(cls_ptr), ptr(gp), ptr(gt),
+         stream_of(pre_w.device))
+    return gp.to(pre_w.dtype), gt.to(table.dtype)

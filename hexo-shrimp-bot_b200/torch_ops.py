@@ -15,10 +15,14 @@ row_encoder.py:368-380, relay.py:452) with a ``register_fake`` so that
   contracts) in a namespace of their own (default ``mantis_b200``) with these
   kernels and fake implementations, for callers without the reference.
 
-Forward only: the ops' backward registrations are the reference's (this
-build has no backward kernels for them). Every output follows the reference
-op's contract, auxiliary statistics included (fused_attention's per-row
-log-sum-exp, the segment attentions' running max and sum).
+Backward: :func:`define` registers autograd for the attention ops and the
+action-row encoder on this library's deterministic backward kernels, and
+:func:`install_into_reference` also takes over the reference's backward ops
+(``*_backward``, e.g. attention.py:823-890, cell_latents.py:869-990,
+window_latents.py:589-700), so the reference's own autograd formulas call
+these kernels. Every output follows the reference op's contract, auxiliary
+statistics included (fused_attention's per-row log-sum-exp, the segment
+attentions' running max and sum).
 """
 
 from __future__ import annotations
@@ -191,6 +195,9 @@ def define(namespace: str = "mantis_b200") -> list[str]:
         lib.define(name + schema)
         lib.impl(name, _KERNELS[name], "CUDA")
         torch.library.register_fake(f"{namespace}::{name}", _FAKES[name], lib=lib)
+        if name in _AUTOGRAD:
+            torch.library.register_autograd(f"{namespace}::{name}", _AUTOGRAD[name], setup_context=_save_all,
+                                            lib=lib)
     _libs[namespace] = lib
     return names
 
@@ -200,12 +207,107 @@ def install_into_reference(namespace: str = "mantisnet") -> list[str]:
     the reference's ops that is defined (import the reference package
     first). Returns the ops it took over."""
     taken = []
-    for name in _SCHEMAS:
+    for name, fn in list(_KERNELS.items()) + list(_BACKWARD_KERNELS.items()):
         qual = f"{namespace}::{name}"
         try:
             torch._C._dispatch_find_schema_or_throw(qual, "")
         except RuntimeError:
             continue
-        torch.library.register_kernel(qual, "cuda", _KERNELS[name])
+        torch.library.register_kernel(qual, "cuda", fn)
         taken.append(qual)
     return taken
+
+
+# ------------------------------------------------------------ backward
+# The reference's backward ops (same argument lists), on this library's
+# deterministic backward kernels.
+def _fused_attention_backward(q, k, v, seq_lens, out, lse, grad_out):
+    if lse.numel() == 0:  # a forward that kept no log-sum-exp: recompute it
+        _, lse = ops.fused_attention(q, k, v, seq_lens, with_lse=True)
+    return ops.stone_attention_backward(q, k, v, seq_lens, out, lse, grad_out)
+
+
+def _cell_attention_backward(q, k, v, bias, vcls, seg_ptr, src, cls, qid, sseg_ptr, sqid, scls, cptr, cedge_q, m,
+                             l, grad_out):
+    return ops.segment_attention_backward(q, k, v, bias, vcls, seg_ptr, src, cls, m, l, grad_out, qid=qid)
+
+
+def _cell_attention_plain_backward(q, k, v, bias, seg_ptr, src, cls, qid, sseg_ptr, sqid, scls, cptr, cedge_q, m,
+                                   l, grad_out):
+    return ops.segment_attention_backward(q, k, v, bias, None, seg_ptr, src, cls, m, l, grad_out, qid=qid)[:4]
+
+
+def _window_latent_read_backward(q, k, v, window_pos, offsets, order, out, m, l, grad_out):
+    return ops.window_latent_read_backward(q, k, v, offsets, order, window_pos, out, m, l, grad_out)
+
+
+def _window_latent_broadcast_backward(q, k, v, window_pos, offsets, order, m, l, grad_out):
+    return ops.window_latent_broadcast_backward(q, k, v, offsets, order, window_pos, m, l, grad_out)
+
+
+_BACKWARD_KERNELS = {
+    "fused_attention_backward": _fused_attention_backward,
+    "cell_attention_backward": _cell_attention_backward,
+    "cell_attention_plain_backward": _cell_attention_plain_backward,
+    "window_latent_read_backward": _window_latent_read_backward,
+    "window_latent_broadcast_backward": _window_latent_broadcast_backward,
+}
+
+
+# Autograd of the ops :func:`define` creates: save what the backward reads,
+# return one gradient per input (None for index tensors and ints).
+def _save_all(ctx, inputs, output):
+    outs = output if isinstance(output, tuple) else (output,)
+    ctx.save_for_backward(*[x for x in inputs if isinstance(x, torch.Tensor)],
+                          *[o for o in outs if isinstance(o, torch.Tensor)])
+    ctx.n_in = sum(isinstance(x, torch.Tensor) for x in inputs)
+    ctx.ints = [x for x in inputs if not isinstance(x, torch.Tensor)]
+
+
+def _bw_fused_attention(ctx, g_out, g_lse):
+    q, k, v, seq_lens, out, lse = ctx.saved_tensors
+    return (*_fused_attention_backward(q, k, v, seq_lens, out, lse, g_out), None)
+
+
+def _bw_cell_attention(ctx, g_out, g_m, g_l):
+    t = ctx.saved_tensors
+    q, k, v, bias, vcls, seg_ptr, src, cls, qid = t[:9]
+    m, l = t[15], t[16]
+    return (*ops.segment_attention_backward(q, k, v, bias, vcls, seg_ptr, src, cls, m, l, g_out, qid=qid),
+            *([None] * 9))
+
+
+def _bw_cell_attention_plain(ctx, g_out, g_m, g_l):
+    t = ctx.saved_tensors
+    q, k, v, bias, seg_ptr, src, cls, qid = t[:8]
+    m, l = t[14], t[15]
+    return (*ops.segment_attention_backward(q, k, v, bias, None, seg_ptr, src, cls, m, l, g_out, qid=qid)[:4],
+            *([None] * 9))
+
+
+def _bw_window_latent_read(ctx, g_out, g_m, g_l):
+    q, k, v, window_pos, offsets, order, out, m, l = ctx.saved_tensors
+    return (*ops.window_latent_read_backward(q, k, v, offsets, order, window_pos, out, m, l, g_out), None, None,
+            None)
+
+
+def _bw_window_latent_broadcast(ctx, g_out, g_m, g_l):
+    q, k, v, window_pos, offsets, order, out, m, l = ctx.saved_tensors
+    return (*ops.window_latent_broadcast_backward(q, k, v, offsets, order, window_pos, m, l, g_out), None, None,
+            None)
+
+
+def _bw_action_row_encode(ctx, g_out):
+    pre_w, table, edge_window, edge_class, edge_cell, edge_rev, out = ctx.saved_tensors
+    gp, gt = ops.encode_rows_backward(pre_w, table, edge_window, edge_class, edge_cell, g_out)
+    return gp, gt, None, None, None, None, None
+
+
+_AUTOGRAD = {
+    "fused_attention": _bw_fused_attention,
+    "cell_attention": _bw_cell_attention,
+    "cell_attention_plain": _bw_cell_attention_plain,
+    "window_latent_read": _bw_window_latent_read,
+    "window_latent_broadcast": _bw_window_latent_broadcast,
+    "action_row_encode": _bw_action_row_encode,
+}

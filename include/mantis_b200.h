@@ -218,6 +218,69 @@ int mb_window_latent_broadcast(const void* q, int64_t ldq, const void* k, const 
 int mb_latent_mix(const void* q, const void* k, const void* v, int64_t ld, int dtype, int64_t n_pos, int heads,
                   int head_dim, void* out, int out_dtype, void* stream);
 
+/* -------------------------------------------------------------- backward --
+ * Gradients for the fit path, deterministic (no atomics; every sum in a
+ * fixed order), fp32 math and fp32 gradients on f32 or bf16 inputs. Scatters
+ * are gathers over stable permutations the caller derives once (edges by
+ * source / class / window: mb_argsort + mb_csr_from_sorted). Softmax
+ * backward per row i: D_i = sum_j P_ij dP_ij, dS_ij = P_ij (dP_ij - D_i).
+ */
+
+/* Typed segment attention (mantisnet::cell_attention_backward and
+ * cell_attention_plain_backward, cell_latents.py:869-990; kernels
+ * cell_latents.py:287-543): from the forward's m, l (n_q, heads) and the
+ * output gradient (n_q, heads * head_dim) fp32, writes dq, dk, dv (row
+ * layouts of q and k), dbias (heads, n_cls) and, with vcls, dvcls (n_cls,
+ * heads * head_dim). qid (E): each edge's query row; src_perm / src_ptr: the
+ * edges by source (stable) and their CSR over sources; cls_perm / cls_ptr:
+ * by class. alpha_ws and dscore_ws: (E, heads) fp32 workspaces. Width
+ * heads * head_dim in {32, 64, 128, 256}. */
+int mb_segment_attention_backward(const void* q, const void* k, const void* v, int dtype, int64_t n_q, int64_t n_src,
+                                  int heads, int head_dim, const float* bias, int64_t n_cls, const void* vcls,
+                                  int vcls_dtype, const int64_t* seg_ptr, const int64_t* src, const int64_t* cls,
+                                  const int64_t* qid, const float* m, const float* l, const float* grad_out,
+                                  int64_t n_edges, const int64_t* src_perm, const int64_t* src_ptr,
+                                  const int64_t* cls_perm, const int64_t* cls_ptr, float* alpha_ws, float* dscore_ws,
+                                  float* dq, float* dk, float* dv, float* dbias, float* dvcls, void* stream);
+
+/* Stone attention (mantisnet::fused_attention_backward, attention.py:823-890;
+ * kernels attention.py:229-531), padded (P, A, T, D) layout of the forward
+ * with its lse (P, A, T): dq, dk, dv (P, A, T, D) contiguous fp32; rows at or
+ * past seq_lens[p] get zero gradients. dsum_ws: (P, A, T) fp32 workspace. */
+int mb_stone_attention_backward(const void* q, const void* k, const void* v, const void* out, const void* grad_out,
+                                int dtype, int64_t n_pos, int heads, int head_dim, int64_t s_pos, int64_t s_head,
+                                int64_t s_row, const int32_t* seq_lens, int64_t t_pad, const float* lse,
+                                float* dsum_ws, float* dq, float* dk, float* dv, void* stream);
+
+/* Window-latent read and broadcast (mantisnet::window_latent_read_backward /
+ * window_latent_broadcast_backward, window_latents.py:589-700; kernels
+ * window_latents.py:270-473), row layouts of the forward (read: q (P * 4,
+ * H), k/v (N_w, H); broadcast: q (N_w, H), k/v (P * 4, H)) with its fp32
+ * out (read only), m, l and output gradient; window_pos per window, the
+ * position CSR offsets / order of mb_window_latent_read. Broadcast
+ * workspaces p_ws, ds_ws: (N_w, 4, heads) fp32. */
+int mb_window_latent_read_backward(const void* q, const void* k, const void* v, int dtype, const float* out,
+                                   const float* m, const float* l, const float* grad_out, const int64_t* window_pos,
+                                   const int64_t* offsets, const int64_t* order, int64_t n_pos, int64_t n_windows,
+                                   int heads, int head_dim, float* dq, float* dk, float* dv, void* stream);
+int mb_window_latent_broadcast_backward(const void* q, const void* k, const void* v, int dtype, const float* m,
+                                        const float* l, const float* grad_out, const int64_t* window_pos,
+                                        const int64_t* offsets, const int64_t* order, int64_t n_pos,
+                                        int64_t n_windows, int heads, int head_dim, float* p_ws, float* ds_ws,
+                                        float* dq, float* dk, float* dv, void* stream);
+
+/* Action-row encoder (the backward of mantisnet::action_row_encode,
+ * row_encoder.py:114-207, 386-413): out[c] = sum_e relu(pre[win_e] +
+ * table[cls_e]) gives grad_pre (n_pre, h) and grad_table (n_table, h) fp32,
+ * the output gradient (n_cells, h) fp32 where the pre-activation is
+ * positive; win_perm / win_ptr and cls_perm / cls_ptr: the edges by window
+ * and by class. h in {32, 64, 128, 256}. */
+int mb_row_encode_backward(const void* pre, int pre_dtype, int64_t n_pre, const float* table, int64_t n_table,
+                           const int64_t* edge_window, const int64_t* edge_class, const int64_t* edge_cell,
+                           int64_t n_edges, const float* grad_out, int64_t n_cells, int64_t h,
+                           const int64_t* win_perm, const int64_t* win_ptr, const int64_t* cls_perm,
+                           const int64_t* cls_ptr, float* grad_pre, float* grad_table, void* stream);
+
 /* ------------------------------------------------------- rows and norms -- */
 
 /* LayerNorm over rows of width h (fp32 statistics, eps), input f32 or bf16,

@@ -52,3 +52,28 @@ def test_reference_evaluator_on_plugin_kernels(reference_setup, autocast):
             scale = want[k].abs().max().clamp(min=1e-6)
             assert (got - want[k]).abs().max() <= 1e-4 * scale, k
     mb._lib.check_device_error()
+
+
+def test_reference_training_gradients_on_plugin_kernels(reference_setup):
+    """The fit path: gradients of a loss on the reference model's policy and
+    critic outputs (fp32), through the reference's own autograd formulas
+    whose backward ops run on this library's kernels, against the same
+    gradients on the reference's eager CPU path."""
+    train, net, batch, want, mf = reference_setup
+    import copy
+    cpu_net = copy.deepcopy(net).to("cpu")
+
+    def loss_grads(model, b):
+        model.zero_grad(set_to_none=True)
+        w, g, cells = model.trunk(b)
+        policy, critic = model.cell_head_logits(w, g, cells, b)
+        (policy.float().square().mean() + critic.float().square().mean()).backward()
+        return {n: p.grad.detach().float().cpu() for n, p in model.named_parameters() if p.grad is not None}
+
+    got = loss_grads(net, batch.to("cuda"))
+    ref = loss_grads(cpu_net, batch)
+    assert set(got) == set(ref) and len(got) > 50
+    for n in ref:
+        scale = ref[n].abs().max().clamp(min=1e-8)
+        assert (got[n] - ref[n]).abs().max() <= 1e-3 * scale, n
+    mb._lib.check_device_error()
