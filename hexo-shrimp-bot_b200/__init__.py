@@ -18,7 +18,7 @@ __all__ = [
 
 
 _SUBMODULES = ("_lib", "ops", "model", "evaluator", "vocab", "engine", "builder", "encoder", "config", "build", "sharding",
-               "hexgraph")
+               "hexgraph", "search", "torch_ops")
 
 
 def __getattr__(name):
@@ -32,7 +32,7 @@ def __getattr__(name):
         from . import model
 
         return getattr(model, name)
-    if name in ("network_evaluate", "Evaluator"):
+    if name in ("network_evaluate", "network_leaf_evaluate", "Evaluator"):
         from . import evaluator
 
         return getattr(evaluator, name)

@@ -73,6 +73,7 @@ SIGNATURES = {
     "mb_encoding_fill": "ppi",
     "mb_encoding_free": "p",
     "mb_encoder_table": "ipl",
+    "mb_segment_argmax": "ppllpp",
     "mb_klent_improve": "ppppllffpppppppppp",
 }
 _CT = {"p": ctypes.c_void_p, "i": ctypes.c_int, "l": ctypes.c_int64, "f": ctypes.c_float}

@@ -150,6 +150,56 @@ __global__ void __launch_bounds__(kThreads) improve_kernel(
   }
 }
 
+// Per segment, the rank of its largest value (the first one on ties), as
+// torch.argmax over the segment; -1 for an empty segment.
+__global__ void __launch_bounds__(kThreads) segment_argmax_kernel(const float* __restrict__ x,
+                                                                  const int64_t* __restrict__ offsets, int64_t n_pos,
+                                                                  int64_t n, int64_t* __restrict__ ranks) {
+  __shared__ float vs[kWarps];
+  __shared__ long long is[kWarps];
+  const int64_t p = blockIdx.x;
+  const int64_t a = offsets[p], b = offsets[p + 1];
+  if (a < 0 || b < a || b > n) {
+    if (threadIdx.x == 0) {
+      report(ERR_RUN_BOUND);
+      ranks[p] = -1;
+    }
+    return;
+  }
+  float best = -INFINITY;
+  long long at = -1;
+  for (int64_t i = a + threadIdx.x; i < b; i += kThreads) {
+    const float v = x[i];
+    if (at < 0 || v > best) {  // strided: the first index wins ties within a thread
+      best = v;
+      at = i - a;
+    }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const long long oi = __shfl_xor_sync(0xffffffffu, at, o);
+    if (oi >= 0 && (at < 0 || ov > best || (ov == best && oi < at))) {
+      best = ov;
+      at = oi;
+    }
+  }
+  if (lane == 0) {
+    vs[warp] = best;
+    is[warp] = at;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kWarps; ++w)
+      if (is[w] >= 0 && (at < 0 || vs[w] > best || (vs[w] == best && is[w] < at))) {
+        best = vs[w];
+        at = is[w];
+      }
+    ranks[p] = at;
+  }
+}
+
 }  // namespace klent
 }  // namespace mb
 
@@ -175,3 +225,14 @@ int mb_klent_improve(const float* policy_logits, const float* q_score, const flo
 }
 
 }  // extern "C"
+
+extern "C" int mb_segment_argmax(const float* x, const int64_t* offsets, int64_t n_pos, int64_t n, int64_t* ranks,
+                                 void* stream) {
+  MB_REQUIRE(n_pos >= 0 && n >= 0, "segment_argmax: negative size");
+  if (n_pos == 0) return MB_OK;
+  MB_REQUIRE(x && offsets && ranks, "segment_argmax: null pointer");
+  MB_REQUIRE(n_pos <= INT32_MAX, "segment_argmax: too many segments");
+  klent::segment_argmax_kernel<<<(unsigned)n_pos, klent::kThreads, 0, as_stream(stream)>>>(x, offsets, n_pos, n,
+                                                                                         ranks);
+  return launch_status("segment_argmax");
+}

@@ -64,9 +64,36 @@ class Position:
         self.board: dict[tuple[int, int], int] = {}
         self.ply = 0
         self.terminal = False
+        self.winner = None
         # Frontier as an indexable list with positions, for O(1) random choice.
         self._front: list[tuple[int, int]] = [(0, 0)]
         self._where: dict[tuple[int, int], int] = {(0, 0): 0}
+
+    @classmethod
+    def replay(cls, moves) -> "Position":
+        """The position after placing ``moves`` ((q, r) pairs) in order."""
+        pos = cls()
+        for q, r in moves:
+            pos.advance(int(q), int(r))
+        return pos
+
+    def copy(self) -> "Position":
+        other = Position.__new__(Position)
+        other.board = dict(self.board)
+        other.ply = self.ply
+        other.terminal = self.terminal
+        other.winner = getattr(self, "winner", None)
+        other._front = list(self._front)
+        other._where = dict(self._where)
+        return other
+
+    @property
+    def is_terminal(self) -> bool:
+        return self.terminal
+
+    def nth_legal(self, rank: int) -> tuple[int, int]:
+        """The legal move of index ``rank`` in engine order (ascending (q, r))."""
+        return self.legal_moves()[rank]
 
     @property
     def current_player(self) -> int:
@@ -119,6 +146,7 @@ class Position:
         self.ply += 1
         if self._wins(q, r, who):
             self.terminal = True
+            self.winner = who
 
     def random_legal(self, rng: random.Random) -> tuple[int, int]:
         return self._front[rng.randrange(len(self._front))]

@@ -238,3 +238,42 @@ def network_evaluate(model, cfg):
             return out[:n], out[n:2 * n], out[2 * n:]
 
     return evaluate
+
+
+class _LeafEvaluator:
+    """``network_evaluate``'s closure plus ``leaves(batch, tau, lam)``: per
+    position the rank of the KLENT-improved policy's largest entry and the
+    improved value (klent/search.py:231-253's per-leaf step), computed on the
+    device so that two numbers per position cross back instead of three
+    floats per legal cell."""
+
+    def __init__(self, model, cfg):
+        self._full = network_evaluate(model, cfg)
+        self._model, self._cfg = model, cfg
+        self._dtype = torch.bfloat16 if getattr(cfg, "autocast", True) else torch.float32
+        self._gemm = getattr(cfg, "gemm", "tcgen05-ln")
+        self._fields = needed_fields(model.cfg)
+        self._device = torch.device(cfg.device)
+
+    def __call__(self, batch: Batch):
+        return self._full(batch)
+
+    def leaves(self, batch: Batch, tau: float, lam: float):
+        with _gpu_lock, torch.no_grad():
+            eng = self._model.engine(self._dtype, gemm=self._gemm)
+            b = to_device(batch, self._device, self._fields)
+            policy, critic = eng.evaluate(b)
+            q_score, q_values = ops.compose(critic, b.legal_offsets, self._cfg.mass_floor)
+            imp = ops.improved_policy(policy.float(), q_score, q_values, b.legal_offsets, tau, lam)
+            ranks = ops.segment_argmax(imp.probs, b.legal_offsets)
+            ranks, values = ranks.cpu(), imp.v_hat.cpu()
+            check_device_error(self._device)
+        return ranks, values
+
+
+def network_leaf_evaluate(model, cfg):
+    """The evaluator closure with the device-side leaf step the Gumbel search
+    (search.gumbel_choose) uses for its leaf waves."""
+    if torch.device(cfg.device).type != "cuda":
+        raise RuntimeError("the B200 evaluator runs on CUDA devices only")
+    return _LeafEvaluator(model, cfg)

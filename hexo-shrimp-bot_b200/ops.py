@@ -927,6 +927,18 @@ def improved_policy(policy_logits, q_score, q_value, offsets, tau, lam, uniforms
     return (imp, draw) if draw is not None else imp
 
 
+def segment_argmax(x, offsets):
+    """Per segment of ``x`` (cut by ``offsets``), the rank of its largest
+    value, the first on ties (-1 for an empty segment): (P,) int64."""
+    _cuda(x, offsets)
+    _i64(offsets, "offsets")
+    xf = x.float().contiguous()
+    p = offsets.shape[0] - 1
+    ranks = torch.empty(p, dtype=torch.int64, device=x.device)
+    call("mb_segment_argmax", ptr(xf), ptr(offsets), p, xf.shape[0], ptr(ranks), stream_of(x.device))
+    return ranks
+
+
 # ============================================================ backward
 # Deterministic gradients of the data-dependent ops (no atomics): the edge
 # permutations by source / class / window come from the stable device sort.

@@ -476,6 +476,12 @@ int mb_klent_improve(const float* policy_logits, const float* q_score, const flo
                      float* norm_entropy, const double* uniforms, float* stored, int64_t* ranks, double* pi_top1,
                      double* pi_chosen, void* stream);
 
+/* ranks[p] = the index within segment p ([offsets[p], offsets[p+1]) of x)
+ * of its largest value, the first one on ties (torch.argmax over the
+ * segment), -1 for an empty segment: the Gumbel search's per-leaf move from
+ * the improved policy (klent/search.py:246-249). Device pointers. */
+int mb_segment_argmax(const float* x, const int64_t* offsets, int64_t n_pos, int64_t n, int64_t* ranks, void* stream);
+
 /* --------------------------------------------------------------- encoder --
  * Host-side batch builder: game positions to the collated batch arrays that
  * the evaluator reads. HOST pointers, no stream, no GPU needed. Replaces the

@@ -16,6 +16,10 @@ It imports the reference's ``mantisnet.klent.improve.improved_policy``
 - seeded random batches: ragged segments (1 to 3,000 cells, one single-cell
   segment), logits, acting scores and action values in the ranges the
   evaluator produces, four (tau, lambda) settings.
+
+It also carries the Gumbel search's parity fixture
+``crates/hexo-search/tests/fixtures/gumbel_parity.json`` (scripted evaluator
+calls, root noise, expected survivors and move) into ``gumbel.npz``.
 """
 
 from __future__ import annotations
@@ -87,6 +91,10 @@ def main():
             out[f"{i}.fixture_v"] = b["fixture_v"]
     np.savez_compressed(HERE / "klent.npz", **out)
     print("wrote", HERE / "klent.npz", len(batches), "cases")
+    # the Gumbel search's cross-language parity fixture, carried as is
+    gumbel = (checkout / "crates/hexo-search/tests/fixtures/gumbel_parity.json").read_text()
+    np.savez_compressed(HERE / "gumbel.npz", fixture=np.array(json.dumps(json.loads(gumbel))))
+    print("wrote", HERE / "gumbel.npz")
 
 
 if __name__ == "__main__":
