@@ -530,7 +530,14 @@ int mb_cell_pass(const void* x, int x_dtype, int64_t n_windows, const float* emb
   if (n_windows == 0) return MB_OK;
   const int vec = row_vec(h);
   MB_REQUIRE(vec > 0, "cell_pass: bad width %lld", (long long)h);
-  MB_REQUIRE(x && emb && cell_ptr && win_ptr && out && (scratch || n_cov == 0), "cell_pass: null pointer");
+  MB_REQUIRE(x && emb && cell_ptr && win_ptr && out && (n_cov == 0 || (scratch && edge_window && edge_class &&
+                                                                          edge_wcell)),
+             "cell_pass: null pointer");
+  // the cell kernel reads x and emb and writes scratch in vec-wide vectors,
+  // the window reduction reads scratch and writes out likewise
+  MB_REQUIRE(aligned(x, (size_t)vec * dtype_size(x_dtype)) && aligned(emb, (size_t)vec * 4) &&
+                 (n_cov == 0 || aligned(scratch, (size_t)vec * 4)) && aligned(out, (size_t)vec * dtype_size(out_dtype)),
+             "cell_pass: x, emb, scratch and out must be aligned to %d elements", vec);
   cudaStream_t s = as_stream(stream);
   int st = MB_DISPATCH_T(x_dtype, TX, [&] {
     return MB_DISPATCH_VEC(vec, V, [&] {

@@ -108,10 +108,11 @@ int mb_cell_pass(const void* x, int x_dtype, int64_t n_windows, const float* emb
  * allocate device memory (a host runtime that owns every device buffer, a
  * fixed memory budget): the (n_cov x h) scratch lives in a 16 MiB array
  * compiled into the library, so n_cov * h may not exceed 4,194,304; larger
- * calls return MB_INVALID_ARGUMENT. The first call on a device looks up the
- * array's address (do it before any stream capture). Calls share the array:
- * calls that overlap on the GPU race. This entry point has no counterpart in
- * the reference. */
+ * calls return MB_INVALID_ARGUMENT. Each call outside a stream capture looks
+ * up the array's address on its device (a call inside a capture reuses the
+ * last one, so make the first call on a device before any capture). Calls
+ * share the array: calls that overlap on the GPU race. This entry point has
+ * no counterpart in the reference. */
 int mb_cell_pass_noalloc(const void* x, int x_dtype, int64_t n_windows, const float* emb, int64_t n_cls,
                          const int64_t* cell_ptr, int64_t n_cov, const int64_t* edge_window, const int64_t* edge_class,
                          const int64_t* win_ptr, const int64_t* edge_wcell, int64_t h,

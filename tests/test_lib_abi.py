@@ -64,3 +64,16 @@ def test_host_side_validation_without_gpu():
                   None, None, None, None, None, None, 1, 300, None, 1, 256, None)
     with pytest.raises(ValueError, match="key_bits"):
         _lib.call("mb_argsort_workspace", 1000, 0, ctypes.byref(ctypes.c_int64(0)))
+
+
+def test_cell_pass_refuses_misaligned_and_missing_arrays():
+    """mb_cell_pass checks its pointers' alignment and the edge arrays before
+    any launch (a misaligned vector access would fault the GPU)."""
+    if not _lib.LIB_PATH.exists():
+        pytest.skip("library not built")
+    _lib.load()
+    good, odd = 1 << 20, (1 << 20) + 4  # fake device addresses: 16-byte aligned and not
+    with pytest.raises(ValueError, match="aligned"):
+        _lib.call("mb_cell_pass", odd, 0, 10, good, 5, good, 3, good, good, good, good, 256, good, good, 0, None)
+    with pytest.raises(ValueError, match="null pointer"):
+        _lib.call("mb_cell_pass", good, 0, 10, good, 5, good, 3, None, good, good, good, 256, good, good, 0, None)
