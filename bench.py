@@ -139,28 +139,61 @@ def cpu_forward_rate(specs, sample, threads):
     return sample / dt, dt
 
 
+def reference_cpu_rate(specs, sample, threads):
+    """The reference's own KLENT evaluator (klent/train.py:100-120, eager,
+    fp32, stock KlentConfig otherwise) on the host cores, on ``sample``
+    positions: positions/s. None when the reference is not installed in
+    baseline/_ref."""
+    sys.path.insert(0, str(Path(__file__).resolve().parent / "tests"))
+    try:
+        import reference_pkg
+    except ImportError:
+        return None
+    if not reference_pkg.available():
+        return None
+    import importlib
+    import torch
+
+    mn = reference_pkg.load()
+    train = importlib.import_module("mantisnet.klent.train")
+    mb = _pkg()
+    torch.set_num_threads(threads)
+    torch.manual_seed(0)
+    net = mn.MantisNet(mn.MantisConfig(**ARCH)).eval()
+    ev = train.network_evaluate(net, train.KlentConfig(device="cpu", autocast=False, mass_floor=0.2))
+    batch = mn.builder.Batch(**vars(mb.collate([mb.from_spec(s) for s in specs[:sample]])))
+    t0 = time.perf_counter()
+    ev(batch)
+    return sample / (time.perf_counter() - t0)
+
+
 def run_reference(args, rank):
-    """The reference arm: the CPU restatement of the reference's forward on
-    the host cores (the reference is Python; its CPU path is eager torch)."""
+    """The reference arm, on rank 0 only: the reference's own eager CPU
+    evaluator from baseline/_ref on the host cores (the reference is Python;
+    its CPU path is eager torch), else the CPU restatement of that path."""
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    specs = make_specs(max(args.ref_sample, 1), args.lo, args.hi, seed=1234)
+    sample = args.ref_sample
+    specs = make_specs(max(sample, 1), args.lo, args.hi, seed=1234)
+    own = reference_cpu_rate(specs, sample, threads) is not None  # also the first warm-up step
     rates = []
-    for i in range(args.warmup + args.steps):
-        r, _ = cpu_forward_rate(specs, args.ref_sample, threads)
-        if i >= args.warmup:
+    for i in range(args.warmup - 1 + args.steps if own else args.warmup + args.steps):
+        r = reference_cpu_rate(specs, sample, threads) if own else cpu_forward_rate(specs, sample, threads)[0]
+        if i >= (args.warmup - 1 if own else args.warmup):
             rates.append(r)
     v = statistics.median(rates)
+    what = ("reference mantisnet network_evaluate, eager fp32 on CPU (baseline/_ref)" if own
+            else "fp32 eager torch-CPU restatement of the reference forward (oracle port)")
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "positions/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * args.ref_sample / v,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * sample / v,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{args.ref_sample} late positions ({args.lo}-{args.hi} stones) per step, "
+        "config": {"workload": f"{sample} late positions ({args.lo}-{args.hi} stones) per step, "
                                "config-4 architecture (h256/8 blocks/8 heads/F4, cell_latents+cell_nodes)",
-                   "positions_per_step": args.ref_sample},
-        "cpu_baseline": {"value": v, "unit": "positions/s", "cores": threads, "kind": "port",
-                         "sample": f"{args.ref_sample} positions per step, fp32 eager torch-CPU oracle"},
+                   "positions_per_step": sample},
+        "cpu_baseline": {"value": v, "unit": "positions/s", "cores": threads, "kind": "reference" if own else "port",
+                         "sample": f"{sample} positions per step, {what}"},
         "e2e": {"value": v, "unit": "positions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -597,7 +630,8 @@ def main():
     ap.add_argument("--lo", type=int, default=150)
     ap.add_argument("--hi", type=int, default=300)
     ap.add_argument("--cpu-sample", type=int, default=4)
-    ap.add_argument("--ref-sample", type=int, default=4)
+    ap.add_argument("--ref-sample", type=int, default=1,
+                    help="positions per step of the reference arm (its eager CPU path takes seconds per position)")
     ap.add_argument("--latency", type=int, default=1)
     ap.add_argument("--gemm", default="tcgen05-ln", help="dense projection path (see model.Engine)")
     ap.add_argument("--op", default=None, choices=["hex", "axial", "resid_ln", "radius"],
