@@ -139,17 +139,23 @@ def cpu_forward_rate(specs, sample, threads):
     return sample / dt, dt
 
 
-def reference_cpu_rate(specs, sample, threads):
-    """The reference's own KLENT evaluator (klent/train.py:100-120, eager,
-    fp32, stock KlentConfig otherwise) on the host cores, on ``sample``
-    positions: positions/s. None when the reference is not installed in
-    baseline/_ref."""
+def _reference_pkg():
+    """The loader of the reference installed in baseline/_ref, or None."""
     sys.path.insert(0, str(Path(__file__).resolve().parent / "tests"))
     try:
         import reference_pkg
     except ImportError:
         return None
-    if not reference_pkg.available():
+    return reference_pkg if reference_pkg.available() else None
+
+
+def reference_cpu_rate(specs, sample, threads):
+    """The reference's own KLENT evaluator (klent/train.py:100-120, eager,
+    fp32, stock KlentConfig otherwise) on the host cores, on ``sample``
+    positions: positions/s. None when the reference is not installed in
+    baseline/_ref."""
+    reference_pkg = _reference_pkg()
+    if reference_pkg is None:
         return None
     import importlib
     import torch
@@ -176,11 +182,11 @@ def run_reference(args, rank):
     threads = os.cpu_count() or 1
     sample = args.ref_sample
     specs = make_specs(max(sample, 1), args.lo, args.hi, seed=1234)
-    own = reference_cpu_rate(specs, sample, threads) is not None  # also the first warm-up step
+    own = _reference_pkg() is not None
     rates = []
-    for i in range(args.warmup - 1 + args.steps if own else args.warmup + args.steps):
+    for i in range(args.warmup + args.steps):
         r = reference_cpu_rate(specs, sample, threads) if own else cpu_forward_rate(specs, sample, threads)[0]
-        if i >= (args.warmup - 1 if own else args.warmup):
+        if i >= args.warmup:
             rates.append(r)
     v = statistics.median(rates)
     what = ("reference mantisnet network_evaluate, eager fp32 on CPU (baseline/_ref)" if own
@@ -375,12 +381,8 @@ def reference_gpu_rate(host, n_chunks, device, repeats=3):
     reference's Batch), on this GPU: its Triton kernels JIT-compile on the
     first call (untimed); the median of ``repeats`` timed calls. None when
     the reference is not installed in baseline/_ref."""
-    sys.path.insert(0, str(Path(__file__).resolve().parent / "tests"))
-    try:
-        import reference_pkg
-    except ImportError:
-        return None
-    if not reference_pkg.available():
+    reference_pkg = _reference_pkg()
+    if reference_pkg is None:
         return None
     import importlib
     import torch
@@ -618,6 +620,48 @@ def run_op(args):
     print(json.dumps(line))
 
 
+def run_multi(args):
+    """One JSON line: ``network_evaluate_multi`` over ``--devices`` GPUs of
+    this process (default: all visible), each call one batch of ``--chunk``
+    late positions per device, cut into cost-balanced slices; host batch in
+    (pinned), CPU outputs back. Not the headline metric (the headline runs
+    one process per GPU)."""
+    import torch
+
+    mb = _pkg()
+    n_dev = args.devices or torch.cuda.device_count()
+    specs = make_specs(args.unique, args.lo, args.hi, seed=1000)
+    reps = math.ceil(args.chunk * n_dev / len(specs))
+    host = mb.encoder.encode((specs * reps)[: args.chunk * n_dev], pin_memory=True)
+    torch.manual_seed(0)
+    net = mb.MantisNet(mb.MantisConfig(**ARCH))
+    with torch.no_grad():
+        for head in (net.mlp_p, net.mlp_q):
+            head.out.weight.normal_(std=0.02)
+            head.out.bias.normal_(std=0.02)
+    net = net.to("cuda:0").eval()
+    cfg = mb.evaluator.EvaluatorConfig(device="cuda:0", autocast=True, mass_floor=0.2, gemm=args.gemm)
+    ev = mb.evaluator.network_evaluate_multi(net, cfg, [f"cuda:{i}" for i in range(n_dev)])
+    try:
+        for _ in range(args.warmup):
+            ev(host)
+        times = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            ev(host)
+            times.append(time.perf_counter() - t0)
+    finally:
+        ev.close()
+    sec = statistics.median(times)
+    off = mb.evaluator._offsets(host, ev.fields)
+    cuts = mb.sharding.balanced_cuts(ev.costs(host, off), n_dev)
+    print(json.dumps({
+        "metric": "positions/s, one network_evaluate_multi call over the devices (host batch in, CPU outputs out)",
+        "value": host.n_pos / sec, "unit": "positions/s", "devices": n_dev, "ms_per_call": sec * 1000.0,
+        "positions_per_call": host.n_pos, "slice_positions": [b - a for a, b in zip(cuts, cuts[1:])],
+        "steps": args.steps, "warmup": args.warmup, "dtype": "bf16", "data": "synthetic", "lost": sorted(ev.lost)}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -634,7 +678,8 @@ def main():
                     help="positions per step of the reference arm (its eager CPU path takes seconds per position)")
     ap.add_argument("--latency", type=int, default=1)
     ap.add_argument("--gemm", default="tcgen05-ln", help="dense projection path (see model.Engine)")
-    ap.add_argument("--op", default=None, choices=["hex", "axial", "resid_ln", "radius"],
+    ap.add_argument("--devices", type=int, default=0, help="GPUs of --op multi (default: all visible)")
+    ap.add_argument("--op", default=None, choices=["hex", "axial", "resid_ln", "radius", "multi"],
                     help="time one isolated-op workload instead of the evaluator (config 3 / config 2 / the "
                          "fused projection + residual + LayerNorm launch)")
     ap.add_argument("--rows", type=int, default=1814720, help="rows of --op resid_ln (default: one chunk's windows)")
@@ -642,6 +687,9 @@ def main():
                     help="also time the reference's own GPU evaluator on one chunk (needs baseline/_ref)")
     ap.add_argument("--ln-outputs", type=int, default=2, help="LayerNorm outputs of --op resid_ln (1-3)")
     args = ap.parse_args()
+    if args.op == "multi":
+        run_multi(args)
+        return
     if args.op:
         run_op(args)
         return

@@ -24,9 +24,13 @@ def batch():
     return mb.collate([mb.from_spec(s) for s in specs])
 
 
+KNOBS = [dict(cell_latents=True, cell_nodes=True), dict(cell_latents=True, cell_nodes=True, cell_adjacency=True)]
+
+
+@pytest.mark.parametrize("knobs", KNOBS, ids=["production", "adjacency"])
 @pytest.mark.parametrize("part", [1, 2, 3, 5, 100])
-def test_runs_reassemble_the_batch(batch, part):
-    cfg = mb.MantisConfig(h=32, blocks=1, heads=2, cell_latents=True, cell_nodes=True)
+def test_runs_reassemble_the_batch(batch, part, knobs):
+    cfg = mb.MantisConfig(h=32, blocks=1, heads=2, **knobs)
     fields = E.needed_fields(cfg)
     assert E.split_supported(fields)
     cuts = E.split_points(batch, part)
@@ -57,6 +61,29 @@ def test_runs_reassemble_the_batch(batch, part):
     assert int(batch.radius_src.max()) == int(off["stone"][-1]) - 1 or batch.radius_src.numel() == 0
 
 
-def test_unsupported_fields_fall_back():
-    cfg = mb.MantisConfig(h=32, blocks=1, heads=2)  # relay path: its tables are not split
-    assert not E.split_supported(E.needed_fields(cfg))
+@pytest.mark.parametrize("cut", [(0, 4), (4, 9), (3, 4)])
+def test_relay_runs_derive_their_own_tables(cut):
+    """The relay configuration's CSR views are rebuilt per run: a run's
+    tables equal those of a batch collated from its positions alone."""
+    specs = mb.engine.random_positions(9, 20, 120, seed=11)
+    whole = mb.collate([mb.from_spec(s) for s in specs])
+    cfg = mb.MantisConfig(h=32, blocks=1, heads=2)
+    fields = E.needed_fields(cfg)
+    assert E.split_supported(fields) and set(mb.builder.RELAY_FIELDS) <= set(fields)
+    off = E._offsets(whole, fields)
+    a, b = cut
+    run = E.part_to_device(whole, fields, off, a, b, "cpu")
+    own = mb.collate([mb.from_spec(s) for s in specs[a:b]])
+    # (padded fields keep the parent batch's padding width, so only the
+    # incidence and its derived views are compared)
+    for f in mb.builder.RELAY_FIELDS + ("dec_cell", "dec_window", "dec_class"):
+        assert torch.equal(getattr(run, f), getattr(own, f)), f
+
+
+def test_range_points():
+    assert E.range_points(5, 9, 0) == [5, 9]
+    assert E.range_points(5, 9, 4) == [5, 9]
+    assert E.range_points(0, 512, 448) == [0, 64, 512]
+    pts = E.range_points(100, 1100, 448)
+    assert pts[0] == 100 and pts[-1] == 1100 and all(a < b for a, b in zip(pts, pts[1:]))
+    assert max(b - a for a, b in zip(pts, pts[1:])) <= 448
