@@ -569,8 +569,9 @@ def run_op(args):
         vcls = (torch.randn(192, cfg.h, device=dev, generator=g) * 0.02).to(torch.bfloat16)
         h, stage = cfg.h, T.max_t - 4
         out = torch.empty_like(q)
-        ms = _time_launches(lambda: ops.radius_read(q, kv[:, :h], kv[:, h:], bias, vcls, T.r_ptr, T.r_pack, T.cell_off,
-                                                    T.stone_off, stage, order=T.r_order, out=out),
+        ms = _time_launches(lambda: ops.radius_read(q, kv[:, :h], kv[:, h:], bias, vcls, T.r_ptr, T.r_pack_slots,
+                                                    T.cell_off, T.stone_off, stage, order=T.r_order, out=out,
+                                                    slots=T.r_slots),
                             args.steps, args.warmup)
         algo = radius_read_bytes(T, cfg)
         line = {"metric": "radius read cells/s", "value": T.N_c / (ms / 1000.0), "unit": "cells/s", "ms_per_step": ms,

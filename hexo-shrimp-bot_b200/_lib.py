@@ -40,7 +40,9 @@ SIGNATURES = {
     "mb_gemm_rows_ln": "pllppplfpppilpppilpppilp",
     "mb_axial_attention": "pppliillllpppplllp",
     "mb_radius_pack_edges": "ppppplllllpp",
-    "mb_radius_read": "plppllliiplpppppppllpilp",
+    "mb_radius_read": "plppllliiplppppppppllpilp",
+    "mb_radius_slots": "ppppplllpplp",
+    "mb_radius_slots_size": "lllp",
     "mb_stone_attention_engine": "i",
     "mb_stone_attention": "pppiliilllplplipilllpp",
     "mb_window_latent_read": "plpplilliipppippp",

@@ -100,18 +100,29 @@ __device__ __forceinline__ float head_sum(float x, int lph) {
 // ------------------------------------------------------- segment attention
 // One warp per batch of kSegRows consecutive query rows (blocks of 2 warps,
 // scheduled in row order, so the GPU works on a narrow band of positions at a
-// time and the gathered source rows stay L2-resident). The batch's run bounds
-// and its first 32 edge indices are fetched by one coalesced load each and
-// broadcast by shuffle, so a row waits on one round trip (its K/V gathers,
-// issued together with its query load) instead of three (run bounds, edge
-// indices, gathers). Two edges per iteration keep two K/V row pairs in flight
-// per lane.
+// time and the gathered source rows stay L2-resident). A lane holds VEC
+// columns of a row; the warp covers the row's full width.
+//
+// The warp walks its rows' edges as one stream (the rows are consecutive, so
+// their edges are one contiguous CSR range): kSegEdges edges at a time, it
+// requests all their K, V and class value rows before using any, and switches
+// row state whenever the stream crosses a run bound. Every query row and the
+// run bounds are requested together at the start, and the edge indices come
+// 32 at a time by one coalesced load, broadcast by shuffle. A row with few
+// edges (the incidence reads average 2.5 and 4.9) so no longer costs a
+// dependent round trip of its own. Edge order, and so the fp32 arithmetic,
+// is the one of a per-row loop.
 constexpr int kSegWarps = 2;   // small blocks: a block's slot frees as soon as its 2 warps finish
 constexpr int kSegRows = 4;
-constexpr int kSegBlocksPerSM = 12;  // 24 resident warps at <= 80 registers
+// Edges requested together: 4 for 16-bit rows, 2 for fp32 rows of 4 or more
+// columns per lane (whose raw rows take twice the registers). At 8 columns
+// per lane that is ~125 registers: 8 blocks (16 warps) per SM there, 10 at
+// narrower lanes.
+template <typename T, int VEC> constexpr int seg_edges() { return sizeof(T) == 4 && VEC >= 4 ? 2 : 4; }
+template <int VEC> constexpr int seg_blocks_per_sm() { return VEC >= 8 ? 8 : 10; }
 
 template <typename T, typename TO, typename TV, int VEC, bool HAS_VCLS>
-__global__ void __launch_bounds__(kSegWarps * 32, kSegBlocksPerSM) segment_attention_kernel(
+__global__ void __launch_bounds__(kSegWarps * 32, seg_blocks_per_sm<VEC>()) segment_attention_kernel(
     const T* __restrict__ q, int64_t ldq, const T* __restrict__ k, const T* __restrict__ v, int64_t ldkv, int64_t n_q,
     int64_t n_src, int heads, int hd, const float* __restrict__ bias, int64_t n_cls, const TV* __restrict__ vcls,
     const int64_t* __restrict__ seg_ptr, const int64_t* __restrict__ src, const int64_t* __restrict__ cls,
@@ -133,113 +144,127 @@ __global__ void __launch_bounds__(kSegWarps * 32, kSegBlocksPerSM) segment_atten
   const int64_t bound = lane <= nrows ? seg_ptr[row0 + lane] : 0;
   int skipped = 0;
   if (skip_ptr && lane < nrows) skipped = skip_ptr[row0 + lane + 1] > skip_ptr[row0 + lane];
-  const int64_t e0 = __shfl_sync(0xffffffffu, bound, 0), e1 = __shfl_sync(0xffffffffu, bound, nrows);
-  int64_t my_src = 0, my_cls = 0;  // the batch's edge e0 + lane
-  if (e0 + lane < e1) {
-    my_src = src[e0 + lane];
-    my_cls = cls[e0 + lane];
+  Raw<T, VEC> qr[kSegRows];
+#pragma unroll
+  for (int r = 0; r < kSegRows; ++r) {
+    if (live && r < nrows) raw_load<false, VEC>(q + (row0 + r) * ldq + col, qr[r]);
+    else qr[r] = Raw<T, VEC>{};
   }
-  auto fetch = [&](int64_t e, int64_t& s, int64_t& c) {
-    const int64_t i = e - e0;  // warp-uniform
-    if (i < 32) {
-      s = __shfl_sync(0xffffffffu, my_src, (int)i);
-      c = __shfl_sync(0xffffffffu, my_cls, (int)i);
-    } else {
-      s = src[e];
-      c = cls[e];
-    }
-  };
+  const int64_t e0 = __shfl_sync(0xffffffffu, bound, 0), e1 = __shfl_sync(0xffffffffu, bound, nrows);
 
-  for (int r = 0; r < nrows; ++r) {
-    const int64_t row = row0 + r;
-    float qv[VEC];
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) qv[i] = 0.f;
-    if (live) load_vec<VEC>(q + row * ldq + col, qv);
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) qv[i] *= scale;
-    const int64_t beg = __shfl_sync(0xffffffffu, bound, r);
-    int64_t end = __shfl_sync(0xffffffffu, bound, r + 1);
-    if (__shfl_sync(0xffffffffu, skipped, r)) end = beg;
-    float m = kNegInf, l = 0.f, acc[VEC];
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) acc[i] = 0.f;
-
-    auto consume = [&](float score, const float* vv) {
-      const float m_new = fmaxf(m, score);
-      const float corr = __expf(m - m_new);
-      const float p = __expf(score - m_new);
-      l = l * corr + p;
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) acc[i] = acc[i] * corr + p * vv[i];
-      m = m_new;
-    };
-    auto add_class_row = [&](int64_t c, float* vv) {
-      if constexpr (HAS_VCLS) {
-        if (live) {
-          float a[VEC];
-          load_vec<VEC>(vcls + c * H + col, a);
-#pragma unroll
-          for (int i = 0; i < VEC; ++i) vv[i] += a[i];
-        }
-      }
-    };
-
-    int64_t e = beg;
-    for (; e + 1 < end; e += 2) {
-      int64_t s0, s1, c0, c1;
-      fetch(e, s0, c0);
-      fetch(e + 1, s1, c1);
-      if (s0 < 0 || s0 >= n_src || s1 < 0 || s1 >= n_src || c0 < 0 || c0 >= n_cls || c1 < 0 || c1 >= n_cls) {
-        report(ERR_INDEX);
-        continue;
-      }
-      float k0[VEC] = {}, k1[VEC] = {}, v0[VEC] = {}, v1[VEC] = {};
-      if (live) {
-        load_vec<VEC>(k + s0 * ldkv + col, k0);
-        load_vec<VEC>(k + s1 * ldkv + col, k1);
-        load_vec<VEC>(v + s0 * ldkv + col, v0);
-        load_vec<VEC>(v + s1 * ldkv + col, v1);
-      }
-      float d0 = 0.f, d1 = 0.f;
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) { d0 += qv[i] * k0[i]; d1 += qv[i] * k1[i]; }
-      d0 = group_sum(d0, lph) + __ldg(brow + c0);
-      d1 = group_sum(d1, lph) + __ldg(brow + c1);
-      add_class_row(c0, v0);
-      add_class_row(c1, v1);
-      consume(d0, v0);
-      consume(d1, v1);
-    }
-    if (e < end) {
-      int64_t s0, c0;
-      fetch(e, s0, c0);
-      if (s0 < 0 || s0 >= n_src || c0 < 0 || c0 >= n_cls) {
+  // Edge indices [eb, eb + 32): lane i holds edge eb + i (source -1: none, or
+  // out of range, which is reported once here and the edge skipped).
+  int64_t eb = e0;
+  int my_src = -1, my_cls = 0;
+  auto refill = [&](int64_t base) {
+    eb = base;
+    my_src = -1;
+    my_cls = 0;
+    const int64_t e = base + lane;
+    if (e < e1) {
+      const int64_t s_ = src[e], c_ = cls[e];
+      if (s_ < 0 || s_ >= n_src || c_ < 0 || c_ >= n_cls) {
         report(ERR_INDEX);
       } else {
-        float k0[VEC] = {}, v0[VEC] = {};
-        if (live) {
-          load_vec<VEC>(k + s0 * ldkv + col, k0);
-          load_vec<VEC>(v + s0 * ldkv + col, v0);
-        }
-        float d0 = 0.f;
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) d0 += qv[i] * k0[i];
-        d0 = group_sum(d0, lph) + __ldg(brow + c0);
-        add_class_row(c0, v0);
-        consume(d0, v0);
+        my_src = (int)s_;
+        my_cls = (int)c_;
       }
     }
-    const float inv = l > 0.f ? 1.f / l : 1.f;
+  };
+  refill(e0);
+
+  int r = 0;
+  int64_t rend = 0;
+  int rskip = 0;
+  float qf[VEC], acc[VEC], m = kNegInf, l = 0.f;
+  auto start_row = [&](int rr) {  // rr is warp-uniform
+    Raw<T, VEC> sel = qr[0];
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) acc[i] *= inv;
+    for (int i = 1; i < kSegRows; ++i)
+      if (rr == i) sel = qr[i];
+    raw_unpack(sel, qf);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      qf[i] *= scale;
+      acc[i] = 0.f;
+    }
+    m = kNegInf;
+    l = 0.f;
+    rend = __shfl_sync(0xffffffffu, bound, rr + 1);
+    rskip = __shfl_sync(0xffffffffu, skipped, rr);
+  };
+  auto finish_row = [&](int rr) {
+    const float inv = l > 0.f ? 1.f / l : 1.f;
+    float o[VEC];
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) o[i] = acc[i] * inv;
     if (live) {
-      store_vec<VEC>(out + row * ldo + col, acc);
+      const int64_t row = row0 + rr;
+      store_vec<VEC>(out + row * ldo + col, o);
       if (m_out && (lane % lph) == 0) {
         m_out[row * heads + head] = m;
         l_out[row * heads + head] = l;
       }
     }
+  };
+  start_row(0);
+
+  constexpr int kSegEdges = seg_edges<T, VEC>();
+  for (int64_t e = e0; e < e1; e += kSegEdges) {
+    if (e + kSegEdges > eb + 32) refill(e);  // warp-uniform
+    int sj[kSegEdges], cj[kSegEdges];
+    Raw<T, VEC> kr[kSegEdges], vr[kSegEdges];
+    Raw<TV, VEC> cr[kSegEdges];
+#pragma unroll
+    for (int j = 0; j < kSegEdges; ++j) {
+      const int at = (int)(e - eb) + j;
+      sj[j] = __shfl_sync(0xffffffffu, my_src, at);
+      cj[j] = __shfl_sync(0xffffffffu, my_cls, at);
+      if (live && sj[j] >= 0) {
+        raw_load<false, VEC>(k + (int64_t)sj[j] * ldkv + col, kr[j]);
+        raw_load<false, VEC>(v + (int64_t)sj[j] * ldkv + col, vr[j]);
+        if constexpr (HAS_VCLS) raw_load<false, VEC>(vcls + (int64_t)cj[j] * H + col, cr[j]);
+      } else {
+        kr[j] = Raw<T, VEC>{};
+        vr[j] = Raw<T, VEC>{};
+        if constexpr (HAS_VCLS) cr[j] = Raw<TV, VEC>{};
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kSegEdges; ++j) {
+      if (e + j >= e1) break;
+      while (e + j >= rend) {  // the stream crossed into the next row(s)
+        finish_row(r);
+        ++r;
+        start_row(r);
+      }
+      if (rskip || sj[j] < 0) continue;
+      float kv_[VEC], vv[VEC];
+      raw_unpack(kr[j], kv_);
+      float d = 0.f;
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) d += qf[i] * kv_[i];
+      d = group_sum(d, lph) + __ldg(brow + cj[j]);
+      raw_unpack(vr[j], vv);
+      if constexpr (HAS_VCLS) {
+        float a[VEC];
+        raw_unpack(cr[j], a);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) vv[i] += a[i];
+      }
+      const float m_new = fmaxf(m, d);
+      const float corr = __expf(m - m_new);
+      const float p = __expf(d - m_new);
+      l = l * corr + p;
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) acc[i] = acc[i] * corr + p * vv[i];
+      m = m_new;
+    }
+  }
+  for (;;) {
+    finish_row(r);
+    if (++r >= nrows) break;
+    start_row(r);
   }
 }
 

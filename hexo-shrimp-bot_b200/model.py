@@ -391,7 +391,7 @@ class _Tables:
             self.r_ptr = ops.csr(r_sorted, self.N_c)
             self.cell_off = ops.csr(b.cell_pos, self.P)  # cells are laid out position by position
             self.skip = self.cell_ptr if cfg.cell_node_scope == "uncovered" else None
-            self.r_pack = self.r_order = None
+            self.r_pack = self.r_order = self.r_slots = self.r_pack_slots = None
             if ops.radius_supported(cfg.heads, cfg.h, cd):
                 # shared by every block's radius read: packed edges, and each
                 # position's cells ordered by edge count
@@ -401,6 +401,8 @@ class _Tables:
                 if self.skip is not None:
                     deg = deg * (self.skip[1:] == self.skip[:-1])
                 _, self.r_order = ops.argsort(b.cell_pos * 64 + deg, self.P * 64)
+                self.r_slots, self.r_pack_slots = ops.radius_slots(self.r_pack, self.r_ptr, self.cell_off, self.r_order,
+                                                                   self.skip)
         if cfg.cell_adjacency:
             a_sorted, aorder = ops.argsort(b.adjacency_dst, self.N_c)
             self.a_src = ops.gather_i64(b.adjacency_src, aorder)
@@ -838,8 +840,8 @@ class Engine:
             with self.timed("radius_read"):
                 if T.r_pack is not None:
                     read = ops.radius_read(q, kv[:, :h], kv[:, h:], blk["radius_bias"], blk["radius_vclass"], T.r_ptr,
-                                           T.r_pack, T.cell_off, T.stone_off, stage, order=T.r_order,
-                                           skip_ptr=T.skip, out_dtype=cd)
+                                           T.r_pack_slots, T.cell_off, T.stone_off, stage, order=T.r_order,
+                                           skip_ptr=T.skip, out_dtype=cd, slots=T.r_slots)
                 elif ops.grouped_supported(cfg.heads, h, cd):
                     # block-diagonal: position p's cells read only position p's stones
                     read = ops.segment_attention_grouped(

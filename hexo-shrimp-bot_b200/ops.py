@@ -209,11 +209,36 @@ def radius_pack(src, cls, seg_ptr, q_off, s_off, n_src: int, n_cls: int) -> torc
     return packed
 
 
+def radius_slots(packed, seg_ptr, q_off, order=None, skip_ptr=None):
+    """(slots, packed_slots) for ``radius_read``: per slot of ``order``
+    (ascending rows when None) the row, where its edges start in
+    ``packed_slots`` and its edge count (0 for a row ``skip_ptr`` skips), and
+    the packed edges (``radius_pack``) copied into slot order, each run padded
+    to a multiple of four. Computed once per forward."""
+    _cuda(packed, seg_ptr, q_off)
+    _i64(seg_ptr, "seg_ptr")
+    _i64(q_off, "q_off")
+    for t, n in ((order, "order"), (skip_ptr, "skip_ptr")):
+        if t is not None:
+            _cuda(t)
+            _i64(t, n)
+    n_q, n_groups, n_edges = seg_ptr.shape[0] - 1, q_off.shape[0] - 1, packed.shape[0]
+    length = ctypes.c_int64(0)
+    call("mb_radius_slots_size", n_q, n_groups, n_edges, ctypes.byref(length))
+    slots = torch.empty(n_q, 4, dtype=torch.int32, device=seg_ptr.device)
+    packed_slots = torch.empty(length.value, dtype=torch.int32, device=seg_ptr.device)
+    call("mb_radius_slots", ptr(packed), ptr(seg_ptr), ptr(skip_ptr), ptr(order), ptr(q_off), n_groups, n_q, n_edges,
+         ptr(slots), ptr(packed_slots), length.value, stream_of(seg_ptr.device))
+    return slots, packed_slots
+
+
 def radius_read(q, k, v, bias, vcls, seg_ptr, packed, q_off, s_off, stage_rows, order=None, skip_ptr=None, out=None,
-                out_dtype=torch.bfloat16):
+                out_dtype=torch.bfloat16, slots=None):
     """The radius read on packed edges: same result as
     ``segment_attention_grouped`` up to float rounding. head_dim 32, bf16
-    q/k/v (and class value rows)."""
+    q/k/v (and class value rows). With ``slots`` (the table of
+    ``radius_slots``), ``packed`` must be its slot-ordered copy of the edges;
+    ``order`` / ``seg_ptr`` / ``skip_ptr`` are then not read."""
     _cuda(q, k, v, bias, seg_ptr, packed, q_off, s_off)
     for t, n in ((q, "q"), (k, "k"), (v, "v")):
         _rowmajor(t, n)
@@ -223,6 +248,8 @@ def radius_read(q, k, v, bias, vcls, seg_ptr, packed, q_off, s_off, stage_rows, 
         raise ValueError("radius_read needs bf16 q, k and v")
     if packed.dtype != torch.int32:
         raise ValueError("packed edges must be int32 (radius_pack)")
+    if slots is not None and (slots.dtype != torch.int32 or slots.shape != (q.shape[0], 4) or not slots.is_contiguous()):
+        raise ValueError("slots must be the (n_q, 4) int32 table of radius_slots")
     heads = bias.shape[0]
     n_q, width = q.shape
     if out is None:
@@ -232,8 +259,8 @@ def radius_read(q, k, v, bias, vcls, seg_ptr, packed, q_off, s_off, stage_rows, 
         vcls = vcls.to(torch.bfloat16).contiguous()
     call("mb_radius_read", ptr(q), q.stride(0), ptr(k), ptr(v), k.stride(0), n_q, k.shape[0], heads, width // heads,
          ptr(bias32), bias32.shape[1], ptr(vcls), ptr(seg_ptr), ptr(packed), ptr(skip_ptr), ptr(q_off), ptr(s_off),
-         ptr(order), q_off.shape[0] - 1, max(int(stage_rows), 1), ptr(out), dtype_code(out.dtype), out.stride(0),
-         stream_of(q.device))
+         ptr(order), ptr(slots), q_off.shape[0] - 1, max(int(stage_rows), 1), ptr(out), dtype_code(out.dtype),
+         out.stride(0), stream_of(q.device))
     return out
 
 

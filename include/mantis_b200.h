@@ -167,11 +167,23 @@ int mb_segment_attention_grouped(const void* q, int64_t ldq, const void* k, cons
 int mb_radius_pack_edges(const int64_t* src, const int64_t* cls, const int64_t* seg_ptr, const int64_t* q_off,
                          const int64_t* s_off, int64_t n_groups, int64_t n_q, int64_t n_edges, int64_t n_src,
                          int64_t n_cls, int32_t* packed, void* stream);
+/* mb_radius_slots: the read order as a table of int32 quadruples (row, first
+ * edge, edge count or 0 for a skipped row, 0) per slot, and the packed edges
+ * (mb_radius_pack_edges) copied into slot order, each cell's run starting at
+ * a multiple of four entries and padded with -1; both 16-byte aligned, the
+ * copy mb_radius_slots_size entries long. Built once per forward; passed to
+ * mb_radius_read as `slots` with the copy as `packed` (then `order`,
+ * `seg_ptr` and `skip_ptr` are not read there). No counterpart in the
+ * reference. */
+int mb_radius_slots_size(int64_t n_q, int64_t n_groups, int64_t n_edges, int64_t* len);
+int mb_radius_slots(const int32_t* packed, const int64_t* seg_ptr, const int64_t* skip_ptr, const int64_t* order,
+                    const int64_t* q_off, int64_t n_groups, int64_t n_q, int64_t n_edges, int32_t* slots,
+                    int32_t* packed_slots, int64_t packed_slots_len, void* stream);
 int mb_radius_read(const void* q, int64_t ldq, const void* k, const void* v, int64_t ldkv, int64_t n_q, int64_t n_src,
                    int heads, int head_dim, const float* bias, int64_t n_cls, const void* vcls,
                    const int64_t* seg_ptr, const int32_t* packed, const int64_t* skip_ptr, const int64_t* q_off,
-                   const int64_t* s_off, const int64_t* order, int64_t n_groups, int64_t stage_rows, void* out,
-                   int out_dtype, int64_t ldo, void* stream);
+                   const int64_t* s_off, const int64_t* order, const int32_t* slots, int64_t n_groups,
+                   int64_t stage_rows, void* out, int out_dtype, int64_t ldo, void* stream);
 
 /* Block-diagonal stone attention over [4 latents; stones] per position.
  * Padded mode (tok_off == NULL): q/k/v/out element (p, a, t, d) at

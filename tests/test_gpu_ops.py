@@ -327,7 +327,8 @@ def _degree_order(seg_ptr, q_off):
 @pytest.mark.parametrize("vdt", [None, torch.bfloat16])
 @pytest.mark.parametrize("odt", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("ordered", [False, True])
-def test_radius_read_matches_generic(heads, vdt, odt, ordered):
+@pytest.mark.parametrize("slotted", [False, True])
+def test_radius_read_matches_generic(heads, vdt, odt, ordered, slotted):
     q, kv, bias, vcls, seg_ptr, src, cls, q_off, s_off, runs = (
         x.to(DEV) for x in _grouped_case(heads, 32, heads * 77 + 5))
     h = heads * 32
@@ -335,9 +336,10 @@ def test_radius_read_matches_generic(heads, vdt, odt, ordered):
     packed = ops.radius_pack(src, cls, seg_ptr, q_off, s_off, kv.shape[0], bias.shape[1])
     order = _degree_order(seg_ptr, q_off) if ordered else None
     want = ops.segment_attention(q, kv[:, :h], kv[:, h:], bias, vc, seg_ptr, src, cls, out_dtype=torch.float32)
+    slots, pk = ops.radius_slots(packed, seg_ptr, q_off, order) if slotted else (None, packed)
     for stage in (1024, 64, 1):  # all staged; the 400-source group from global memory; every group from global
-        got = ops.radius_read(q, kv[:, :h], kv[:, h:], bias, vc, seg_ptr, packed, q_off, s_off, stage, order=order,
-                              out_dtype=odt)
+        got = ops.radius_read(q, kv[:, :h], kv[:, h:], bias, vc, seg_ptr, pk, q_off, s_off, stage, order=order,
+                              out_dtype=odt, slots=slots)
         torch.cuda.synchronize()
         tol = 1e-5 if odt == torch.float32 else 8e-3
         torch.testing.assert_close(got.float(), want, rtol=tol, atol=tol, msg=f"stage_rows={stage}")
@@ -345,8 +347,9 @@ def test_radius_read_matches_generic(heads, vdt, odt, ordered):
                       (torch.arange(q.shape[0], device=DEV) % 3 == 0).long().cumsum(0)])
     want = ops.segment_attention(q, kv[:, :h], kv[:, h:], bias, vc, seg_ptr, src, cls, skip_ptr=skip,
                                  out_dtype=torch.float32)
-    got = ops.radius_read(q, kv[:, :h], kv[:, h:], bias, vc, seg_ptr, packed, q_off, s_off, 1024, order=order,
-                          skip_ptr=skip, out_dtype=odt)
+    slots, pk = ops.radius_slots(packed, seg_ptr, q_off, order, skip) if slotted else (None, packed)
+    got = ops.radius_read(q, kv[:, :h], kv[:, h:], bias, vc, seg_ptr, pk, q_off, s_off, 1024, order=order,
+                          skip_ptr=skip, out_dtype=odt, slots=slots)
     tol = 1e-5 if odt == torch.float32 else 8e-3
     torch.testing.assert_close(got.float(), want, rtol=tol, atol=tol, msg="skip")
     mb._lib.check_device_error()
