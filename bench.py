@@ -269,11 +269,13 @@ def run_ours(args, rank, world, local_rank):
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     eng.probe = {}
     with ClockSampler(local_rank) as clocks:
+        torch.cuda.nvtx.range_push("timed")  # lets a profiler select the timed steps' launches
         start.record()
         for _ in range(args.steps):
             step_device()
         end.record()
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     probe, eng.probe = eng.probe, None
     tables = eng.tables
     launches = (lib.call_count() - calls0) // max(args.steps, 1)
@@ -300,6 +302,14 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     ms_e2e = max_over_ranks(e0.elapsed_time(e1) / args.steps)
     e2e_value = world * positions_per_step / (ms_e2e / 1000.0)
+    # The whole box's host encoder rate (the ranks encoded concurrently on the
+    # shared host cores): a self-play pipeline that encodes what the GPUs
+    # evaluate runs at the smaller of it and the end-to-end rate.
+    enc_box = encoder["value"]
+    if world > 1:
+        t = torch.tensor([enc_box], dtype=torch.float64, device=device)
+        dist.all_reduce(t)
+        enc_box = float(t.item())
     h2d = batch_bytes(host, fields) * n_chunks
     d2h = 3 * host.n_cells * 4 * n_chunks
 
@@ -367,6 +377,10 @@ def run_ours(args, rank, world, local_rank):
             "clocks": clocks.summary(),
             "p50_batch64_ms": p50,
             "encoder": encoder,
+            "pipeline": {"value": min(enc_box, e2e_value), "unit": "positions/s", "encoder_box": enc_box,
+                         "bound": "host encoder" if enc_box < e2e_value else "gpus",
+                         "note": "encode + evaluate on this box: the smaller of the summed concurrent encoder "
+                                 "rates of the ranks and the end-to-end rate"},
             "reference_gpu": ref_gpu,
         }
         print(json.dumps(line), flush=True)

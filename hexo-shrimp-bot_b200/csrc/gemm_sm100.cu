@@ -273,7 +273,11 @@ struct Plan {
   // once per tile; its A tiles are re-read for each N block.
   static_assert(!WS || (KB == 4 && !RESID && !XS && (PRO == PRO_TMA || PRO == PRO_LN)),
                 "the weight-stationary plan serves K = 256 bf16-output launches");
-  static constexpr int A_BUFS = (XS || RESID || KB > 4 || WS) ? 1 : 2;
+  // The neighbour-mean prologue keeps one tile and one W stage so that the
+  // L1 cache keeps most of the SM's 256 KB: a tile's neighbour rows (its own
+  // rows +- 64) are then gathered from L1 after their first touch.
+  static constexpr bool L1_HEAVY = PRO == PRO_HEXMEAN;
+  static constexpr int A_BUFS = (XS || RESID || KB > 4 || WS || L1_HEAVY) ? 1 : 2;
   // PRO_TMA keeps K-block slots in a ring instead of whole tiles: a slot is
   // refilled as soon as the MMAs that read it finish.
   static constexpr bool RING_A = PRO == PRO_TMA;
@@ -284,7 +288,7 @@ struct Plan {
   static constexpr bool OUT_BOXES = EPI == EPI_RESID_LN || EPI == EPI_STORE || EPI == EPI_ADD_X;
   // W K-blocks in flight. The residual epilogues are long enough to hide a
   // one-stage W stream; the freed 32 KB hold the output staging boxes.
-  static constexpr int W_STAGES = RESID ? 1 : 2;
+  static constexpr int W_STAGES = (RESID || L1_HEAVY) ? 1 : 2;
   // Residual boxes (32 rows x 32 fp32 columns, 4 KB) per epilogue warp.
   static constexpr int RING = KB > 4 ? 1 : 3;
   // Warps writing the A tile (1..PRODUCERS) and draining TMEM (the rest).
@@ -1114,6 +1118,8 @@ static int launch_rowgemm(const Params& prm, cudaStream_t s, const char* what) {
   constexpr int smem_bytes = Plan<PRO, EPI, XS, KB, WS>::SMEM;
   auto kern = rowgemm_kernel<PRO, EPI, XS, KB, WS>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+  if (Plan<PRO, EPI, XS, KB, WS>::L1_HEAVY)  // the smallest shared-memory carveout that fits: the rest is L1
+    cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 0);
   const int64_t tiles = cdiv(prm.m, BM);
   const int grid = (int)(tiles < num_sms() ? tiles : num_sms());
   kern<<<grid, THREADS, smem_bytes, s>>>(prm);
