@@ -390,11 +390,11 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const __grid_consta
   if (warp == 0) {
     // ------------------------------------- W stream + MMA issuer (1 lane)
     if (lane == 0) {
-      const uint64_t total_kb = WS ? 0 : (uint64_t)my_tiles * nbn * KB;
+      const int64_t total_kb = WS ? 0 : (int64_t)my_tiles * nbn * KB;
       const uint8_t* wimg = reinterpret_cast<const uint8_t*>(p.w_img);
       uint64_t issued = 0;
       auto issue_w = [&](uint64_t upto) -> bool {
-        for (; issued < upto && issued < total_kb; ++issued) {
+        for (; (int64_t)issued < total_kb && issued < upto; ++issued) {
           const uint32_t s = issued % L::W_STAGES, ph = (issued / L::W_STAGES) & 1;
           if (!mbar_wait(smem_u32(&w_empty[s]), ph ^ 1, abort)) return false;
           const int nb = (int)((issued / KB) % nbn), kb = (int)(issued % KB);
@@ -494,8 +494,9 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const __grid_consta
         bool ok = true;
         for (int kb = 0; kb < KB; ++kb) {
           const uint64_t aseq = (uint64_t)u * KB + kb;
-          const uint32_t slot = aseq % L::A_SLOTS;
-          if (!mbar_wait(smem_u32(&a_empty[slot]), ((aseq / L::A_SLOTS) & 1) ^ 1, abort)) { ok = false; break; }
+          constexpr uint32_t kSlots = L::A_SLOTS > 0 ? L::A_SLOTS : 1;  // (RING_A plans only)
+          const uint32_t slot = aseq % kSlots;
+          if (!mbar_wait(smem_u32(&a_empty[slot]), ((aseq / kSlots) & 1) ^ 1, abort)) { ok = false; break; }
           mbar_expect_tx(smem_u32(&a_full[slot]), A_KB_BYTES);
           tma_load_2d(smem_u32(a_smem + slot * A_KB_BYTES), &p.tmap_x, kb * BK, (int)(tile * BM),
                       smem_u32(&a_full[slot]));
