@@ -320,10 +320,12 @@ def run_ours(args, rank, world, local_rank):
         n_dec = int(tables.dec_window.numel())
         roof = dominant_roofline([
             resid_ln_roofline(probe), radius_roofline(probe, tables, cfg),
-            segment_roofline(probe, "cell_read", "segment_attention_kernel (cells<-windows, class rows)", tables.N_c,
-                             tables.N_w, n_dec, cfg, 726),
-            segment_roofline(probe, "window_read", "segment_attention_kernel (windows<-cells)", tables.N_w,
-                             tables.N_c, n_dec, cfg, 726)])
+            segment_roofline(probe, "cell_read", "radius_read_kernel (block-diagonal read: cells<-windows, class rows)"
+                             if tables.cr_slots is not None else "segment_attention_kernel (cells<-windows, class rows)",
+                             tables.N_c, tables.N_w, n_dec, cfg, 726, packed=tables.cr_slots is not None),
+            segment_roofline(probe, "window_read", "radius_read_kernel (block-diagonal read: windows<-cells)"
+                             if tables.wr_slots is not None else "segment_attention_kernel (windows<-cells)",
+                             tables.N_w, tables.N_c, n_dec, cfg, 726, packed=tables.wr_slots is not None)])
 
     # p50 batch-64 latency (config-4 distribution: 40-150 stones), end to end
     p50 = None
@@ -429,18 +431,18 @@ def reference_gpu_rate(host, n_chunks, device, repeats=3):
 def radius_read_bytes(T, cfg):
     """Algorithmic HBM bytes of one radius read (cells <- stones): per cell its
     bf16 query row in and output row out, its run bound and its slot in the
-    edge-count order; per edge the packed int32 stone | class; each stone's
+    edge-count order (one 16-byte slot); per edge the packed int32 stone | class; each stone's
     bf16 K and V rows once; the bf16 class value rows and fp32 bias rows once."""
     h, n_cls = cfg.h, 192
-    return (T.N_c * h * 2 * 2 + (T.N_c + 1) * 8 + T.N_c * 8 + int(T.r_src.numel()) * 4 + T.N_s * 2 * h * 2
+    return (T.N_c * h * 2 * 2 + T.N_c * 16 + int(T.r_src.numel()) * 4 + T.N_s * 2 * h * 2
             + n_cls * h * 2 + cfg.heads * n_cls * 4)
 
 
 # DRAM bytes per cell of one radius read, from an ncu capture of the same
-# kernel (dram__bytes_read.sum + dram__bytes_write.sum = 450.1 MB over 438,658
+# kernel (dram__bytes_read.sum + dram__bytes_write.sum = 445.8 MB over 438,658
 # cells; profiles/radius_read_64pos.md), scaled to the timed launch by its
 # cell count.
-RADIUS_DRAM_BYTES_PER_CELL = 450_067_712 / 438_658
+RADIUS_DRAM_BYTES_PER_CELL = 445_866_240 / 438_658
 
 
 def radius_roofline(probe, T, cfg):
@@ -461,17 +463,19 @@ def radius_roofline(probe, T, cfg):
             "launches_timed": len(ms), "edges": int(T.r_src.numel()), "total_ms": sum(ms)}
 
 
-def segment_roofline(probe, name, kernel, n_q, n_src, n_edges, cfg, n_cls):
-    """A generic segment attention's launches inside the timed region:
-    algorithmic bytes per launch (per query row its bf16 query and output
-    rows and run bound, per edge the int64 source and class, each source's
-    bf16 K and V rows once, class value rows and bias once) over the mean
+def segment_roofline(probe, name, kernel, n_q, n_src, n_edges, cfg, n_cls, packed=True):
+    """An incidence read's launches inside the timed region: algorithmic
+    bytes per launch (per query row its bf16 query and output rows and its
+    16-byte slot, per edge its packed int32 source | class; or, on the generic
+    kernel, the run bound and the int64 source and class; each source's bf16
+    K and V rows once, class value rows and bias once) over the mean
     CUDA-event duration."""
     ev = probe.get(name, [])
     if not ev:
         return None
     h = cfg.h
-    algo = (n_q * (2 * h * 2 + 8) + n_edges * 16 + n_src * 2 * h * 2 + n_cls * (h * 2 + cfg.heads * 4))
+    per_row, per_edge = (16, 4) if packed else (8, 16)
+    algo = (n_q * (2 * h * 2 + per_row) + n_edges * per_edge + n_src * 2 * h * 2 + n_cls * (h * 2 + cfg.heads * 4))
     ms = [s.elapsed_time(e) for s, e in ev]
     sec = statistics.mean(ms) / 1000.0
     pk, kind = peaks()

@@ -1133,6 +1133,10 @@ static int launch_rowgemm(const Params& prm, cudaStream_t s, const char* what) {
 static int g_store_plan = 1;
 static int g_ln_plan = 2;
 
+// The window path of the hex message pass (hex_sm100.cu).
+static int hex_window_launch(const void* x, int64_t n, const int32_t* nbr, const void* w_image, const float* bias,
+                             void* out, int64_t ldo, cudaStream_t s);
+
 static Params base_params() {
   Params prm{};
   prm.n_blocks = 1;
@@ -1329,6 +1333,9 @@ int mb_hex_message_pass(const void* x, int64_t ldx, int64_t n, const int32_t* nb
   MB_REQUIRE(aligned(out, 16) && (ldo * 2) % 16 == 0 && ldo >= BN, "hex_message_pass: out rows must be 16-byte aligned");
   MB_REQUIRE(aligned(nbr, 4) && aligned(w_image, 16) && (!bias || aligned(bias, 16)),
              "hex_message_pass: misaligned table, weight image or bias");
+  // contiguous rows: the kernel that keeps each tile's neighbour rows in
+  // shared memory; strided rows: the row GEMM with a gathering prologue
+  if (ldx == KDIM && n < (int64_t(1) << 31)) return hex_window_launch(x, n, nbr, w_image, bias, out, ldo, as_stream(stream));
   Params prm = base_params();
   prm.x = x;
   prm.ldx = ldx;

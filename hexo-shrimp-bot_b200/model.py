@@ -384,6 +384,18 @@ class _Tables:
             self.win_ptr = ops.csr(w_sorted, self.N_w)
             self.edge_wcell = ops.gather_i64(dc_sorted, worder)
             self.edge_wclass = ops.gather_i64(self.dec_class, worder)
+        # The two incidence reads (cells <- windows, windows <- cells) on the
+        # block-diagonal read kernel: packed edges, each position's rows by
+        # edge count and the slot tables, shared by every block.
+        self.cr_slots = self.wr_slots = None
+        if cfg.uses_cell_state and ops.radius_supported(cfg.heads, cfg.h, cd):
+            self.pos_cell_off = ops.csr(b.cell_pos, self.P)  # cells are laid out position by position
+            self.cr_order, self.cr_slots, self.cr_pack = self._read_plan(
+                self.dec_window, self.dec_class, self.cell_ptr, self.pos_cell_off, self.wl_off, self.N_w,
+                b.cell_pos, cfg.dec_classes)
+            self.wr_order, self.wr_slots, self.wr_pack = self._read_plan(
+                self.edge_wcell, self.edge_wclass, self.win_ptr, self.wl_off, self.pos_cell_off, self.N_c,
+                self.window_pos, cfg.dec_classes)
         if cfg.cell_nodes:
             r_sorted, rorder = ops.argsort(b.radius_dst, self.N_c)
             self.r_src = ops.gather_i64(b.radius_src, rorder)
@@ -408,6 +420,16 @@ class _Tables:
             self.a_src = ops.gather_i64(b.adjacency_src, aorder)
             self.a_cls = torch.zeros_like(self.a_src)
             self.a_ptr = ops.csr(a_sorted, self.N_c)
+
+
+    def _read_plan(self, src, cls, seg_ptr, q_off, s_off, n_src, q_pos, n_cls):
+        """(order, slots, slot-ordered packed edges) of a block-diagonal read:
+        rows of a position by ascending edge count."""
+        packed = ops.radius_pack(src, cls, seg_ptr, q_off, s_off, n_src, n_cls)
+        deg = (seg_ptr[1:] - seg_ptr[:-1]).clamp(max=63)
+        _, order = ops.argsort(q_pos * 64 + deg, self.P * 64)
+        slots, packed_slots = ops.radius_slots(packed, seg_ptr, q_off, order)
+        return order, slots, packed_slots
 
 
 class Engine:
@@ -822,8 +844,13 @@ class Engine:
         q = self.linear(zc_cr, blk["cr_wq"])
         kv = self.linear(zw_cr, blk["cr_kv"])
         with self.timed("cell_read"):
-            read = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["cr_bias"], blk["cr_vclass"], T.cell_ptr,
-                                         T.dec_window, T.dec_class, out_dtype=cd)
+            if T.cr_slots is not None:
+                read = ops.radius_read(q, kv[:, :h], kv[:, h:], blk["cr_bias"], blk["cr_vclass"], T.cell_ptr,
+                                       T.cr_pack, T.pos_cell_off, T.wl_off, 1, order=T.cr_order, out_dtype=cd,
+                                       slots=T.cr_slots)
+            else:
+                read = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["cr_bias"], blk["cr_vclass"], T.cell_ptr,
+                                             T.dec_window, T.dec_class, out_dtype=cd)
         simple = not (cfg.cell_structure or cfg.cell_adjacency)
         exit_ln = (nxt["ln_cr_c"], None) if nxt is not None else (self.ln_out, self._exit_c)
         reads = None
@@ -878,8 +905,12 @@ class Engine:
         q = self.linear(zw_wr, blk["wr_wq"])
         kv = self.linear(zc_wr, blk["wr_kv"])
         with self.timed("window_read"):
-            back = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["wr_bias"], None, T.win_ptr, T.edge_wcell,
-                                         T.edge_wclass, out_dtype=cd)
+            if T.wr_slots is not None:
+                back = ops.radius_read(q, kv[:, :h], kv[:, h:], blk["wr_bias"], None, T.win_ptr, T.wr_pack, T.wl_off,
+                                       T.pos_cell_off, 1, order=T.wr_order, out_dtype=cd, slots=T.wr_slots)
+            else:
+                back = ops.segment_attention(q, kv[:, :h], kv[:, h:], blk["wr_bias"], None, T.win_ptr, T.edge_wcell,
+                                             T.edge_wclass, out_dtype=cd)
         if nxt is not None:
             return back, c, zc_out, None
         return back, c, None, zc_out

@@ -42,6 +42,28 @@ def test_hex_message_pass_matches_restatement(n_pos, rows):
     mb._lib.check_device_error()
 
 
+@pytest.mark.parametrize("layout", ["far", "strided"])
+def test_hex_message_pass_far_neighbours_and_strided_rows(layout):
+    """Neighbours outside a tile's rows +- 64 (read from global memory, not
+    the shared-memory window), and strided rows (the gathering row GEMM)."""
+    x, nbr, w, b = _message_case(4, 21)
+    n = x.shape[0]
+    if layout == "far":
+        g = torch.Generator().manual_seed(5)
+        far = torch.randint(0, n, (n, 6), generator=g, dtype=torch.int32)
+        keep = torch.rand(n, 6, generator=g) < 0.3
+        nbr = torch.where(keep, far, nbr)
+        xd = x.to(DEV)
+    else:
+        xd = torch.empty(n, 384, dtype=torch.bfloat16, device=DEV)[:, :256]
+        xd.copy_(x.to(DEV))
+    want = ISO.hex_message_pass(x.double(), nbr, w.double(), b.double())
+    got = ops.hex_message_pass(xd, nbr.to(DEV), ops.weight_image(w.to(DEV)), b.to(DEV))
+    torch.cuda.synchronize()
+    torch.testing.assert_close(got.double().cpu(), want, rtol=1e-2, atol=2e-2)
+    mb._lib.check_device_error()
+
+
 def test_hex_message_pass_edges():
     x, nbr, w, b = _message_case(2, 3)
     nbr[:100] = -1  # rows with no neighbour: y = x + b
