@@ -338,13 +338,20 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const __grid_consta
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n_tiles = (p.m + BM - 1) / BM;
-  const int64_t my_tiles = n_tiles > blockIdx.x ? (n_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  // A units: the A tiles the producers write, in MMA order. Without WS one per
-  // tile, shared by its N blocks (work items t * n_blocks + nb); with WS one
-  // per work item, N-block-major (item nb * my_tiles + t).
   const int nbn = p.n_blocks;
-  const int64_t n_units = WS ? my_tiles * nbn : my_tiles;
-  auto unit_tile = [&](int64_t u) -> int64_t { return WS ? u % my_tiles : u; };
+  // Tile groups: without WS a CTA takes tiles blockIdx.x + k * gridDim.x and
+  // runs all N blocks of each. With WS the grid is n_blocks CTAs per group:
+  // CTA b holds N block b % n_blocks of W and takes the tiles of group
+  // b / n_blocks, so the CTAs of one group read the same A tiles at about
+  // the same time and every A tile but the first read of it comes from L2.
+  const int64_t grp = WS ? blockIdx.x / nbn : blockIdx.x;
+  const int64_t gstride = WS ? gridDim.x / nbn : gridDim.x;
+  const int ws_nb = WS ? (int)(blockIdx.x % nbn) : 0;
+  const int64_t my_tiles = n_tiles > grp ? (n_tiles - 1 - grp) / gstride + 1 : 0;
+  // A units: the A tiles the producers write, in MMA order: one per tile
+  // (shared by its N blocks without WS: work items t * n_blocks + nb).
+  const int64_t n_units = my_tiles;
+  auto unit_tile = [&](int64_t u) -> int64_t { return u; };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < A_RING; ++i) {
@@ -405,16 +412,15 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const __grid_consta
         }
         return true;
       };
-      // WS: the whole N block nb into shared memory once the previous block's
-      // MMAs are done with it
+      // WS: the CTA's N block nb into shared memory, once (each CTA of a tile
+      // group holds one N block for all its tiles)
       auto load_block = [&](int nb) -> bool {
-        if (nb > 0 && !mbar_wait(smem_u32(&w_empty[0]), (nb - 1) & 1, abort)) return false;
         const uint32_t kb_bytes = (uint32_t)(nb == nbn - 1 ? p.n_last : BN) * 128u;
         mbar_expect_tx(smem_u32(&w_full[0]), kb_bytes * KB);
         for (int kb = 0; kb < KB; ++kb)
           bulk_g2s(smem_u32(w_smem + kb * kb_bytes), wimg + (size_t)nb * BN * KB * 128 + (size_t)kb * kb_bytes,
                    kb_bytes, smem_u32(&w_full[0]));
-        if (!mbar_wait(smem_u32(&w_full[0]), nb & 1, abort)) return false;
+        if (!mbar_wait(smem_u32(&w_full[0]), 0, abort)) return false;
         tc_fence_after();
         return true;
       };
@@ -423,7 +429,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const __grid_consta
       for (int64_t u = 0; ok && u < n_units && !*abort; ++u) {
         const int64_t t = unit_tile(u);
         const uint32_t ab = u % L::A_BUFS, aph = (u / L::A_BUFS) & 1;
-        const int nb0 = WS ? (int)(u / my_tiles) : 0, nb1 = WS ? nb0 + 1 : nbn;
+        const int nb0 = WS ? ws_nb : 0, nb1 = WS ? nb0 + 1 : nbn;
         if constexpr (WS) {
           if (t == 0 && !load_block(nb0)) break;
         }
@@ -479,9 +485,6 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const __grid_consta
         }
         if (!ok) break;
         if constexpr (!L::RING_A) umma_commit(smem_u32(&a_empty[ab]));  // the A tile may be rewritten
-        if constexpr (WS) {
-          if (t == my_tiles - 1) umma_commit(smem_u32(&w_empty[0]));  // this N block's W may be replaced
-        }
       }
     }
   }
@@ -490,7 +493,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const __grid_consta
     if (lane == 1) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tmap_x)) : "memory");
       for (int64_t u = 0; u < n_units && !*abort; ++u) {
-        const int64_t tile = blockIdx.x + unit_tile(u) * gridDim.x;
+        const int64_t tile = grp + unit_tile(u) * gstride;
         bool ok = true;
         for (int kb = 0; kb < KB; ++kb) {
           const uint64_t aseq = (uint64_t)u * KB + kb;
@@ -509,7 +512,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const __grid_consta
     if (lane == 1) {
       const float* x = reinterpret_cast<const float*>(p.x);
       for (int64_t t = 0; t < my_tiles && !*abort; ++t) {
-        const int64_t tile = blockIdx.x + t * gridDim.x;
+        const int64_t tile = grp + t * gstride;
         bool ok = true;
         for (int grp = 0; grp < BM / XG_ROWS; ++grp) {
           const uint64_t seq = (uint64_t)t * (BM / XG_ROWS) + grp;
@@ -572,7 +575,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const __grid_consta
     if constexpr (XS) {
       const int pw = warp - 1;  // 0..6: rows pw, pw + 7, ... of each 32-row group
       for (int64_t t = 0; t < my_tiles && !*abort; ++t) {
-        const int64_t tile = blockIdx.x + t * gridDim.x;
+        const int64_t tile = grp + t * gstride;
         uint8_t* abuf = a_smem;
         bool ok = true;
         for (int grp = 0; grp < BM / XG_ROWS; ++grp) {
@@ -613,7 +616,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const __grid_consta
     } else {
       const int pw = warp - 1;  // rows pw, pw + PRODUCERS, ... of each tile
       for (int64_t u = 0; u < n_units && !*abort; ++u) {
-        const int64_t tile = blockIdx.x + unit_tile(u) * gridDim.x;
+        const int64_t tile = grp + unit_tile(u) * gstride;
         const uint32_t ab = u % L::A_BUFS, aph = (u / L::A_BUFS) & 1;
         uint8_t* abuf = a_smem + ab * L::A_BYTES;
         if constexpr (PRO == PRO_COPY) {
@@ -752,7 +755,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const __grid_consta
     const int64_t n_boxes = L::RESID ? my_tiles * CHUNKS : 0;
     auto issue_box = [&](int64_t k) {
       if (k < n_boxes) {
-        const int64_t tile = blockIdx.x + (k / CHUNKS) * gridDim.x;
+        const int64_t tile = grp + (k / CHUNKS) * gstride;
         const int col = half * (BN / PARTS) + (int)(k % CHUNKS) * 32 + (lane & 7) * 4;
         float* box = ring + (k % RING) * BOX_FLOATS;
 #pragma unroll
@@ -769,10 +772,11 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const __grid_consta
     if constexpr (L::RESID) {
       for (int64_t k = 0; k < RING; ++k) issue_box(k);
     }
-    for (int64_t it = 0; it < my_tiles * nbn && !*abort; ++it) {  // nbn = 1 for the residual epilogues
-      const int64_t t = WS ? it % my_tiles : it / nbn;
-      const int nb = (int)(WS ? it / my_tiles : it % nbn);
-      const int64_t tile = blockIdx.x + t * gridDim.x;
+    const int64_t n_items = WS ? my_tiles : my_tiles * nbn;  // nbn = 1 for the residual epilogues
+    for (int64_t it = 0; it < n_items && !*abort; ++it) {
+      const int64_t t = WS ? it : it / nbn;
+      const int nb = WS ? ws_nb : (int)(it % nbn);
+      const int64_t tile = grp + t * gstride;
       const uint32_t tb = it & 1, tph = (it >> 1) & 1;
       if (!mbar_wait(smem_u32(&t_full[tb]), tph, abort)) break;
       tc_fence_after();
@@ -1122,7 +1126,10 @@ static int launch_rowgemm(const Params& prm, cudaStream_t s, const char* what) {
   if (Plan<PRO, EPI, XS, KB, WS>::L1_HEAVY)  // the smallest shared-memory carveout that fits: the rest is L1
     cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 0);
   const int64_t tiles = cdiv(prm.m, BM);
-  const int grid = (int)(tiles < num_sms() ? tiles : num_sms());
+  // WS: n_blocks CTAs per tile group (see rowgemm_kernel)
+  const int per = WS ? prm.n_blocks : 1;
+  const int64_t groups = std::max<int64_t>(1, std::min<int64_t>(tiles, num_sms() / per));
+  const int grid = (int)(groups * per);
   kern<<<grid, THREADS, smem_bytes, s>>>(prm);
   return launch_status(what);
 }
