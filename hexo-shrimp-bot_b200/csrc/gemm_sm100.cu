@@ -238,9 +238,13 @@ struct alignas(64) Params {
   void* ln_out[MAX_LN];
   int ln_dtype[MAX_LN];
   int64_t ln_ld[MAX_LN];
-  // N blocks per tile (256 columns each; the last one n_last = 128 or 256)
+  // N blocks per tile (256 columns each, 128 for the K = 512 weight-
+  // stationary plan; the last one n_last = 128 or 256)
   int n_blocks;
   int n_last;
+  // the weight image's own 256-row blocks (w_blocks, the last w_last rows)
+  int w_blocks;
+  int w_last;
   // EPI_STORE: optional fp32 addend rows (add + row * ld_add + column)
   const float* add;
   int64_t ld_add;
@@ -271,8 +275,13 @@ struct Plan {
   // 256: 128 KB) and runs every one of its row tiles against it before the
   // next N block, so W crosses from L2 once per CTA and N block instead of
   // once per tile; its A tiles are re-read for each N block.
-  static_assert(!WS || (KB == 4 && !RESID && !XS && (PRO == PRO_TMA || PRO == PRO_LN)),
-                "the weight-stationary plan serves K = 256 bf16-output launches");
+  static_assert(!WS || (!RESID && !XS && (PRO == PRO_TMA || (PRO == PRO_LN && KB == 4))),
+                "the weight-stationary plan serves bf16-output launches");
+  // K = 512 keeps a 128-column N block stationary (128 KB of W) and streams
+  // its A K-blocks through a four-slot ring.
+  static constexpr bool HALF = WS && KB == 8;
+  static constexpr int BNB = HALF ? 128 : BN;       // columns per N block
+  static constexpr int WKB = BNB * BK * 2;          // bytes per stationary W K-block
   // The neighbour-mean prologue keeps one tile and one W stage so that the
   // L1 cache keeps most of the SM's 256 KB: a tile's neighbour rows (its own
   // rows +- 64) are then gathered from L1 after their first touch.
@@ -281,8 +290,8 @@ struct Plan {
   // PRO_TMA keeps K-block slots in a ring instead of whole tiles: a slot is
   // refilled as soon as the MMAs that read it finish.
   static constexpr bool RING_A = PRO == PRO_TMA;
-  static constexpr int A_SLOTS = RING_A ? ((RESID || WS) ? KB : A_RING) : 0;
-  static_assert(!RING_A || A_SLOTS >= KB, "a tile's K-blocks must fit the ring");
+  static constexpr int A_SLOTS = RING_A ? (RESID ? KB : (WS ? (HALF ? 4 : KB) : A_RING)) : 0;
+  static_assert(!RING_A || A_SLOTS >= KB || HALF, "a tile's K-blocks must fit the ring");
   static constexpr int A_SPACE = RING_A ? A_SLOTS * A_KB_BYTES : A_BUFS * A_BYTES;
   // bf16-output epilogues stage 32 x 32 boxes for whole-segment stores
   static constexpr bool OUT_BOXES = EPI == EPI_RESID_LN || EPI == EPI_STORE || EPI == EPI_ADD_X;
@@ -298,7 +307,7 @@ struct Plan {
   static constexpr int EPI_WARPS = 16 - 1 - PRODUCERS;
   static constexpr int A_OFF = 0;
   static constexpr int W_OFF = A_OFF + A_SPACE;
-  static constexpr int X_OFF = W_OFF + (WS ? KB : W_STAGES) * W_KB_BYTES;
+  static constexpr int X_OFF = W_OFF + (WS ? KB * WKB : W_STAGES * W_KB_BYTES);
   // staged LayerNorm rows: 32-row groups in flight (two when the output boxes
   // need the space)
   static constexpr int XSTAGES = OUT_BOXES ? 2 : X_STAGES;
@@ -415,11 +424,15 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const __grid_consta
       // WS: the CTA's N block nb into shared memory, once (each CTA of a tile
       // group holds one N block for all its tiles)
       auto load_block = [&](int nb) -> bool {
-        const uint32_t kb_bytes = (uint32_t)(nb == nbn - 1 ? p.n_last : BN) * 128u;
+        const uint32_t kb_bytes = (uint32_t)(nb == nbn - 1 ? p.n_last : L::BNB) * 128u;
+        // block nb in the image: 256-row image block wb, rows from h * BNB
+        const int wb = L::HALF ? nb >> 1 : nb, h = L::HALF ? nb & 1 : 0;
+        const size_t wrows = (size_t)(wb == p.w_blocks - 1 ? p.w_last : BN);
         mbar_expect_tx(smem_u32(&w_full[0]), kb_bytes * KB);
         for (int kb = 0; kb < KB; ++kb)
-          bulk_g2s(smem_u32(w_smem + kb * kb_bytes), wimg + (size_t)nb * BN * KB * 128 + (size_t)kb * kb_bytes,
-                   kb_bytes, smem_u32(&w_full[0]));
+          bulk_g2s(smem_u32(w_smem + kb * kb_bytes),
+                   wimg + (size_t)wb * BN * KB * 128 + (size_t)kb * wrows * 128 + (size_t)h * L::BNB * 128, kb_bytes,
+                   smem_u32(&w_full[0]));
         if (!mbar_wait(smem_u32(&w_full[0]), 0, abort)) return false;
         tc_fence_after();
         return true;
@@ -443,7 +456,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const __grid_consta
           if (!mbar_wait(smem_u32(&t_empty[tb]), tph ^ 1, abort)) { ok = false; break; }
           tc_fence_after();
           const uint32_t d = tmem_base + tb * BN;
-          const int rows = nb == nbn - 1 ? p.n_last : BN;
+          const int rows = nb == nbn - 1 ? p.n_last : L::BNB;
           const uint32_t idesc = make_idesc(rows);
           for (int kb = 0; kb < KB; ++kb, ++used) {
             const uint32_t s = used % L::W_STAGES, ph = (used / L::W_STAGES) & 1;
@@ -969,7 +982,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const __grid_consta
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&t_empty[tb]));
       } else {
-      const int cols = nb == nbn - 1 ? p.n_last : BN;
+      const int cols = nb == nbn - 1 ? p.n_last : L::BNB;
       const int cend = (half + 1) * (BN / PARTS) < cols ? (half + 1) * (BN / PARTS) : cols;
       const int nr = (int)(p.m - row0 < 32 ? (p.m - row0 < 0 ? 0 : p.m - row0) : 32);  // live rows of the warp
       uint4* sb = reinterpret_cast<uint4*>(smem + L::OUT_OFF + ew * OUT_BOX_BYTES);
@@ -977,7 +990,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const __grid_consta
       for (int c0 = half * (BN / PARTS); c0 < cend; c0 += 32) {
         float v[32];
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + tb * BN + c0, v);
-        const int oc = nb * BN + c0;  // output column
+        const int oc = nb * L::BNB + c0;  // output column
         if (p.bias) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
@@ -1148,6 +1161,8 @@ static Params base_params() {
   Params prm{};
   prm.n_blocks = 1;
   prm.n_last = BN;
+  prm.w_blocks = 1;
+  prm.w_last = BN;
   return prm;
 }
 
@@ -1215,6 +1230,8 @@ int mb_gemm_rows_ex(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t 
   prm.ld_add = ld_add;
   prm.n_blocks = (int)cdiv(n, BN);
   prm.n_last = (int)(n - (int64_t)(prm.n_blocks - 1) * BN);
+  prm.w_blocks = prm.n_blocks;
+  prm.w_last = prm.n_last;
   cudaStream_t s = as_stream(stream);
   if (ln) {
     if (g_ln_plan == 1) return launch_rowgemm<PRO_LN, EPI_STORE, false, 4, true>(prm, s, "gemm_rows");
@@ -1227,7 +1244,16 @@ int mb_gemm_rows_ex(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t 
   if (!encode_rows_map(&prm.tmap_x, x, m, k, ldx))
     return ::mb::fail(MB_LAUNCH_FAILED, "gemm_rows: could not encode the input tensor map");
   if (out) {
-    if (k == 512) return launch_rowgemm<PRO_TMA, EPI_STORE, false, 8>(prm, s, "gemm_rows");
+    if (k == 512) {
+      // 128-column weight-stationary blocks; wider outputs stream W instead,
+      // which measured faster there (four CTAs per tile group re-read A)
+      if (g_store_plan == 1 && n <= BN) {
+        prm.n_blocks = (int)(n / 128);
+        prm.n_last = 128;
+        return launch_rowgemm<PRO_TMA, EPI_STORE, false, 8, true>(prm, s, "gemm_rows");
+      }
+      return launch_rowgemm<PRO_TMA, EPI_STORE, false, 8>(prm, s, "gemm_rows");
+    }
     if (g_store_plan == 1) return launch_rowgemm<PRO_TMA, EPI_STORE, false, 4, true>(prm, s, "gemm_rows");
     return launch_rowgemm<PRO_TMA, EPI_STORE, false, 4>(prm, s, "gemm_rows");
   }
@@ -1271,6 +1297,7 @@ int mb_gemm_rows_head(const void* x, int64_t ldx, int64_t m, const void* w_image
   prm.bias = bias;
   prm.m = m;
   prm.n_last = (int)n;
+  prm.w_last = (int)n;
   prm.tok = (const __nv_bfloat16*)tok;
   prm.ld_tok = ld_tok;
   prm.n_tok = n_tok;
