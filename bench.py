@@ -217,23 +217,25 @@ def run_ours(args, rank, world, local_rank):
     lib.load()
 
     # Inputs: encoded on the host (the native encoder, all host threads)
-    # before touching the GPU; its rate on the distinct positions is reported.
+    # straight into pinned host memory, ready for the host-to-device copy;
+    # its rate on the distinct positions is reported (the second call: the
+    # first one also sets up the vocabulary tables and the pinned blocks).
     n_chunks = math.ceil(args.positions / args.chunk)
     specs = make_specs(args.unique, args.lo, args.hi, seed=1000 + rank)
-    mb.encoder.encode(specs[:8])  # first call builds the vocabulary tables
-    t0 = time.perf_counter()
-    mb.encoder.encode(specs)
-    enc_s = time.perf_counter() - t0
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    for _ in range(2):
+        t0 = time.perf_counter()
+        mb.encoder.encode(specs, pin_memory=True)
+        enc_s = time.perf_counter() - t0
     encoder = {"value": len(specs) / enc_s, "unit": "positions/s", "threads": os.cpu_count() or 1,
                "sample": f"{len(specs)} distinct late positions ({args.lo}-{args.hi} stones), collated batch "
-                         "in pageable host memory"}
+                         "written into pinned host memory"}
     reps = math.ceil(args.chunk / len(specs))
     host = mb.encoder.encode((specs * reps)[: args.chunk])
     fields = mb.evaluator.needed_fields(mb.MantisConfig(**ARCH))
     host_pinned = host.pin_memory()
 
-    device = torch.device("cuda", local_rank)
-    torch.cuda.set_device(device)
     if world > 1:
         dist.init_process_group("nccl", device_id=device, timeout=__import__("datetime").timedelta(seconds=600))
 
