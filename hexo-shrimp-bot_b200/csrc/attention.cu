@@ -631,9 +631,16 @@ __global__ void __cluster_dims__(1, kReadSplit, 1) __launch_bounds__(kReadWarps 
         m[s] = m_new;
       }
     };
+    // the next step's order entries are requested a step ahead, so a step
+    // waits on its K/V rows only
+    int64_t n0 = beg + warp < end ? order[beg + warp] : -1;
+    int64_t n1 = beg + warp + kReadWarps < end ? order[beg + warp + kReadWarps] : -1;
     for (int64_t i = beg + warp; i < end; i += 2 * kReadWarps) {
       const int64_t i1 = i + kReadWarps;
-      int64_t w0 = order[i], w1 = i1 < end ? order[i1] : -1;
+      int64_t w0 = n0, w1 = i1 < end ? n1 : -1;
+      const int64_t j = i + 2 * kReadWarps;
+      if (j < end) n0 = order[j];
+      if (j + kReadWarps < end) n1 = order[j + kReadWarps];
       const bool ok0 = w0 >= 0 && w0 < n_windows, ok1 = i1 < end && w1 >= 0 && w1 < n_windows;
       if (!ok0 || (i1 < end && !ok1)) report(ERR_INDEX);
       Raw<T, VEC> k0 = {}, v0 = {}, k1 = {}, v1 = {};
