@@ -612,9 +612,23 @@ def run_op(args):
         ms = _time_launches(lambda: ops.hex_message_pass(x, nb, img, b, out=out), args.steps, args.warmup)
         algo = 2 * n * 256 * 2 + n * 6 * 4 + 256 * 256 * 2 + 256 * 4
         flops = 2 * n * 256 * 256
+        # the fp32 eager CPU restatement on the first 16 positions (all host threads), scaled per node
+        from oracle import isolated as ISO
+        torch.set_num_threads(os.cpu_count() or 1)
+        sub = 16 * 256
+        xs, ns, ws, bs = x[:sub].float().cpu(), nb[:sub].cpu().clone(), w.float().cpu(), b.cpu()
+        ns[ns >= sub] = -1
+        ISO.hex_message_pass(xs, ns, ws, bs)
+        t0 = time.perf_counter()
+        ISO.hex_message_pass(xs, ns, ws, bs)
+        cpu_ms = (time.perf_counter() - t0) * 1000.0
         line = {"metric": "hex message-pass nodes/s (config 3)", "value": n / (ms / 1000.0), "unit": "nodes/s",
                 "ms_per_step": ms, "config": {"workload": f"config 3: {p} x 256 cell tokens, F=256, bf16", "nodes": n},
-                "roofline": {"kernel": "rowgemm_kernel<HEXMEAN, ADD_X>", "bound": "hbm",
+                "cpu_baseline": {"kind": "port", "sample": f"{sub} nodes (16 positions), fp32 eager CPU restatement",
+                                 "ms": cpu_ms, "cores": os.cpu_count() or 1,
+                                 "value": sub / (cpu_ms / 1000.0), "unit": "nodes/s"},
+                "roofline": {"kernel": "hex_window_kernel" if x.stride(0) == 256 else "rowgemm_kernel<HEXMEAN, ADD_X>",
+                             "bound": "hbm",
                              "achieved": algo / ms / 1e6, "peak": pk["hbm_gbs"], "unit": "GB/s",
                              "frac": algo / ms / 1e6 / pk["hbm_gbs"], "peak_kind": kind, "algorithmic_bytes": algo,
                              "tflops": flops / ms / 1e9}}
@@ -629,8 +643,20 @@ def run_op(args):
         lv = valid.astype(np.float64)
         flops = float((8 * 4 * 32 * lv ** 2).sum())
         algo = float(((3 * lv + 256) * 8 * 32 * 2 + 256 * 8 + 4).sum() + 33 * 33 * 8 * 4)
+        # the fp32 eager CPU restatement on the first 16 positions (all host threads)
+        from oracle import isolated as ISO
+        torch.set_num_threads(os.cpu_count() or 1)
+        qs, ks, vs = (t[:16].float().cpu() for t in (q, k, v))
+        cs, vls, bs = c[:16].cpu(), vl[:16].cpu(), bias.cpu()
+        ISO.axial_attention(qs[:2], ks[:2], vs[:2], cs[:2], vls[:2], bs)
+        t0 = time.perf_counter()
+        ISO.axial_attention(qs, ks, vs, cs, vls, bs)
+        cpu_ms = (time.perf_counter() - t0) * 1000.0
         line = {"metric": "axial-bias attention positions/s (config 2)", "value": p / (ms / 1000.0),
                 "unit": "positions/s", "ms_per_step": ms,
+                "cpu_baseline": {"kind": "port", "sample": "16 positions, fp32 eager CPU restatement", "ms": cpu_ms,
+                                 "cores": os.cpu_count() or 1, "value": 16 / (cpu_ms / 1000.0),
+                                 "unit": "positions/s"},
                 "config": {"workload": f"config 2: {p} positions x 8 heads x 256 tokens, d=32, bf16"},
                 "roofline": {"kernel": "axial_attention_kernel", "bound": "hbm", "achieved": algo / ms / 1e6,
                              "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": algo / ms / 1e6 / pk["hbm_gbs"],
@@ -639,6 +665,75 @@ def run_op(args):
     line.update({"n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "bf16",
                  "data": "synthetic", "gpu_launches": 1})
     print(json.dumps(line))
+
+
+def run_config1(args):
+    """One JSON line per knob set for the config-1 baseline: 16 positions of
+    10-40 stones at the reference's default architecture (h=128, 4 blocks, 4
+    heads), the default (relay) knobs and the production knobs (cell_latents +
+    cell_nodes). This build's full forward (every head) on the GPU in fp32
+    and bf16, the batch resident, CUDA events (median of 20 after 3 warm-ups),
+    against the reference's own eager CPU `MantisNet.forward` from
+    baseline/_ref on all host threads (median of --steps after one warm-up),
+    and the reference's Python builder (build + collate) on the same
+    positions."""
+    import torch
+
+    mb = _pkg()
+    specs = make_specs(16, 10, 40, seed=17)
+    host = mb.collate([mb.from_spec(s) for s in specs])
+    dev = torch.device("cuda", 0)
+    ref = _reference_pkg()
+    mn = ref.load() if ref is not None else None
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    builder_ms = None
+    if mn is not None:
+        times = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            mn.builder.collate([mn.builder.build(s.stone_qr, s.stone_owner, s.mover, s.legal_qr, s.moves_remaining)
+                                for s in specs])
+            times.append((time.perf_counter() - t0) * 1000.0)
+        builder_ms = statistics.median(times)
+    for name, knobs in (("relay", {}), ("production", {"cell_latents": True, "cell_nodes": True})):
+        cfg = mb.MantisConfig(**knobs)
+        torch.manual_seed(0)
+        net = mb.MantisNet(cfg).to(dev).eval()
+        b = mb.evaluator.to_device(host, dev, tuple(k for k, v in vars(host).items() if isinstance(v, torch.Tensor)))
+        ours = {}
+        for dtype, key in ((torch.float32, "fp32"), (torch.bfloat16, "bf16")):
+            for _ in range(3):
+                net.forward(b, 0.2, dtype)
+            ms = []
+            for _ in range(20):
+                s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s0.record()
+                net.forward(b, 0.2, dtype)
+                s1.record()
+                torch.cuda.synchronize()
+                ms.append(s0.elapsed_time(s1))
+            ours[key] = statistics.median(ms)
+        ref_ms = None
+        if mn is not None:
+            torch.manual_seed(0)
+            rnet = mn.MantisNet(mn.MantisConfig(**knobs)).eval()
+            rb = mn.builder.Batch(**vars(host))
+            times = []
+            with torch.no_grad():
+                for i in range(1 + max(args.steps, 5)):
+                    t0 = time.perf_counter()
+                    rnet(rb, 0.2)
+                    if i > 0:
+                        times.append((time.perf_counter() - t0) * 1000.0)
+            ref_ms = statistics.median(times)
+        print(json.dumps({
+            "metric": "config 1 forward ms (16 positions, 10-40 stones, h128/4 blocks/4 heads)", "knobs": name,
+            "b200_ms": ours, "b200_positions_per_s": {k: 16 / (v / 1000.0) for k, v in ours.items()},
+            "reference_cpu_ms": ref_ms,
+            "reference_cpu_positions_per_s": (16 / (ref_ms / 1000.0)) if ref_ms else None,
+            "reference_builder_ms": builder_ms, "host_cores": threads, "torch_threads": torch.get_num_threads(),
+            "data": "synthetic", "unit": "ms"}), flush=True)
 
 
 def run_multi(args):
@@ -700,7 +795,7 @@ def main():
     ap.add_argument("--latency", type=int, default=1)
     ap.add_argument("--gemm", default="tcgen05-ln", help="dense projection path (see model.Engine)")
     ap.add_argument("--devices", type=int, default=0, help="GPUs of --op multi (default: all visible)")
-    ap.add_argument("--op", default=None, choices=["hex", "axial", "resid_ln", "radius", "multi"],
+    ap.add_argument("--op", default=None, choices=["hex", "axial", "resid_ln", "radius", "multi", "config1"],
                     help="time one isolated-op workload instead of the evaluator (config 3 / config 2 / the "
                          "fused projection + residual + LayerNorm launch)")
     ap.add_argument("--rows", type=int, default=1814720, help="rows of --op resid_ln (default: one chunk's windows)")
@@ -710,6 +805,9 @@ def main():
     args = ap.parse_args()
     if args.op == "multi":
         run_multi(args)
+        return
+    if args.op == "config1":
+        run_config1(args)
         return
     if args.op:
         run_op(args)
