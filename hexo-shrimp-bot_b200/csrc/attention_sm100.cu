@@ -7,18 +7,19 @@
 // keys j < valid[b] only; query rows i >= valid[b] are written as zeros.
 // head_dim 32, bf16 q/k/v/out, fp32 scores and softmax.
 //
-// One CTA per (position, head), 16 warps. Q, K and V^T are staged in shared
-// memory in the 128-byte-swizzled K-major layout the UMMA descriptors read
-// (Q and K rows carry the 32 head columns in the first 64 bytes). One thread
-// issues S = Q K^T for both 128-query tiles into TMEM (M=128, N=256, two
-// K=16 steps each). The warps split each live tile's keys into parts (two
-// parts per tile when both tiles are live, else four): a thread holds one
-// query row of one part (TMEM lane quadrant = warp % 4). A first pass adds
-// the offset bias, writes the biased scores back into TMEM and finds the part
-// maximum; the parts' maxima meet in shared memory; a second pass writes
-// exp(x - max) as bf16 into the P tile and sums it. P V^T (M=128, N=32,
-// K up to 256) then lands in the tile's own, now consumed, TMEM columns, and
-// the row is scaled by 1/sum and stored. Work is bounded by each position's
+// One CTA per (position, head), eight warps, two CTAs per SM so that one
+// CTA's staging and softmax overlap the other's. Q and K share one 128-byte
+// swizzled row per token (Q in the first 64 bytes, K in the second; the
+// UMMA descriptors start 0 or 64 bytes into the row), V is staged
+// transposed. Query tiles of 128 run one after the other: one thread issues
+// S = Q K^T into TMEM (M=128, N up to 256, two K=16 steps); a thread holds one
+// query row of one key half (TMEM lane quadrant = warp % 4). A first pass adds
+// the offset bias, writes the biased scores back into TMEM and finds the
+// half-row maximum; the halves' maxima meet in shared memory. Then per half of
+// the keys (128 at a time, through one 32 KB P buffer) a second pass writes
+// exp(x - max) as bf16 into P and sums it, and P V^T (M=128, N=32) accumulates
+// into the tile's first TMEM columns, whose scores are consumed by then. The
+// row is scaled by 1/sum and stored. Work is bounded by each position's
 // valid length. Every mbarrier wait is bounded (see gemm_sm100.cu).
 #include "common.cuh"
 
@@ -28,28 +29,26 @@ namespace sm100 {
 constexpr int AX_L = 256;          // tokens per position (maximum)
 constexpr int AX_D = 32;           // head dim
 constexpr int AX_SPAN = 33;        // relative offsets -16..16
-constexpr int AX_THREADS = 512;
-constexpr int AX_Q_BYTES = AX_L * 128;           // 32 KB, rows padded to 128 B
-constexpr int AX_K_BYTES = AX_L * 128;           // 32 KB
+constexpr int AX_THREADS = 256;
+constexpr int AX_QK_BYTES = AX_L * 128;          // 32 KB: Q | K per token row
 constexpr int AX_VT_KB = AX_D * 128;             // 4 KB per 64-key block of V^T (32 rows)
 constexpr int AX_VT_BYTES = 4 * AX_VT_KB;        // 16 KB
-constexpr int AX_P_KB = 128 * 128;               // 16 KB per 64-key block of a P tile
-constexpr int AX_P_BYTES = 4 * AX_P_KB;          // 64 KB per tile
-constexpr int AX_Q_OFF = 0;
-constexpr int AX_K_OFF = AX_Q_OFF + AX_Q_BYTES;
-constexpr int AX_VT_OFF = AX_K_OFF + AX_K_BYTES;
+constexpr int AX_P_KB = 128 * 128;               // 16 KB per 64-key block of P
+constexpr int AX_P_BYTES = 2 * AX_P_KB;          // one key half (128 keys)
+constexpr int AX_QK_OFF = 0;
+constexpr int AX_VT_OFF = AX_QK_OFF + AX_QK_BYTES;
 constexpr int AX_P_OFF = AX_VT_OFF + AX_VT_BYTES;
-constexpr int AX_BIAS_OFF = AX_P_OFF + 2 * AX_P_BYTES;
+constexpr int AX_BIAS_OFF = AX_P_OFF + AX_P_BYTES;
 constexpr int AX_COORD_OFF = AX_BIAS_OFF + 4400;  // 33*33 floats, rounded up
 constexpr int AX_RED_OFF = AX_COORD_OFF + AX_L * 8;  // per-row half maxima / sums
 constexpr int AX_BAR_OFF = AX_RED_OFF + 2 * 2 * 128 * 4;
 constexpr int AX_SMEM = AX_BAR_OFF + 64 + 1024;   // + alignment slack
-static_assert(AX_SMEM <= 232448, "axial attention shared memory exceeds 227 KB");
+static_assert(2 * AX_SMEM <= 232448, "axial attention must fit two CTAs per SM");
+constexpr int AX_TMEM_COLS = 256;                 // S of one tile; O reuses its first columns
 
 constexpr uint32_t idesc_f16(int m, int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
-constexpr uint32_t AX_IDESC_S = idesc_f16(128, AX_L);
 constexpr uint32_t AX_IDESC_O = idesc_f16(128, AX_D);
 
 __device__ __forceinline__ void umma_i(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -65,24 +64,24 @@ __device__ __forceinline__ void umma_i(uint32_t tmem_d, uint64_t adesc, uint64_t
 // K-major block whose rows are 128 bytes.
 __device__ __forceinline__ int swz(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
 
-__global__ void __launch_bounds__(AX_THREADS, 1) axial_attention_kernel(
+__global__ void __launch_bounds__(AX_THREADS, 2) axial_attention_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
     int64_t s_pos, int64_t s_head, int64_t s_row, int heads, int length, const int32_t* __restrict__ coords,
     const int32_t* __restrict__ valid, const float* __restrict__ bias, __nv_bfloat16* __restrict__ out,
     int64_t o_pos, int64_t o_head, int64_t o_row) {
   extern __shared__ uint8_t ax_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ax_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* qs = smem + AX_Q_OFF;
-  uint8_t* ks = smem + AX_K_OFF;
+  uint8_t* qk = smem + AX_QK_OFF;
   uint8_t* vt = smem + AX_VT_OFF;
   uint8_t* ps = smem + AX_P_OFF;
   float* bias_s = reinterpret_cast<float*>(smem + AX_BIAS_OFF);
   int2* kc = reinterpret_cast<int2*>(smem + AX_COORD_OFF);
+  float* red = reinterpret_cast<float*>(smem + AX_RED_OFF);  // [max | sum][half][128 rows]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + AX_BAR_OFF);
-  uint64_t* s_done = bars;       // [2]
-  uint64_t* o_done = bars + 2;   // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
-  volatile int* abort = reinterpret_cast<volatile int*>(bars + 5);
+  uint64_t* s_done = bars;       // one phase per query tile
+  uint64_t* o_done = bars + 1;   // one phase per (tile, key half)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
+  volatile int* abort = reinterpret_cast<volatile int*>(bars + 3);
 
   const int b = blockIdx.x / heads, h = blockIdx.x % heads;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -99,27 +98,23 @@ __global__ void __launch_bounds__(AX_THREADS, 1) axial_attention_kernel(
   const int32_t* cb = coords + (int64_t)b * length * 2;
 
   if (tid == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(smem_u32(&s_done[i]), 1);
-      mbar_init(smem_u32(&o_done[i]), 1);
-    }
+    mbar_init(smem_u32(&s_done[0]), 1);
+    mbar_init(smem_u32(&o_done[0]), 1);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(512)
+                 "r"(AX_TMEM_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
 
-  // ---- stage Q, K (4 logical 16-byte chunks per row), V^T, bias, key coords.
-  // Every global load of the thread is issued before the first shared store.
+  // ---- stage Q | K rows, V^T, bias, key coords (zero past the valid length)
+  // every global load of the thread is issued before the first shared store
   constexpr int PER = AX_L * 4 / AX_THREADS;  // 16-byte chunks of Q (and of K, V) per thread
-  constexpr int BPER = (AX_SPAN * AX_SPAN + AX_THREADS - 1) / AX_THREADS;
   const uint4 zero = make_uint4(0, 0, 0, 0);
   uint4 qv[PER], kv[PER], vv[PER];
-  float bv[BPER];
 #pragma unroll
   for (int u = 0; u < PER; ++u) {
     const int idx = tid + u * AX_THREADS, r = idx >> 2, c = idx & 3;
@@ -131,17 +126,10 @@ __global__ void __launch_bounds__(AX_THREADS, 1) axial_attention_kernel(
     }
   }
 #pragma unroll
-  for (int u = 0; u < BPER; ++u) {
-    const int idx = tid + u * AX_THREADS;
-    bv[u] = idx < AX_SPAN * AX_SPAN ? __ldg(bias + (int64_t)idx * heads + h) : 0.f;
-  }
-  const int2 kcv = tid < length && tid < AX_L ? make_int2(__ldg(cb + 2 * tid), __ldg(cb + 2 * tid + 1))
-                                              : make_int2(0, 0);
-#pragma unroll
   for (int u = 0; u < PER; ++u) {
     const int idx = tid + u * AX_THREADS, r = idx >> 2, c = idx & 3;
-    *reinterpret_cast<uint4*>(qs + swz(r, c)) = qv[u];
-    *reinterpret_cast<uint4*>(ks + swz(r, c)) = kv[u];
+    *reinterpret_cast<uint4*>(qk + swz(r, c)) = qv[u];
+    *reinterpret_cast<uint4*>(qk + swz(r, 4 + c)) = kv[u];
     // V row r, columns 8c..8c+7 -> V^T rows 8c..8c+7, column r
     const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&vv[u]);
     const int blk = r >> 6, jj = r & 63;
@@ -149,158 +137,153 @@ __global__ void __launch_bounds__(AX_THREADS, 1) axial_attention_kernel(
     for (int w = 0; w < 8; ++w)
       *reinterpret_cast<__nv_bfloat16*>(vt + blk * AX_VT_KB + swz(8 * c + w, jj >> 3) + (jj & 7) * 2) = e[w];
   }
-#pragma unroll
-  for (int u = 0; u < BPER; ++u) {
-    const int idx = tid + u * AX_THREADS;
-    if (idx < AX_SPAN * AX_SPAN) bias_s[idx] = bv[u];
-  }
-  if (tid < AX_L) kc[tid] = kcv;
+  for (int idx = tid; idx < AX_SPAN * AX_SPAN; idx += AX_THREADS) bias_s[idx] = __ldg(bias + (int64_t)idx * heads + h);
+  if (tid < AX_L) kc[tid] = tid < length ? make_int2(__ldg(cb + 2 * tid), __ldg(cb + 2 * tid + 1)) : make_int2(0, 0);
   fence_proxy_async();  // generic-proxy shared stores -> visible to the tensor cores
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // ---- S = Q K^T for each live query tile
-  if (tid == 0) {
-    for (int t = 0; t < n_tiles; ++t) {
-      const uint32_t d = tmem + t * AX_L;
-      const uint32_t a0 = smem_u32(qs + t * 128 * 128), b0 = smem_u32(ks);
-#pragma unroll
-      for (int j = 0; j < AX_D / 16; ++j) umma_i(d, smem_desc(a0 + j * 32), smem_desc(b0 + j * 32), AX_IDESC_S, j);
-      umma_commit(smem_u32(&s_done[t]));
-    }
-  }
-
-  // Warp roles: tile t = warp / 8 (queries 128t..128t+127), key half hf =
-  // (warp / 4) % 2 (keys 128hf..128hf+127), TMEM lane quadrant qd = warp % 4
-  // (rows 32qd..32qd+31 of the tile); a thread owns one query row of one half.
-  // With one live query tile all sixteen warps work on it in four key parts;
-  // with two, eight warps per tile in two parts.
-  const int NP = n_tiles == 2 ? 2 : 4;
-  const int t = warp / (4 * NP), hf = (warp >> 2) % NP, qd = warp & 3;
-  const int row = t * 128 + qd * 32 + lane;  // this thread's query
-  const int rl = qd * 32 + lane;             // row within the tile
+  // Warp roles: TMEM lane quadrant qd = warp % 4 (rows 32qd..32qd+31 of the
+  // tile), key half hf = warp / 4. Work is bounded by the valid length:
+  // score columns up to nv rounded to a 32-column load, P and P V up to nv
+  // rounded to a 64-key block.
+  const int qd = warp & 3, hf = warp >> 2;
+  const int rl = qd * 32 + lane;
   const float scale = 0.17677669529663687f;  // 1 / sqrt(32)
-  // Work is bounded by the valid length: score columns up to nv rounded to a
-  // 32-column load, P and the P V product up to nv rounded to a 64-key block,
-  // and warps whose 32 queries all lie past nv skip the softmax (their rows
-  // are written as zeros). TMEM loads are warp-collective, so the bound is
-  // per warp.
   const int kend = min(AX_L, (nv + 31) & ~31);
+  const int npad = (nv + 15) & ~15;
   const int kblocks = (nv + 63) >> 6;
-  const bool warp_live = t < n_tiles && t * 128 + qd * 32 < nv;
-  // this part's keys: a multiple of 32, parts together covering kblocks * 64
-  const int span = ((kend + NP * 32 - 1) / (NP * 32)) * 32;
-  const int c_lo = hf * span, c_hi = min(c_lo + span, kend), p_hi = min(c_lo + span, kblocks * 64);
-  const int nthr = 128 * NP;  // threads of this tile's group
-  float* red = reinterpret_cast<float*>(smem + AX_RED_OFF);  // [tile][part][128 rows]
-  float* red_t = red + t * NP * 128;
+  const int halves = (kblocks + 1) >> 1;
+  const uint32_t taddr = tmem + ((uint32_t)(qd * 32) << 16);
+  float* red_m = red;
+  float* red_s = red + 2 * 128;
   bool ok = true;
-  float m = -INFINITY, sum = 0.f;
-  const uint32_t taddr = tmem + ((uint32_t)(qd * 32) << 16) + t * AX_L;
-  if (warp_live) {
-    ok = mbar_wait(smem_u32(&s_done[t]), 0, abort);
-    tc_fence_after();
-    const int2 qc = row < length ? make_int2(__ldg(cb + 2 * row), __ldg(cb + 2 * row + 1)) : make_int2(0, 0);
+  int phase_s = 0, phase_o = 0;
+  for (int t = 0; t < n_tiles; ++t) {
+    const int row = t * 128 + rl;
+    const bool warp_live = t * 128 + qd * 32 < nv;
+    if (tid == 0 && !*abort) {
+      const uint32_t a0 = smem_u32(qk + t * 128 * 128), b0 = smem_u32(qk);
+#pragma unroll
+      for (int j = 0; j < AX_D / 16; ++j)
+        umma_i(tmem, smem_desc(a0 + j * 32), smem_desc(b0 + 64 + j * 32), idesc_f16(128, npad), j);
+      umma_commit(smem_u32(&s_done[0]));
+    }
     // pass 1: biased scores back into TMEM, the half-row maximum
-    if (ok) {
+    float m = -INFINITY;
+    ok = ok && mbar_wait(smem_u32(&s_done[0]), phase_s, abort);
+    phase_s ^= 1;
+    tc_fence_after();
+    if (ok && warp_live) {
+      const int2 qc = row < length ? make_int2(__ldg(cb + 2 * row), __ldg(cb + 2 * row + 1)) : make_int2(0, 0);
+      const int c_lo = hf * 128, c_hi = min(c_lo + 128, kend);
 #pragma unroll 1
       for (int c0 = c_lo; c0 < c_hi; c0 += 32) {
-        float s[32];
-        tmem_ld32(taddr + c0, s);
+        float sc[32];
+        tmem_ld32(taddr + c0, sc);
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
           const int j = c0 + jj;
           const int2 c = kc[j];
           const int dq = min(max(c.x - qc.x, -16), 16) + 16, dr = min(max(c.y - qc.y, -16), 16) + 16;
-          s[jj] = j < nv ? s[jj] * scale + bias_s[dq * AX_SPAN + dr] : -INFINITY;
-          m = fmaxf(m, s[jj]);
+          sc[jj] = j < nv ? sc[jj] * scale + bias_s[dq * AX_SPAN + dr] : -INFINITY;
+          m = fmaxf(m, sc[jj]);
         }
-        tmem_st32(taddr + c0, s);
+        tmem_st32(taddr + c0, sc);
       }
       tmem_st_wait();
     }
-    red_t[hf * 128 + rl] = m;
-  }
-  asm volatile("bar.sync %0, %1;" ::"r"(1 + t), "r"(nthr) : "memory");
-  if (warp_live) {
-    for (int pp = 0; pp < NP; ++pp) m = fmaxf(m, red_t[pp * 128 + rl]);
-    // pass 2: P = exp(x - m) in bf16 into the tile's P blocks, the half-row sum
-    uint8_t* pt = ps + t * AX_P_BYTES;
-#pragma unroll 1
-    for (int c0 = c_lo; c0 < p_hi; c0 += 32) {
-      float s[32];
-      if (ok && c0 < c_hi) tmem_ld32(taddr + c0, s);
-#pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
-        const float p = (ok && c0 + jj < nv) ? __expf(s[jj] - m) : 0.f;
-        sum += p;
-        s[jj] = p;
-      }
-      const int blk = c0 >> 6;
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        store_vec<8>(reinterpret_cast<__nv_bfloat16*>(pt + blk * AX_P_KB + swz(rl, ((c0 & 63) >> 3) + u)), s + 8 * u);
-    }
-    fence_proxy_async();
+    red_m[hf * 128 + rl] = m;
     tc_fence_before();
-  }
-  // the maxima are read; the sums reuse the same slots after the barrier
-  asm volatile("bar.sync %0, %1;" ::"r"(1 + t), "r"(nthr) : "memory");
-  if (warp_live) red_t[hf * 128 + rl] = sum;
-  asm volatile("bar.sync %0, %1;" ::"r"(1 + t), "r"(nthr) : "memory");
-  // the tile's eight warps have written P and read all of S: O may overwrite S
-  if (t < n_tiles && hf == 0 && qd == 0 && lane == 0) {
+    __syncthreads();
     tc_fence_after();
-    const uint32_t d = tmem + t * AX_L;
-    for (int blk = 0; blk < kblocks; ++blk) {
-      const uint32_t a0 = smem_u32(ps + t * AX_P_BYTES + blk * AX_P_KB), b0 = smem_u32(vt + blk * AX_VT_KB);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) umma_i(d, smem_desc(a0 + j * 32), smem_desc(b0 + j * 32), AX_IDESC_O, (blk | j) != 0);
-    }
-    umma_commit(smem_u32(&o_done[t]));
-  }
-  if (hf == 0) {
-    float o[AX_D];
-#pragma unroll
-    for (int i = 0; i < AX_D; ++i) o[i] = 0.f;
-    if (warp_live && ok) {
-      float tot = 0.f;
-      for (int pp = 0; pp < NP; ++pp) tot += red_t[pp * 128 + rl];
-      const float inv = tot > 0.f ? 1.f / tot : 0.f;
-      if (mbar_wait(smem_u32(&o_done[t]), 0, abort)) {
+    m = fmaxf(red_m[rl], red_m[128 + rl]);
+    // per key half: P = exp(x - m) in bf16 (this warp's 64-key block of the
+    // half), the partial sum, then P V^T accumulated into columns 0..31
+    float sum = 0.f;
+    for (int hh = 0; hh < halves; ++hh) {
+      const int blk = 2 * hh + hf;  // this warp's P block
+      if (hh > 0) {  // the previous half's MMA has read the P buffer
+        ok = ok && mbar_wait(smem_u32(&o_done[0]), phase_o, abort);
+        phase_o ^= 1;
         tc_fence_after();
+      }
+      if (blk < kblocks) {
+        uint8_t* pb = ps + hf * AX_P_KB;
+#pragma unroll 1
+        for (int c0 = blk * 64; c0 < blk * 64 + 64; c0 += 32) {
+          float sc[32];
+          const bool live = ok && warp_live && c0 < kend;
+          if (live) tmem_ld32(taddr + c0, sc);
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            const float p = (live && c0 + jj < nv) ? __expf(sc[jj] - m) : 0.f;
+            sum += p;
+            sc[jj] = p;
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            store_vec<8>(reinterpret_cast<__nv_bfloat16*>(pb + swz(rl, ((c0 & 63) >> 3) + u)), sc + 8 * u);
+        }
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      __syncthreads();  // P written; this half's scores (and so columns 0..31 after half 0) are consumed
+      if (tid == 0 && !*abort) {
+        tc_fence_after();
+        for (int kb2 = 2 * hh; kb2 < min(2 * hh + 2, kblocks); ++kb2) {
+          const uint32_t a0 = smem_u32(ps + (kb2 & 1) * AX_P_KB), b0 = smem_u32(vt + kb2 * AX_VT_KB);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) umma_i(tmem, smem_desc(a0 + j * 32), smem_desc(b0 + j * 32), AX_IDESC_O,
+                                             (kb2 | j) != 0);
+        }
+        umma_commit(smem_u32(&o_done[0]));
+      }
+    }
+    red_s[hf * 128 + rl] = sum;
+    __syncthreads();
+    ok = ok && (halves == 0 || mbar_wait(smem_u32(&o_done[0]), phase_o, abort));
+    if (halves > 0) phase_o ^= 1;
+    tc_fence_after();
+    if (hf == 0) {
+      float o[AX_D];
+#pragma unroll
+      for (int i = 0; i < AX_D; ++i) o[i] = 0.f;
+      if (ok && warp_live) {
+        const float tot = red_s[rl] + red_s[128 + rl];
+        const float inv = tot > 0.f ? 1.f / tot : 0.f;
         tmem_ld32(taddr, o);
 #pragma unroll
         for (int i = 0; i < AX_D; ++i) o[i] *= inv;
       }
-    }
-    if (row < length) {
-      if (row >= nv) {
+      if (row < length) {
+        if (row >= nv) {
 #pragma unroll
-        for (int i = 0; i < AX_D; ++i) o[i] = 0.f;
+          for (int i = 0; i < AX_D; ++i) o[i] = 0.f;
+        }
+        __nv_bfloat16* orow = ob + row * o_row;
+#pragma unroll
+        for (int i = 0; i < AX_D / 8; ++i) store_vec<8>(orow + 8 * i, o + 8 * i);
       }
-      __nv_bfloat16* orow = ob + row * o_row;
-#pragma unroll
-      for (int i = 0; i < AX_D / 8; ++i) store_vec<8>(orow + 8 * i, o + 8 * i);
     }
-  } else if (NP == 4 && hf == 1) {
-    // fewer than two live tiles: every warp worked on tile 0, so these warps
-    // write tile 1's rows, all past the valid length, as zeros
-    const int zrow = 128 + qd * 32 + lane;
-    if (zrow < length) {
-      float o[8] = {};
-      __nv_bfloat16* orow = ob + zrow * o_row;
+    tc_fence_before();
+    __syncthreads();  // O read before the next tile's S overwrites it
+    tc_fence_after();
+  }
+  // rows of tiles past the valid length (or every row without keys) read zero
+  for (int r = n_tiles * 128 + tid; r < length; r += AX_THREADS) {
+    float o[8] = {};
+    __nv_bfloat16* orow = ob + r * o_row;
 #pragma unroll
-      for (int i = 0; i < AX_D / 8; ++i) store_vec<8>(orow + 8 * i, o);
-    }
+    for (int i = 0; i < AX_D / 8; ++i) store_vec<8>(orow + 8 * i, o);
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(AX_TMEM_COLS) : "memory");
   }
 }
 
