@@ -234,7 +234,9 @@ def run_ours(args, rank, world, local_rank):
     reps = math.ceil(args.chunk / len(specs))
     host = mb.encoder.encode((specs * reps)[: args.chunk])
     fields = mb.evaluator.needed_fields(mb.MantisConfig(**ARCH))
-    host_pinned = host.pin_memory()
+    # the end-to-end input: the encoder's narrow layout (int32 index fields,
+    # widened on the device), in pinned memory
+    host_pinned = mb.encoder.encode((specs * reps)[: args.chunk], narrow=True, pin_memory=True)
 
     if world > 1:
         dist.init_process_group("nccl", device_id=device, timeout=__import__("datetime").timedelta(seconds=600))
@@ -312,7 +314,7 @@ def run_ours(args, rank, world, local_rank):
         t = torch.tensor([enc_box], dtype=torch.float64, device=device)
         dist.all_reduce(t)
         enc_box = float(t.item())
-    h2d = batch_bytes(host, fields) * n_chunks
+    h2d = batch_bytes(host_pinned, fields) * n_chunks
     d2h = 3 * host.n_cells * 4 * n_chunks
 
     # Roofline of the dominant native kernel (the larger total time inside the
@@ -333,7 +335,7 @@ def run_ours(args, rank, world, local_rank):
     p50 = None
     if rank == 0 and args.latency:
         lat_specs = make_specs(64, 40, 150, seed=77)
-        lat_batch = mb.encoder.encode(lat_specs, pin_memory=True)
+        lat_batch = mb.encoder.encode(lat_specs, pin_memory=True, narrow=True)
         times = []
         for i in range(3 + 20):
             torch.cuda.synchronize()

@@ -73,6 +73,7 @@ SIGNATURES = {
     "mb_encode_positions": "lpppppppip",
     "mb_encoding_sizes": "pp",
     "mb_encoding_fill": "ppi",
+    "mb_encoding_fill_narrow": "ppi",
     "mb_encoding_free": "p",
     "mb_encoder_table": "ipl",
     "mb_segment_argmax": "ppllpp",

@@ -581,7 +581,12 @@ int mb_encoding_sizes(const mb_encoding* e, int64_t* sizes) {
   return MB_OK;
 }
 
-int mb_encoding_fill(const mb_encoding* e, void* const* fields, int threads) {
+}  // extern "C"
+
+// The collated arrays with index fields of type T (int64, or int32 for
+// the narrow layout whose host-to-device copy is half the size).
+template <typename T>
+static int encoding_fill(const mb_encoding* e, void* const* fields, int threads) {
   using namespace mb::enc;
   MB_REQUIRE(e && fields, "encoding_fill: null pointer");
   for (int f = 0; f < MB_ENC_NFIELDS; ++f) MB_REQUIRE(fields[f] != nullptr, "encoding_fill: field %d is null", f);
@@ -594,7 +599,7 @@ int mb_encoding_fill(const mb_encoding* e, void* const* fields, int threads) {
   const auto& ao = e->off[5];
   const auto& dof = e->off[6];
   const int64_t max_t = e->max_t, max_w = e->max_w;
-  auto L = [&](int f) { return static_cast<int64_t*>(fields[f]); };
+  auto L = [&](int f) { return static_cast<T*>(fields[f]); };
   std::vector<int32_t> cls_hist((size_t)P * DEC_CLASSES, 0);
   parallel_for(P, threads, [&](int64_t i) {
     const Graph& g = e->graphs[i];
@@ -662,7 +667,7 @@ int mb_encoding_fill(const mb_encoding* e, void* const* fields, int threads) {
     // windows and rows both form one contiguous block. Class counts feed the
     // batch-wide class view below.
     const int64_t k0 = e->cov_off[i];
-    int64_t* cell_ptr = L(MB_ENC_RELAY_CELL_PTR);
+    T* cell_ptr = L(MB_ENC_RELAY_CELL_PTR);
     const size_t nd = g.dec.size();
     std::vector<int64_t> ecell(nd);
     int64_t k = k0 - 1;
@@ -670,7 +675,7 @@ int mb_encoding_fill(const mb_encoding* e, void* const* fields, int threads) {
       if (x == 0 || g.dec[x].cell != g.dec[x - 1].cell) cell_ptr[++k] = d0 + (int64_t)x;
       ecell[x] = k;
     }
-    int64_t* win_ptr = L(MB_ENC_RELAY_WIN_PTR) + w0;
+    T* win_ptr = L(MB_ENC_RELAY_WIN_PTR) + w0;
     std::vector<int64_t> at(g.n_w + 1, 0);
     for (size_t x = 0; x < nd; ++x) ++at[g.dec[x].window + 1];
     for (int64_t w = 0; w < g.n_w; ++w) at[w + 1] += at[w];
@@ -690,7 +695,7 @@ int mb_encoding_fill(const mb_encoding* e, void* const* fields, int threads) {
   const int64_t n_d = dof[P], n_w = wo[P];
   L(MB_ENC_RELAY_CELL_PTR)[e->n_covered] = n_d;
   L(MB_ENC_RELAY_WIN_PTR)[n_w] = n_d;
-  int64_t* cls_ptr = L(MB_ENC_RELAY_CLS_PTR);
+  T* cls_ptr = L(MB_ENC_RELAY_CLS_PTR);
   std::vector<int64_t> start((size_t)P * DEC_CLASSES);
   int64_t run = 0;
   for (int c = 0; c < DEC_CLASSES; ++c) {
@@ -711,6 +716,22 @@ int mb_encoding_fill(const mb_encoding* e, void* const* fields, int threads) {
     }
   });
   return MB_OK;
+}
+
+extern "C" {
+
+int mb_encoding_fill(const mb_encoding* e, void* const* fields, int threads) {
+  return encoding_fill<int64_t>(e, fields, threads);
+}
+
+int mb_encoding_fill_narrow(const mb_encoding* e, void* const* fields, int threads) {
+  MB_REQUIRE(e, "encoding_fill_narrow: null encoding");
+  int64_t sizes[11];
+  const int st = mb_encoding_sizes(e, sizes);
+  if (st != MB_OK) return st;
+  for (int i = 0; i < 11; ++i)
+    MB_REQUIRE(sizes[i] < INT32_MAX, "encoding_fill_narrow: %lld entries do not fit int32 indices", (long long)sizes[i]);
+  return encoding_fill<int32_t>(e, fields, threads);
 }
 
 int mb_encoding_free(mb_encoding* e) {

@@ -64,6 +64,10 @@ _FIELDS = (
 )
 
 
+# The fields the narrow layout writes as int32 (int64 in the batch contract).
+INT64_FIELDS = frozenset(name for name, dt, _ in _FIELDS if dt == torch.int64)
+
+
 def _flat(arrays, cols: int) -> tuple[np.ndarray, np.ndarray]:
     """Concatenated int64 rows and the (n + 1) row offsets."""
     parts = [np.asarray(a, dtype=np.int64).reshape(-1, cols) for a in arrays]
@@ -73,11 +77,14 @@ def _flat(arrays, cols: int) -> tuple[np.ndarray, np.ndarray]:
     return flat, off
 
 
-def encode(positions: Sequence, threads: int = 0, pin_memory: bool = False) -> Batch:
+def encode(positions: Sequence, threads: int = 0, pin_memory: bool = False, narrow: bool = False) -> Batch:
     """The collated batch of ``positions`` (objects with ``stone_qr``,
     ``stone_owner``, ``mover``, ``legal_qr``, ``moves_remaining``, such as
     ``engine.PositionSpec``). ``threads`` = 0 uses every hardware thread.
-    Raises ``ValueError`` for a position the builder refuses, naming it."""
+    ``narrow`` writes the int64 fields as int32 (the same values; half the
+    host memory and host-to-device bytes), which ``network_evaluate`` widens
+    on the device. Raises ``ValueError`` for a position the builder refuses,
+    naming it."""
     if len(positions) == 0:
         raise ValueError("empty batch")
     stone_qr, stone_off = _flat([p.stone_qr for p in positions], 2)
@@ -101,6 +108,8 @@ def encode(positions: Sequence, threads: int = 0, pin_memory: bool = False) -> B
         s = [int(v) for v in sizes]
         out = {}
         for name, dt, shape in _FIELDS:
+            if narrow and dt == torch.int64:
+                dt = torch.int32
             t = torch.empty(shape(s), dtype=dt, pin_memory=pin_memory)
             out[name] = t
         # torch.bool is one byte per flag, 0 or 1, as the encoder writes it;
@@ -109,7 +118,7 @@ def encode(positions: Sequence, threads: int = 0, pin_memory: bool = False) -> B
         addrs = (ctypes.c_void_p * len(_FIELDS))(
             *[out[name].data_ptr() if out[name].numel() else keep[i].data_ptr() for i, (name, _, _) in
               enumerate(_FIELDS)])
-        _lib.call("mb_encoding_fill", handle, addrs, int(threads))
+        _lib.call("mb_encoding_fill_narrow" if narrow else "mb_encoding_fill", handle, addrs, int(threads))
     finally:
         lib.mb_encoding_free(handle)
     return Batch(n_pos=s[_P], max_t=s[_MAXT], max_w=s[_MAXW], n_cells=s[_NC], **out)

@@ -30,6 +30,7 @@ import torch
 from . import ops, sharding
 from ._lib import check_device_error
 from .builder import RELAY_FIELDS, Batch, relay_tables
+from .encoder import INT64_FIELDS
 from .vocab import GLOBAL_ROWS, TERN_DEC_CLASSES
 from .config import MantisConfig
 
@@ -71,15 +72,27 @@ def needed_fields(cfg: MantisConfig) -> tuple[str, ...]:
     return tuple(f)
 
 
+def _device_dtype(k: str, v: torch.Tensor) -> torch.dtype:
+    """The batch contract's dtype of field ``k`` (int64 for an index field
+    of a narrow batch, whose host copy is int32)."""
+    return torch.int64 if (v.dtype == torch.int32 and k in INT64_FIELDS) else v.dtype
+
+
+def _widened(k: str, t: torch.Tensor) -> torch.Tensor:
+    """An index field copied from a narrow batch, widened on the device."""
+    return t.long() if (t.dtype == torch.int32 and k in INT64_FIELDS) else t
+
+
 def to_device(batch: Batch, device, fields) -> Batch:
-    """Copy only ``fields`` (others become empty placeholders on the device)."""
+    """Copy only ``fields`` (others become empty placeholders on the device);
+    int32 index fields of a narrow batch are widened to int64 there."""
     moved = {}
     for k, v in vars(batch).items():
         if isinstance(v, torch.Tensor):
             if k in fields:
-                moved[k] = v.to(device, non_blocking=True)
+                moved[k] = _widened(k, v.to(device, non_blocking=True))
             else:
-                moved[k] = torch.empty((0,) + tuple(v.shape[1:]), dtype=v.dtype, device=device)
+                moved[k] = torch.empty((0,) + tuple(v.shape[1:]), dtype=_device_dtype(k, v), device=device)
         else:
             moved[k] = v
     # cell_pos is long and needed; keep shapes consistent for size reads
@@ -156,7 +169,7 @@ def part_to_device(batch: Batch, fields, off, p0: int, p1: int, device) -> Batch
             moved[k] = v
             continue
         if k not in fields or k in _DERIVED_FIELDS:
-            moved[k] = torch.empty((0,) + tuple(v.shape[1:]), dtype=v.dtype, device=device)
+            moved[k] = torch.empty((0,) + tuple(v.shape[1:]), dtype=_device_dtype(k, v), device=device)
             continue
         rows, by = _SPLIT_FIELDS[k]
         if rows == "pos+1":
@@ -164,7 +177,7 @@ def part_to_device(batch: Batch, fields, off, p0: int, p1: int, device) -> Batch
         else:
             o = off[rows]
             a, z = int(o[p0]), int(o[p1])
-        t = v[a:z].to(device, non_blocking=True, copy=True)
+        t = _widened(k, v[a:z].to(device, non_blocking=True, copy=True))
         if by is not None and base[by]:
             t.sub_(base[by])
         moved[k] = t

@@ -571,6 +571,11 @@ int mb_encode_positions(int64_t n_pos, const int64_t* stone_off, const int64_t* 
                         const int64_t* moves_remaining, int threads, mb_encoding** out);
 int mb_encoding_sizes(const mb_encoding* encoding, int64_t* sizes);
 int mb_encoding_fill(const mb_encoding* encoding, void* const* fields, int threads);
+/* The same arrays with every int64 field written as int32 (the narrow
+ * layout: half the host memory and host-to-device bytes; the evaluator
+ * widens them on the device). Refuses a batch whose sizes do not fit int32.
+ * No counterpart in the reference. */
+int mb_encoding_fill_narrow(const mb_encoding* encoding, void* const* fields, int threads);
 int mb_encoding_free(mb_encoding* encoding);
 /* The encoder's vocabulary tables (0 window-pattern rank [729], 1 occupied-
  * slot class [729 x 6], 2 decoder class [729 x 6], 3 post-placement class

@@ -98,3 +98,21 @@ def test_pinned_output_matches():
         if isinstance(v, torch.Tensor):
             p = getattr(pinned, k)
             assert p.is_pinned() and torch.equal(p, v), k
+
+
+def test_narrow_layout_holds_the_same_values():
+    """encode(narrow=True) writes every int64 field as int32 with the same
+    values (the layout the evaluator widens on the device)."""
+    specs = mb.engine.random_positions(6, 5, 120, seed=41)
+    wide = mb.encoder.encode(specs, threads=2)
+    narrow = mb.encoder.encode(specs, threads=2, narrow=True)
+    for k, v in vars(wide).items():
+        if not isinstance(v, torch.Tensor):
+            assert getattr(narrow, k) == v, k
+            continue
+        n = getattr(narrow, k)
+        if k in mb.encoder.INT64_FIELDS:
+            assert v.dtype == torch.int64 and n.dtype == torch.int32, k
+            assert torch.equal(n.long(), v), k
+        else:
+            assert n.dtype == v.dtype and torch.equal(n, v), k

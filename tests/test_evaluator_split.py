@@ -87,3 +87,24 @@ def test_range_points():
     pts = E.range_points(100, 1100, 448)
     assert pts[0] == 100 and pts[-1] == 1100 and all(a < b for a, b in zip(pts, pts[1:]))
     assert max(b - a for a, b in zip(pts, pts[1:])) <= 448
+
+
+def test_narrow_batch_runs_equal_the_wide_ones():
+    """Runs cut from a narrow (int32) batch are the wide batch's runs: the
+    index fields are widened to int64 on the way to the device."""
+    specs = mb.engine.random_positions(9, 20, 120, seed=11)
+    wide = mb.encoder.encode(specs, threads=1)
+    narrow = mb.encoder.encode(specs, threads=1, narrow=True)
+    for knobs in (dict(cell_latents=True, cell_nodes=True), dict()):
+        cfg = mb.MantisConfig(h=32, blocks=1, heads=2, **knobs)
+        fields = E.needed_fields(cfg)
+        ow, on = E._offsets(wide, fields), E._offsets(narrow, fields)
+        for a, b in ((0, 4), (4, 9)):
+            rw = E.part_to_device(wide, fields, ow, a, b, "cpu")
+            rn = E.part_to_device(narrow, fields, on, a, b, "cpu")
+            for f in fields:
+                assert getattr(rn, f).dtype == getattr(rw, f).dtype, f
+                assert torch.equal(getattr(rn, f), getattr(rw, f)), f
+        dw, dn = E.to_device(wide, "cpu", fields), E.to_device(narrow, "cpu", fields)
+        for f in fields:
+            assert torch.equal(getattr(dn, f), getattr(dw, f)), f

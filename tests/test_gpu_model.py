@@ -150,3 +150,19 @@ def test_pipelined_evaluator_equals_one_shot(autocast):
     got = runs(batch)
     for a, b in zip(got, want):
         torch.testing.assert_close(a, b, rtol=0, atol=1e-5 if not autocast else 1e-2)
+
+
+def test_narrow_batch_evaluates_identically():
+    """A narrow (int32) batch from the encoder evaluates to exactly the wide
+    batch's outputs: its index fields are widened on the device, one shot and
+    pipelined."""
+    cfg = mb.MantisConfig(h=64, blocks=2, heads=4, cell_latents=True, cell_nodes=True)
+    torch.manual_seed(5)
+    net = mb.MantisNet(cfg).to(DEV).eval()
+    specs = mb.engine.random_positions(11, 20, 160, seed=21)
+    wide = mb.encoder.encode(specs)
+    narrow = mb.encoder.encode(specs, narrow=True)
+    for part in (0, 3):
+        ev = mb.network_evaluate(net, mb.evaluator.EvaluatorConfig(device=DEV, autocast=True, part_positions=part))
+        for a, b in zip(ev(narrow), ev(wide)):
+            assert torch.equal(a, b)
