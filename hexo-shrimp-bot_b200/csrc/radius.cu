@@ -237,16 +237,18 @@ __global__ void __launch_bounds__(kThreads, 2) radius_read_kernel(
     int64_t n_cls, const __nv_bfloat16* __restrict__ vcls, int64_t ld_vcls, const int64_t* __restrict__ seg_ptr,
     const int32_t* __restrict__ packed, const int64_t* __restrict__ skip_ptr, const int64_t* __restrict__ q_off,
     const int64_t* __restrict__ s_off, const int64_t* __restrict__ order, const int4* __restrict__ slots,
-    int stage_rows, TO* __restrict__ out, int64_t ldo, float scale) {
+    int stage_rows, int split, TO* __restrict__ out, int64_t ldo, float scale) {
   extern __shared__ __align__(16) unsigned char smem[];
-  const int grp = blockIdx.x;
+  // `split` CTAs share a group's rows (small batches: more CTAs than groups)
+  const int grp = blockIdx.x / split, part = blockIdx.x % split;
   const int cb = blockIdx.y * kCols;
   const int64_t q0 = q_off[grp], q1 = q_off[grp + 1], s0 = s_off[grp], s1 = s_off[grp + 1];
   if (q0 < 0 || q1 < q0 || q1 > n_q || s0 < 0 || s1 < s0 || s1 > n_src) {
-    if (threadIdx.x == 0) report(ERR_RUN_BOUND);
+    if (threadIdx.x == 0 && part == 0) report(ERR_RUN_BOUND);
     return;
   }
-  if (q1 == q0) return;
+  const int64_t qa = q0 + (q1 - q0) * part / split, qb = q0 + (q1 - q0) * (part + 1) / split;  // this CTA's slots
+  if (qb == qa) return;
   const int64_t ns = s1 - s0;
   const bool staged = ns <= stage_rows;
 
@@ -306,10 +308,10 @@ __global__ void __launch_bounds__(kThreads, 2) radius_read_kernel(
     }
   };
   int4 next_info = make_int4(0, 0, 0, 0);
-  if (slots && q0 + warp * kCellsPerWarp + ci < q1) next_info = __ldg(slots + q0 + warp * kCellsPerWarp + ci);
-  for (int64_t base = q0 + warp * kCellsPerWarp; base < q1; base += kStep) {
+  if (slots && qa + warp * kCellsPerWarp + ci < qb) next_info = __ldg(slots + qa + warp * kCellsPerWarp + ci);
+  for (int64_t base = qa + warp * kCellsPerWarp; base < qb; base += kStep) {
     const int64_t slot = base + ci;
-    const bool rv = slot < q1;
+    const bool rv = slot < qb;
     int64_t row = 0, beg = 0;
     int n = 0;
     if (rv) {
@@ -321,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 2) radius_read_kernel(
         cell_of(slot, row, beg, n);
       }
     }
-    if (slots && slot + kStep < q1) next_info = __ldg(slots + slot + kStep);
+    if (slots && slot + kStep < qb) next_info = __ldg(slots + slot + kStep);
     const bool own = rv && row >= q0 && row < q1;  // the order must permute the position's own rows
     if (rv && !own) report(ERR_INDEX);
     if (!own) n = 0;
@@ -491,7 +493,16 @@ int mb_radius_read(const void* q, int64_t ldq, const void* k, const void* v, int
   const int64_t rows = std::min<int64_t>(stage_rows, (limit - fixed) / radius::kKvRowBytes);
   const int smem = fixed + (int)rows * radius::kKvRowBytes;
   const float scale = 1.f / sqrtf((float)head_dim);
-  dim3 grid((unsigned)n_groups, (unsigned)(H / radius::kCols));
+  // Enough CTAs for two per SM: a small batch's groups are split over
+  // several CTAs (each at least one 128-row step on average).
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t col_blocks = H / radius::kCols;
+  const int64_t want = (2 * (int64_t)sms + n_groups * col_blocks - 1) / (n_groups * col_blocks);
+  const int64_t most = std::max<int64_t>(1, n_q / (n_groups * radius::kThreads / radius::kHeads));
+  const int split = (int)std::max<int64_t>(1, std::min<int64_t>({want, most, 64}));
+  MB_REQUIRE(n_groups * split <= INT32_MAX, "radius_read: too many groups");
+  dim3 grid((unsigned)(n_groups * split), (unsigned)col_blocks);
   int rc = MB_OK;
   MB_DISPATCH_T(out_dtype, TO, [&] {
     auto kern = vcls ? radius::radius_read_kernel<TO, true> : radius::radius_read_kernel<TO, false>;
@@ -502,7 +513,7 @@ int mb_radius_read(const void* q, int64_t ldq, const void* k, const void* v, int
     kern<<<grid, radius::kThreads, smem, as_stream(stream)>>>(
         (const __nv_bfloat16*)q, ldq, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, ldkv, n_q, n_src, bias, n_cls,
         (const __nv_bfloat16*)vcls, H, seg_ptr, packed, skip_ptr, q_off, s_off, order,
-        reinterpret_cast<const int4*>(slots), (int)rows, (TO*)out, ldo, scale);
+        reinterpret_cast<const int4*>(slots), (int)rows, split, (TO*)out, ldo, scale);
   });
   if (rc != MB_OK) return rc;
   return launch_status("radius_read");
