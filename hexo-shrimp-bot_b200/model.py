@@ -948,7 +948,18 @@ class Engine:
         # (N_c, 2H): [p-head | q-head] = [cells | acts] @ W_dec^T + sum of the
         # cell's decoder class rows
         extra = ops.run_reduce(self.e_pq, T.dec_class, T.cell_ptr, n_c)
-        base = self.linear(buf, self.dec_pq, add=extra)
+        lin = self.dec_pq
+        if self._tc(lin, buf) and lin.k == 512 and lin.n == 2 * h == 512:
+            # K = 512 with 512 outputs: as two 256-output launches on the
+            # weight-stationary plan (each image half is an image of its own)
+            base = torch.empty(n_c, 2 * h, dtype=cd, device=buf.device)
+            half = lin.img.view(-1).shape[0] // 2
+            for j in range(2):
+                img = lin.img.view(-1)[j * half:(j + 1) * half].view(h, lin.k)
+                ops.gemm_rows(buf, img, bias=None if lin.b is None else lin.b[j * h:(j + 1) * h],
+                              add=extra[:, j * h:(j + 1) * h], out=base[:, j * h:(j + 1) * h])
+        else:
+            base = self.linear(buf, lin, add=extra)
         gh = self.linear(g.to(cd), self.lin_b_pq)  # (P, 2 * P_H)
         ph = cfg.policy_hidden
         outs = []
