@@ -40,7 +40,8 @@ constexpr int AX_VT_OFF = AX_QK_OFF + AX_QK_BYTES;
 constexpr int AX_P_OFF = AX_VT_OFF + AX_VT_BYTES;
 constexpr int AX_BIAS_OFF = AX_P_OFF + AX_P_BYTES;
 constexpr int AX_COORD_OFF = AX_BIAS_OFF + 4400;  // 33*33 floats, rounded up
-constexpr int AX_RED_OFF = AX_COORD_OFF + AX_L * 8;  // per-row half maxima / sums
+constexpr int AX_KPK_OFF = AX_COORD_OFF + AX_L * 8;   // packed key offsets (int32 per key)
+constexpr int AX_RED_OFF = AX_KPK_OFF + AX_L * 4;     // per-row half maxima / sums
 constexpr int AX_BAR_OFF = AX_RED_OFF + 2 * 2 * 128 * 4;
 constexpr int AX_SMEM = AX_BAR_OFF + 64 + 1024;   // + alignment slack
 static_assert(2 * AX_SMEM <= 232448, "axial attention must fit two CTAs per SM");
@@ -50,6 +51,21 @@ constexpr uint32_t idesc_f16(int m, int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 constexpr uint32_t AX_IDESC_O = idesc_f16(128, AX_D);
+// Packed offsets: a key's coordinates relative to the position's first token,
+// plus AX_OFF, in the two 16-bit halves of one word (q high, r low). With
+// every coordinate within AX_NEAR of the first token's, key word - query word
+// holds (dq + AX_OFF, dr + AX_OFF) in its halves with no borrow between them,
+// and both halves are clamped at once with 16-bit SIMD min / max.
+constexpr int AX_OFF = 16384, AX_NEAR = 8192;
+constexpr unsigned AX_LO2 = (unsigned)(AX_OFF - 16) * 0x10001u, AX_HI2 = (unsigned)(AX_OFF + 16) * 0x10001u;
+constexpr int AX_CIDX = (AX_OFF - 16) * (AX_SPAN + 1);  // the clamped halves' index at (-16, -16)
+constexpr float AX_LOG2E = 1.4426950408889634f;
+
+__device__ __forceinline__ float ax_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __device__ __forceinline__ void umma_i(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                        uint32_t accumulate) {
@@ -76,6 +92,7 @@ __global__ void __launch_bounds__(AX_THREADS, 2) axial_attention_kernel(
   uint8_t* ps = smem + AX_P_OFF;
   float* bias_s = reinterpret_cast<float*>(smem + AX_BIAS_OFF);
   int2* kc = reinterpret_cast<int2*>(smem + AX_COORD_OFF);
+  int* kpk = reinterpret_cast<int*>(smem + AX_KPK_OFF);
   float* red = reinterpret_cast<float*>(smem + AX_RED_OFF);  // [max | sum][half][128 rows]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + AX_BAR_OFF);
   uint64_t* s_done = bars;       // one phase per query tile
@@ -137,11 +154,25 @@ __global__ void __launch_bounds__(AX_THREADS, 2) axial_attention_kernel(
     for (int w = 0; w < 8; ++w)
       *reinterpret_cast<__nv_bfloat16*>(vt + blk * AX_VT_KB + swz(8 * c + w, jj >> 3) + (jj & 7) * 2) = e[w];
   }
-  for (int idx = tid; idx < AX_SPAN * AX_SPAN; idx += AX_THREADS) bias_s[idx] = __ldg(bias + (int64_t)idx * heads + h);
-  if (tid < AX_L) kc[tid] = tid < length ? make_int2(__ldg(cb + 2 * tid), __ldg(cb + 2 * tid + 1)) : make_int2(0, 0);
+  // scores are kept in log2 units: the bias table is stored times log2(e)
+  for (int idx = tid; idx < AX_SPAN * AX_SPAN; idx += AX_THREADS)
+    bias_s[idx] = __ldg(bias + (int64_t)idx * heads + h) * AX_LOG2E;
+  const int bx = length > 0 ? __ldg(cb) : 0, by = length > 0 ? __ldg(cb + 1) : 0;
+  bool near = true;
+  if (tid < AX_L) {
+    const int2 c = tid < length ? make_int2(__ldg(cb + 2 * tid), __ldg(cb + 2 * tid + 1)) : make_int2(0, 0);
+    kc[tid] = c;
+    const int64_t ox = (int64_t)c.x - bx, oy = (int64_t)c.y - by;
+    const bool in = tid < nv;  // keys (and the queries that are written) are the first nv tokens
+    near = !in || (ox > -AX_NEAR && ox < AX_NEAR && oy > -AX_NEAR && oy < AX_NEAR);
+    // keys past the valid length sit at the first token (in range; masked later)
+    kpk[tid] = in && near ? (int)((((uint32_t)(ox + AX_OFF)) << 16) | (uint32_t)(oy + AX_OFF))
+                          : (int)(((uint32_t)AX_OFF << 16) | (uint32_t)AX_OFF);
+  }
   fence_proxy_async();  // generic-proxy shared stores -> visible to the tensor cores
   tc_fence_before();
-  __syncthreads();
+  // packed offsets are used when every valid token is near the first one
+  const bool packed = __syncthreads_and(near) != 0;
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -151,7 +182,7 @@ __global__ void __launch_bounds__(AX_THREADS, 2) axial_attention_kernel(
   // rounded to a 64-key block.
   const int qd = warp & 3, hf = warp >> 2;
   const int rl = qd * 32 + lane;
-  const float scale = 0.17677669529663687f;  // 1 / sqrt(32)
+  const float scale = 0.17677669529663687f * AX_LOG2E;  // 1 / sqrt(32), in log2 units
   const int kend = min(AX_L, (nv + 31) & ~31);
   const int npad = (nv + 15) & ~15;
   const int kblocks = (nv + 63) >> 6;
@@ -178,19 +209,42 @@ __global__ void __launch_bounds__(AX_THREADS, 2) axial_attention_kernel(
     tc_fence_after();
     if (ok && warp_live) {
       const int2 qc = row < length ? make_int2(__ldg(cb + 2 * row), __ldg(cb + 2 * row + 1)) : make_int2(0, 0);
+      // the query's packed offsets (rows past the valid length are written as
+      // zeros: they take the first token's, which keeps the index in range)
+      const int qp = row < nv ? (int)((uint32_t)(qc.x - bx) << 16) + (qc.y - by) : 0;
       const int c_lo = hf * 128, c_hi = min(c_lo + 128, kend);
 #pragma unroll 1
       for (int c0 = c_lo; c0 < c_hi; c0 += 32) {
         float sc[32];
         tmem_ld32(taddr + c0, sc);
+        if (packed) {
+          const int4* k4p = reinterpret_cast<const int4*>(kpk + c0);
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          const int j = c0 + jj;
-          const int2 c = kc[j];
-          const int dq = min(max(c.x - qc.x, -16), 16) + 16, dr = min(max(c.y - qc.y, -16), 16) + 16;
-          sc[jj] = j < nv ? sc[jj] * scale + bias_s[dq * AX_SPAN + dr] : -INFINITY;
-          m = fmaxf(m, sc[jj]);
+          for (int u = 0; u < 8; ++u) {
+            const int4 k4 = k4p[u];
+            const int kk[4] = {k4.x, k4.y, k4.z, k4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const unsigned d = __vmins2(__vmaxs2((unsigned)(kk[e] - qp), AX_LO2), AX_HI2);
+              const int idx = (int)(d >> 16) * AX_SPAN + (int)(d & 0xffffu) - AX_CIDX;
+              sc[4 * u + e] = fmaf(sc[4 * u + e], scale, bias_s[idx]);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            const int2 c = kc[c0 + jj];
+            const int dq = min(max(c.x - qc.x, -16), 16) + 16, dr = min(max(c.y - qc.y, -16), 16) + 16;
+            sc[jj] = fmaf(sc[jj], scale, bias_s[dq * AX_SPAN + dr]);
+          }
         }
+        if (c0 + 32 > nv) {  // the last chunk: keys past the valid length
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj)
+            if (c0 + jj >= nv) sc[jj] = -INFINITY;
+        }
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) m = fmaxf(m, sc[jj]);
         tmem_st32(taddr + c0, sc);
       }
       tmem_st_wait();
@@ -216,12 +270,18 @@ __global__ void __launch_bounds__(AX_THREADS, 2) axial_attention_kernel(
         for (int c0 = blk * 64; c0 < blk * 64 + 64; c0 += 32) {
           float sc[32];
           const bool live = ok && warp_live && c0 < kend;
-          if (live) tmem_ld32(taddr + c0, sc);
+          if (live) {
+            tmem_ld32(taddr + c0, sc);
+            // masked keys hold -inf and read 0
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const float p = (live && c0 + jj < nv) ? __expf(sc[jj] - m) : 0.f;
-            sum += p;
-            sc[jj] = p;
+            for (int jj = 0; jj < 32; ++jj) {
+              const float p = ax_exp2(sc[jj] - m);
+              sum += p;
+              sc[jj] = p;
+            }
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) sc[jj] = 0.f;
           }
 #pragma unroll
           for (int u = 0; u < 4; ++u)

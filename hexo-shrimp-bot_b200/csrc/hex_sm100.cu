@@ -38,7 +38,9 @@ constexpr int HX_WIN_OFF = 0;
 constexpr int HX_A_OFF = HX_WIN_OFF + HX_NSEG * HX_SEG_BYTES;
 constexpr int HX_W_OFF = HX_A_OFF + 2 * A_KB_BYTES;
 constexpr int HX_BAR_OFF = HX_W_OFF + 2 * W_KB_BYTES;
-constexpr int HX_SMEM = HX_BAR_OFF + 256 + 1024;  // + alignment slack
+constexpr int HX_BIAS_OFF = HX_BAR_OFF + 256;      // the bias (256 fp32)
+constexpr int HX_ZERO_OFF = HX_BIAS_OFF + KDIM * 4;  // one zero row: absent neighbours read it
+constexpr int HX_SMEM = HX_ZERO_OFF + KDIM * 2 + 1024;  // + alignment slack
 static_assert(HX_SMEM <= 232448, "hex window plan exceeds 227 KB");
 static_assert(BN == KDIM && BM == 2 * HX_SEG, "the window plan assumes 128-row tiles of 256 columns");
 
@@ -52,6 +54,7 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hex_window_kernel(
   uint8_t* a_smem = smem + HX_A_OFF;
   uint8_t* w_smem = smem + HX_W_OFF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + HX_BAR_OFF);
+  float* bias_s = reinterpret_cast<float*>(smem + HX_BIAS_OFF);
   uint64_t* seg_full = bars;        // [4]
   uint64_t* mean_done = bars + 4;   // [1]
   uint64_t* a_full = bars + 5;      // [2]
@@ -88,6 +91,10 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hex_window_kernel(
                  "r"(TMEM_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (threadIdx.x < KDIM) {
+    bias_s[threadIdx.x] = bias ? bias[threadIdx.x] : 0.f;
+    reinterpret_cast<__nv_bfloat16*>(smem + HX_ZERO_OFF)[threadIdx.x] = __float2bfloat16(0.f);
   }
   tc_fence_before();
   __syncthreads();
@@ -159,11 +166,64 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hex_window_kernel(
     }
   } else if (warp <= HX_PRODUCERS) {
     // ------------------------------------------------- mean A tile (K-blocks)
+    // A thread's rows of a tile are r = 4 g + sub for g = pw + 7 k. Their
+    // neighbour indices are loaded a tile ahead and turned once per tile into
+    // codes: >= 0 the byte offset of the neighbour row in shared memory (an
+    // absent slot reads the zero row), <= -2 a row outside the window (-2 -
+    // code, read from global memory). Unless some row of the warp has such a
+    // neighbour, the four K-blocks of the tile read six shared-memory rows per
+    // row with no branch.
     const int pw = warp - 1;
     const int sub = lane >> 3, c8 = lane & 7;  // 4 rows per warp step, 8 lanes (16 B each) per row
+    constexpr int GROUPS = (BM / 4 + HX_PRODUCERS - 1) / HX_PRODUCERS;
+    int raw[GROUPS][HEX_SLOTS];
+    auto fetch = [&](int64_t t) {
+#pragma unroll
+      for (int k = 0; k < GROUPS; ++k) {
+        const int g = pw + HX_PRODUCERS * k;
+        const int64_t row = t * BM + g * 4 + sub;
+        const bool live = g < BM / 4 && row < n;
+#pragma unroll
+        for (int j = 0; j < HEX_SLOTS; ++j) raw[k][j] = live ? __ldg(nbr + row * HEX_SLOTS + j) : -1;
+      }
+    };
+    if (my_tiles > 0) fetch(t0);
     bool ok = true;
     for (int64_t i = 0; ok && i < my_tiles && !*abort; ++i) {
       const int64_t t = t0 + i, r0 = t * BM;
+      const int64_t wbase = r0 - HX_SEG;  // first row of the window (segment 2t - 1)
+      int code[GROUPS][HEX_SLOTS];
+      float inv[GROUPS];
+#pragma unroll
+      for (int k = 0; k < GROUPS; ++k) {
+        int present = 0;
+#pragma unroll
+        for (int j = 0; j < HEX_SLOTS; ++j) {
+          const int64_t nb = raw[k][j];
+          int c = HX_ZERO_OFF;
+          if (nb >= n) {
+            report(ERR_INDEX);
+          } else if (nb >= 0) {
+            const int64_t wr = nb - wbase;
+            if (wr >= 0 && wr < HX_NSEG * HX_SEG) {
+              const int slot = (int)((2 * t - 1 + wr / HX_SEG - s0) & (HX_NSEG - 1));
+              c = slot * HX_SEG_BYTES + (int)(nb & (HX_SEG - 1)) * (KDIM * 2);
+            } else {
+              c = -2 - (int)nb;
+            }
+            ++present;
+          }
+          code[k][j] = c;
+        }
+        inv[k] = present ? 1.f / (float)present : 0.f;
+      }
+      bool far_row = false;
+#pragma unroll
+      for (int k = 0; k < GROUPS; ++k)
+#pragma unroll
+        for (int j = 0; j < HEX_SLOTS; ++j) far_row |= code[k][j] < 0;
+      const bool far = __any_sync(0xffffffffu, far_row);
+      if (i + 1 < my_tiles) fetch(t + 1);  // in flight during this tile
       // this tile's new segments (all four for the first tile)
       for (int64_t s = (i == 0 ? s0 : 2 * t + 1); s <= 2 * t + 2; ++s) {
         const int slot = (int)((s - s0) & (HX_NSEG - 1));
@@ -173,7 +233,6 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hex_window_kernel(
         }
       }
       if (!ok) break;
-      const int64_t wbase = r0 - HX_SEG;  // first row of the window
       for (int kb = 0; ok && kb < KDIM / BK; ++kb) {
         const int64_t q = i * (KDIM / BK) + kb;
         const uint32_t s = q & 1, ph = (q >> 1) & 1;
@@ -182,44 +241,39 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hex_window_kernel(
           break;
         }
         uint8_t* abuf = a_smem + s * A_KB_BYTES;
-        for (int g = pw; g < BM / 4; g += HX_PRODUCERS) {
+        const uint8_t* wk = win + kb * 128 + c8 * 16;
+#pragma unroll
+        for (int k = 0; k < GROUPS; ++k) {
+          const int g = pw + HX_PRODUCERS * k;
+          if (g >= BM / 4) break;
           const int r = g * 4 + sub;
-          const int64_t row = r0 + r;
           float acc[8] = {};
-          int present = 0;
-          if (row < n) {
+          uint4 raw16[HEX_SLOTS];
+          if (!far) {
+#pragma unroll
+            for (int j = 0; j < HEX_SLOTS; ++j) raw16[j] = *reinterpret_cast<const uint4*>(wk + code[k][j]);
+          } else {
 #pragma unroll
             for (int j = 0; j < HEX_SLOTS; ++j) {
-              const int64_t nb = __ldg(nbr + row * HEX_SLOTS + j);
-              if (nb < 0) continue;
-              if (nb >= n) {
-                report(ERR_INDEX);
-                continue;
-              }
-              const int64_t wr = nb - wbase;
-              uint4 raw;
-              if (wr >= 0 && wr < HX_NSEG * HX_SEG) {
-                const int slot = (int)(((wbase / HX_SEG + wr / HX_SEG) - s0) & (HX_NSEG - 1));
-                raw = *reinterpret_cast<const uint4*>(win + slot * HX_SEG_BYTES + (nb & (HX_SEG - 1)) * (KDIM * 2) +
-                                                      kb * 128 + c8 * 16);
-              } else {
-                raw = __ldg(reinterpret_cast<const uint4*>(x + nb * KDIM + kb * BK) + c8);
-              }
-              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float2 f = __bfloat1622float2(h[e]);
-                acc[2 * e] += f.x;
-                acc[2 * e + 1] += f.y;
-              }
-              ++present;
+              const int c = code[k][j];
+              raw16[j] = c >= 0 ? *reinterpret_cast<const uint4*>(wk + c)
+                                : __ldg(reinterpret_cast<const uint4*>(x + (int64_t)(-2 - c) * KDIM + kb * BK) + c8);
             }
           }
-          const float inv = present ? 1.f / (float)present : 0.f;
+#pragma unroll
+          for (int j = 0; j < HEX_SLOTS; ++j) {
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw16[j]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __bfloat1622float2(h[e]);
+              acc[2 * e] += f.x;
+              acc[2 * e + 1] += f.y;
+            }
+          }
           uint4 w4;
           __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w4);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) hw[e] = __floats2bfloat162_rn(acc[2 * e] * inv, acc[2 * e + 1] * inv);
+          for (int e = 0; e < 4; ++e) hw[e] = __floats2bfloat162_rn(acc[2 * e] * inv[k], acc[2 * e + 1] * inv[k]);
           *reinterpret_cast<uint4*>(abuf + r * 128 + ((c8 ^ (r & 7)) << 4)) = w4;
         }
         fence_proxy_async();  // generic-proxy stores -> visible to the tensor cores
@@ -237,24 +291,35 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hex_window_kernel(
       if (!mbar_wait(smem_u32(&t_full[tb]), tph, abort)) break;
       tc_fence_after();
       const int64_t row = (t0 + i) * BM + qd * 32 + lane;
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      const bool live = row < n;
+      // x[r] is read back through L2 (the window slots may be refilled by
+      // now), each 32-column chunk's 64 bytes requested two chunks ahead
+      const uint4* xr = reinterpret_cast<const uint4*>(x + (live ? row : 0) * KDIM);
+      constexpr int CH = BN / 32;
+      uint4 xq[3][4];
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) xq[c][e] = live ? __ldg(xr + 4 * c + e) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        if (c + 2 < CH) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) xq[(c + 2) % 3][e] = live ? __ldg(xr + 4 * (c + 2) + e) : make_uint4(0, 0, 0, 0);
+        }
+        const int c0 = 32 * c;
         float v[32];
         tmem_ld32(tmem_base + ((uint32_t)(qd * 32) << 16) + tb * BN + c0, v);
-        if (bias) {
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float4 bb = __ldg(reinterpret_cast<const float4*>(bias + c0) + e);
-            v[4 * e] += bb.x; v[4 * e + 1] += bb.y; v[4 * e + 2] += bb.z; v[4 * e + 3] += bb.w;
-          }
+        for (int e = 0; e < 8; ++e) {
+          const float4 bb = reinterpret_cast<const float4*>(bias_s + c0)[e];
+          v[4 * e] += bb.x; v[4 * e + 1] += bb.y; v[4 * e + 2] += bb.z; v[4 * e + 3] += bb.w;
         }
-        if (row < n) {
-          const uint4* xr = reinterpret_cast<const uint4*>(x + row * KDIM + c0);
+        if (live) {
           uint4* orow = reinterpret_cast<uint4*>(out + row * ldo + c0);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const uint4 xx = __ldg(xr + e);
-            const __nv_bfloat162* hx = reinterpret_cast<const __nv_bfloat162*>(&xx);
+            const __nv_bfloat162* hx = reinterpret_cast<const __nv_bfloat162*>(&xq[c % 3][e]);
             uint4 w4;
             __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w4);
 #pragma unroll

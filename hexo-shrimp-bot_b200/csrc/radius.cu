@@ -203,10 +203,15 @@ __device__ __forceinline__ float dot32(const uint64_t (&q2)[16], const uint4 (&k
 
 // One edge of a (cell, head): the online-softmax update with the score and
 // the edge's value row (+ class value row), both 4 x 8 bf16.
+constexpr float kSlack = 8.f;
+
 template <bool HAS_VCLS>
 __device__ __forceinline__ void edge_update(float score, const uint4 (&vr)[4], const uint4 (&cr)[4], float& m,
                                             float& l, uint64_t (&acc)[16]) {
-  if (score > m) {  // a new running maximum: rescale what is accumulated
+  // The reference point m is raised only when a score passes it by more than
+  // kSlack (or on the first edge, m = -inf), so the rescale runs about once
+  // per run; weights exp(score - m) stay below exp(kSlack), well inside fp32.
+  if (score > m + kSlack) {
     const float corr = __expf(m - score);  // m = -inf before the first edge: exp(-inf) = 0
     l *= corr;
     const uint64_t c2 = pack2(corr, corr);
