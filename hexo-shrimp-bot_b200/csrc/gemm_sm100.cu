@@ -983,11 +983,13 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const __grid_consta
         if (lane == 0) mbar_arrive(smem_u32(&t_empty[tb]));
       } else {
       const int cols = nb == nbn - 1 ? p.n_last : L::BNB;
-      const int cend = (half + 1) * (BN / PARTS) < cols ? (half + 1) * (BN / PARTS) : cols;
+      // column ranges of BNB / PARTS (a 128-column block gives each warp 64)
+      constexpr int SPAN = L::BNB / PARTS;
+      const int cend = (half + 1) * SPAN < cols ? (half + 1) * SPAN : cols;
       const int nr = (int)(p.m - row0 < 32 ? (p.m - row0 < 0 ? 0 : p.m - row0) : 32);  // live rows of the warp
       uint4* sb = reinterpret_cast<uint4*>(smem + L::OUT_OFF + ew * OUT_BOX_BYTES);
 #pragma unroll 1
-      for (int c0 = half * (BN / PARTS); c0 < cend; c0 += 32) {
+      for (int c0 = half * SPAN; c0 < cend; c0 += 32) {
         float v[32];
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + tb * BN + c0, v);
         const int oc = nb * L::BNB + c0;  // output column
