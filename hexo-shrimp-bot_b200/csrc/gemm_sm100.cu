@@ -150,6 +150,18 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
+// Tensor-map store of one 32-column x 32-row bf16 box (64-byte swizzle) from
+// shared memory; rows past the tensor's end are not written.
+__device__ __forceinline__ void tma_store_2d(const void* tmap, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(x), "r"(y), "r"(src)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -216,6 +228,7 @@ __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.
 
 struct alignas(64) Params {
   CUtensorMap tmap_x;   // PRO_TMA: the (m, K) bf16 input rows, 64 x 128 boxes, 128-byte swizzle
+  CUtensorMap tmap_out; // EPI_STORE: the (m, N) bf16 output rows, 32 x 32 boxes, 64-byte swizzle
   const void* x;        // prologue input rows (fp32 for LN, bf16 for COPY)
   int64_t ldx;
   const float* gamma;   // LN
@@ -315,7 +328,11 @@ struct Plan {
   static constexpr int OUT_OFF = E_OFF + (RESID ? EPILOGUE * RING * BOX_FLOATS * 4 : 0);
   // bias and the LayerNorms' gamma / beta, copied once per CTA (uniform
   // reads in the epilogue, kept out of the busy L1 miss path)
-  static constexpr int PAR_OFF = OUT_OFF + (OUT_BOXES ? EPILOGUE * OUT_BOX_BYTES : 0);
+  // EPI_STORE writes its boxes with tensor-map stores: two boxes per warp
+  // where they fit, so a box is refilled while the other one's store reads it
+  static constexpr int OUT_NBOX =
+      (EPI == EPI_STORE && OUT_OFF + 2 * EPILOGUE * OUT_BOX_BYTES + BAR_BYTES + 1024 <= 232448) ? 2 : 1;
+  static constexpr int PAR_OFF = OUT_OFF + (OUT_BOXES ? EPILOGUE * OUT_BOX_BYTES * OUT_NBOX : 0);
   static constexpr int RED_OFF = PAR_OFF + (RESID ? (1 + 2 * MAX_LN) * BN * 4 : 0);
   static constexpr int BAR_OFF = RED_OFF + (EPI == EPI_RESID_LN ? 4 * 64 * 4 : 0) +
                                  (EPI == EPI_HEAD ? 4 * MAX_HEAD_OUT * 32 * 4 : 0);
@@ -754,6 +771,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const __grid_consta
     const int q = warp & 3;           // TMEM lane quadrant this warp may access
     constexpr int PARTS = L::EPI_WARPS / 4;  // column ranges per quadrant
     const int half = ew >> 2;                // this warp's column range
+    uint32_t out_seq = 0;                    // EPI_STORE: boxes this warp has handed to the tensor store
     // Residual variants: the warp's residual rows arrive by cp.async in
     // boxes of 32 rows x 32 columns (one box per 32-column chunk of its
     // column range, the chunks of all its tiles in one sequence). A box is
@@ -1027,6 +1045,33 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const __grid_consta
               }
             }
           }
+          if constexpr (EPI == EPI_STORE) {
+            // Into one of the warp's boxes in the tensor map's 64-byte swizzle
+            // (16-byte piece j of row r at j ^ ((r >> 1) & 3): conflict-free
+            // row-wise writes), then one tensor-map store of the 32 x 32 box
+            // by lane 0. The box's previous store must have read it first.
+            const uint32_t bi = out_seq % L::OUT_NBOX;
+            uint4* ob = reinterpret_cast<uint4*>(smem + L::OUT_OFF + (bi * EPILOGUE + ew) * OUT_BOX_BYTES);
+            if (lane == 0) bulk_wait_read<L::OUT_NBOX - 1>();
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float* x = v + 8 * j;
+              uint4 w;
+              __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+              ob[lane * 4 + (j ^ ((lane >> 1) & 3))] = w;
+            }
+            fence_proxy_async();  // generic-proxy writes -> the tensor store's reads
+            __syncwarp();
+            if (lane == 0 && nr > 0) {
+              tma_store_2d(&p.tmap_out, smem_u32(ob), oc, (int)row0);
+              bulk_commit();
+            }
+            ++out_seq;
+            continue;
+          }
           // Through the warp's staging box (32 rows of 64 bytes, 16-byte piece
           // j of row r at j ^ ((r >> 1) & 3): the row-wise writes and the
           // piece-wise reads are both conflict-free), so that each store
@@ -1057,6 +1102,9 @@ __global__ void __launch_bounds__(THREADS, 1) rowgemm_kernel(const __grid_consta
       }
     }
     if constexpr (L::RESID) cp_async_wait<0>();  // no box load outlives the loop
+    if constexpr (EPI == EPI_STORE) {
+      if (lane == 0) bulk_wait_all();  // every tensor store has finished
+    }
   }
 
   tc_fence_before();
@@ -1129,6 +1177,20 @@ static bool encode_rows_map(CUtensorMap* map, const void* x, int64_t m, int64_t 
   const cuuint32_t elem[2] = {1, 1};
   return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, elem,
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The (m, n) bf16 output rows at out (leading dim ldo) as a tensor map of
+// 32-column x 32-row boxes with the 64-byte swizzle of the staging boxes.
+static bool encode_out_map(CUtensorMap* map, void* out, int64_t m, int64_t n, int64_t ldo) {
+  EncodeTiledFn encode = encode_tiled();
+  if (!encode) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)m};
+  const cuuint64_t strides[1] = {(cuuint64_t)(ldo * 2)};
+  const cuuint32_t box[2] = {32, 32};
+  const cuuint32_t elem[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -1235,6 +1297,11 @@ int mb_gemm_rows_ex(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t 
   prm.w_blocks = prm.n_blocks;
   prm.w_last = prm.n_last;
   cudaStream_t s = as_stream(stream);
+  if (out) {
+    MB_REQUIRE(m < (int64_t(1) << 31), "gemm_rows: at most 2^31 - 1 rows per call");
+    if (!encode_out_map(&prm.tmap_out, out, m, n, ldo))
+      return ::mb::fail(MB_LAUNCH_FAILED, "gemm_rows: could not encode the output tensor map");
+  }
   if (ln) {
     if (g_ln_plan == 1) return launch_rowgemm<PRO_LN, EPI_STORE, false, 4, true>(prm, s, "gemm_rows");
     // contiguous fp32 rows take the bulk-copy staged path (one block per 32-row group)
