@@ -206,6 +206,13 @@ class CellIndex {
     if ((uint64_t)dq >= (uint64_t)nq_ || (uint64_t)dr >= (uint64_t)nr_) return -1;
     return grid_[(size_t)(dq * nr_ + dr)];
   }
+  // Dense grids only: the grid offset of a cell inside the box, the offset
+  // step of a coordinate step, and the entry at an offset (no bounds check:
+  // the caller keeps to the box).
+  bool dense() const { return dense_; }
+  int64_t offset(int64_t q, int64_t r) const { return (q - q0_) * nr_ + (r - r0_); }
+  int64_t stride(int64_t dq, int64_t dr) const { return dq * nr_ + dr; }
+  int64_t at(int64_t off) const { return grid_[(size_t)off]; }
 
  private:
   int64_t q0_, r0_, nq_, nr_;
@@ -293,10 +300,15 @@ std::string build_one(const PosIn& in, Graph& g) {
     struct Hit { int32_t c, s, d; };
     std::vector<Hit> hits;
     hits.reserve(n_s * T.disk_q.size());  // at most one hit per disk offset
+    // dense box: each disk offset is one grid step (a stone's disk, radius
+    // 8, stays inside the 9-cell margin)
+    std::vector<int64_t> disk_off(dense ? nd : 0);
+    for (int d = 0; d < (int)disk_off.size(); ++d) disk_off[d] = legal.stride(T.disk_q[d], T.disk_r[d]);
     for (int64_t s = 0; s < n_s; ++s) {
       const int64_t q = in.stone_qr[2 * s], r = in.stone_qr[2 * s + 1];
+      const int64_t sbase = dense ? legal.offset(q, r) : 0;
       for (int d = 0; d < nd; ++d) {
-        const int64_t c = legal.find(q + T.disk_q[d], r + T.disk_r[d]);
+        const int64_t c = dense ? legal.at(sbase + disk_off[d]) : legal.find(q + T.disk_q[d], r + T.disk_r[d]);
         if (c < 0) continue;
         hits.push_back({(int32_t)c, (int32_t)s, d});
         ++cnt[c + 1];
@@ -326,8 +338,10 @@ std::string build_one(const PosIn& in, Graph& g) {
     hits.reserve(6 * n_l);
     for (int64_t c = 0; c < n_l; ++c) {
       const int64_t q = in.legal_qr[2 * c], r = in.legal_qr[2 * c + 1];
+      const int64_t cbase = dense ? legal.offset(q, r) : 0;
       for (int j = 0; j < 6; ++j) {
-        const int64_t dst = legal.find(q + steps[j][0], r + steps[j][1]);
+        const int64_t dst = dense ? legal.at(cbase + legal.stride(steps[j][0], steps[j][1]))
+                                  : legal.find(q + steps[j][0], r + steps[j][1]);
         if (dst < 0) continue;
         hits.push_back({(int32_t)c, (int32_t)dst, (uint8_t)(j % 3)});
         ++cnt[dst + 1];
@@ -351,6 +365,15 @@ std::string build_one(const PosIn& in, Graph& g) {
     const int64_t s = stones.find(q, r);
     return s < 0 ? 0 : 1 + (int)g.stone_own[s];
   };
+  // With a dense box the digits sit in a grid of their own: a legal cell's
+  // 11-cell line samples and window starts (at most 5 steps away, inside the
+  // 9-cell margin) are then plain offsets from the cell's.
+  std::vector<uint8_t> digit;
+  if (dense) {
+    digit.assign((size_t)(nq * nr), 0);
+    for (int64_t s = 0; s < n_s; ++s)
+      digit[(size_t)stones.offset(in.stone_qr[2 * s], in.stone_qr[2 * s + 1])] = (uint8_t)(1 + g.stone_own[s]);
+  }
 
   // ---- windows: every (axis, start) through a stone, ascending key (builder.py:572-585)
   struct Cand { int64_t key, q, r; int a; };
@@ -404,11 +427,18 @@ std::string build_one(const PosIn& in, Graph& g) {
   const float rows_total = (float)(3 * W);
   for (int64_t c = 0; c < n_l; ++c) {
     const int64_t q0 = in.legal_qr[2 * c], r0 = in.legal_qr[2 * c + 1];
+    const int64_t base = dense ? stones.offset(q0, r0) : 0;
     int any_win = 0, max_own = 0, max_opp = 0, make5 = 0, make4 = 0, hit5 = 0, four_rows = 0, kept_rows = 0;
     for (int a = 0; a < 3; ++a) {
       int line[2 * W - 1];
-      for (int o = 0; o < 2 * W - 1; ++o)
-        line[o] = digit_at(q0 + AX[a][0] * (o - (W - 1)), r0 + AX[a][1] * (o - (W - 1)));
+      const int64_t step = dense ? stones.stride(AX[a][0], AX[a][1]) : 0;
+      if (dense) {
+        const uint8_t* d0 = digit.data() + base - step * (W - 1);
+        for (int o = 0; o < 2 * W - 1; ++o) line[o] = d0[step * o];
+      } else {
+        for (int o = 0; o < 2 * W - 1; ++o)
+          line[o] = digit_at(q0 + AX[a][0] * (o - (W - 1)), r0 + AX[a][1] * (o - (W - 1)));
+      }
       if (line[W - 1] != 0) return "a legal cell holds a stone";
       // The window starting k steps before the cell covers line[5 - k ..
       // 10 - k]; its pattern and counts slide from k = 5 down to k = 0.
@@ -438,7 +468,9 @@ std::string build_one(const PosIn& in, Graph& g) {
         if (post1 < 0) return "internal: a placement slot has no post-placement class";
         const bool kept = own > 0 || opp > 0;
         // only a row holding a stone can name a live window
-        const int64_t w = kept ? live[a].find(q0 - AX[a][0] * k, r0 - AX[a][1] * k) : -1;
+        const int64_t w = !kept ? -1
+                                : dense ? live[a].at(base - step * k)
+                                        : live[a].find(q0 - AX[a][0] * k, r0 - AX[a][1] * k);
         if ((w >= 0) != kept) return "internal: a window through a stone is missing from the live set";
         max_own = std::max(max_own, own);
         max_opp = std::max(max_opp, opp);
