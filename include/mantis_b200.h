@@ -396,7 +396,9 @@ int mb_gemm_rows(const void* x, int x_dtype, int64_t ldx, int64_t m, const float
  * memory), w_image = mb_gemm_weight_image of the (N, K) weight. With `out`
  * (bf16, ldo >= n) an optional fp32 addend `add` (ld_add) is summed before the
  * activation; `residual` (fp32, N = 256) takes the in-place update instead.
- * Replaces every nn.Linear of the trunk and the decoder (model.py:246-260,
+ * A bf16 `out` is written by tensor-map stores of 32 x 32 boxes, so m must be
+ * below 2^31 with `out` too; MB_LAUNCH_FAILED if the driver's tensor-map
+ * encoder cannot be had. Replaces every nn.Linear of the trunk and the decoder (model.py:246-260,
  * 425-692 Q / K|V / FFN / PairMlp projections, 1031-1139 decoder GEMMs),
  * which the reference runs through cuBLAS under autocast. */
 int mb_gemm_rows_ex(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k, const float* gamma,
@@ -406,7 +408,8 @@ int mb_gemm_rows_ex(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t 
 
 /* Launch plan of the bf16-output row GEMMs (a measurement knob; the
  * defaults are the measured best): store_plan 0 streams W K-blocks per row
- * tile, 1 holds a whole N block of W in shared memory per CTA (K = 256);
+ * tile, 1 holds a whole N block of W in shared memory per CTA (256 columns
+ * at K = 256, 128 columns at K = 512 when N <= 256);
  * ln_plan 0 stages the LayerNorm prologue's fp32 rows in 32-row groups, 1
  * weight-stationary with per-row loads, 2 per-row loads with W streamed.
  * Process-wide; not for use while launches are being issued from other
