@@ -9,19 +9,21 @@
 // follow the reference adjacency walk (builder.py:458-471).
 //
 // A neighbour row lies within 64 rows of its own in the workload's token
-// order, so a 128-row tile reads its neighbours from its rows +- 64. One
-// persistent CTA per SM takes a contiguous range of tiles and keeps that
-// window in shared memory as a ring of four 64-row segments (128 KB): moving
-// to the next tile drops two segments and bulk-copies two new ones, so each
+// order, so a 64-row tile (M = 64 MMAs) reads its neighbours from its rows
+// +- 64: three 64-row segments. One persistent CTA per SM takes a contiguous
+// range of tiles and keeps a ring of four segments (128 KB) in shared
+// memory: the fourth holds the next tile's new segment, copied while this
+// tile's mean is formed, so the copies run a tile ahead of the mean and each
 // x row crosses from DRAM once per CTA. Rows outside the window (other
 // inputs) are read from global memory instead.
 //
 // Warp roles (12 warps): warp 0 lane 0 issues the MMAs, lane 1 streams W
 // K-blocks (two 32 KB stages), lane 2 loads window segments; warps 1-7 form
-// the mean A tile K-block by K-block (two 16 KB stages, 128-byte swizzled
+// the mean A tile K-block by K-block (two 8 KB stages, 128-byte swizzled
 // K-major, eight lanes per row reading one 128-byte piece of each neighbour
 // row: conflict-free); warps 8-11 drain the two TMEM accumulators (256
-// columns each), add bias and x[r] (read back through L2, where the window
+// columns each; an M = 64 accumulator keeps 16 rows in lanes 0-15 of each
+// lane quadrant), add bias and x[r] (read back through L2, where the window
 // copy left it) and write y. Every mbarrier wait is bounded.
 #include "common.cuh"
 
@@ -30,19 +32,25 @@ namespace sm100 {
 
 constexpr int HX_SEG = 64;                        // rows per window segment
 constexpr int HX_SEG_BYTES = HX_SEG * KDIM * 2;   // 32 KB
-constexpr int HX_NSEG = 4;                        // a tile's rows +- 64
+constexpr int HX_NSEG = 4;                        // ring slots: a tile's three segments and the next one
+constexpr int HX_WIN = 3;                         // segments a tile reads: its own rows +- 64
+constexpr int HX_TM = 64;                         // rows per tile (M = 64 MMAs)
+constexpr int HX_A_KB = HX_TM * BK * 2;           // 8 KB per A K-block stage
+constexpr uint32_t HX_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                              ((uint32_t)(HX_TM >> 4) << 24);
+
 constexpr int HX_PRODUCERS = 7;
 constexpr int HX_EPI = 4;
 constexpr int HX_THREADS = (1 + HX_PRODUCERS + HX_EPI) * 32;
 constexpr int HX_WIN_OFF = 0;
 constexpr int HX_A_OFF = HX_WIN_OFF + HX_NSEG * HX_SEG_BYTES;
-constexpr int HX_W_OFF = HX_A_OFF + 2 * A_KB_BYTES;
+constexpr int HX_W_OFF = HX_A_OFF + 2 * HX_A_KB;
 constexpr int HX_BAR_OFF = HX_W_OFF + 2 * W_KB_BYTES;
 constexpr int HX_BIAS_OFF = HX_BAR_OFF + 256;      // the bias (256 fp32)
 constexpr int HX_ZERO_OFF = HX_BIAS_OFF + KDIM * 4;  // one zero row: absent neighbours read it
 constexpr int HX_SMEM = HX_ZERO_OFF + KDIM * 2 + 1024;  // + alignment slack
 static_assert(HX_SMEM <= 232448, "hex window plan exceeds 227 KB");
-static_assert(BN == KDIM && BM == 2 * HX_SEG, "the window plan assumes 128-row tiles of 256 columns");
+static_assert(BN == KDIM && HX_TM == HX_SEG, "the window plan assumes 64-row tiles of 256 columns");
 
 __global__ void __launch_bounds__(HX_THREADS, 1) hex_window_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t n, const int32_t* __restrict__ nbr,
@@ -56,25 +64,29 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hex_window_kernel(
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + HX_BAR_OFF);
   float* bias_s = reinterpret_cast<float*>(smem + HX_BIAS_OFF);
   uint64_t* seg_full = bars;        // [4]
-  uint64_t* mean_done = bars + 4;   // [1]
-  uint64_t* a_full = bars + 5;      // [2]
-  uint64_t* a_empty = bars + 7;     // [2]
-  uint64_t* w_full = bars + 9;      // [2]
-  uint64_t* w_empty = bars + 11;    // [2]
-  uint64_t* t_full = bars + 13;     // [2]
-  uint64_t* t_empty = bars + 15;    // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
-  volatile int* abort = reinterpret_cast<volatile int*>(bars + 18);
+  // mean_done alternates by tile parity: the producers may finish tile i + 1
+  // before the segment loader has seen tile i, never tile i + 2 (it needs the
+  // segment loaded after tile i), so neither barrier runs a phase ahead of
+  // the loader's wait
+  uint64_t* mean_done = bars + 4;   // [2]
+  uint64_t* a_full = bars + 6;      // [2]
+  uint64_t* a_empty = bars + 8;     // [2]
+  uint64_t* w_full = bars + 10;     // [2]
+  uint64_t* w_empty = bars + 12;    // [2]
+  uint64_t* t_full = bars + 14;     // [2]
+  uint64_t* t_empty = bars + 16;    // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  volatile int* abort = reinterpret_cast<volatile int*>(bars + 19);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t n_tiles = (n + BM - 1) / BM;
+  const int64_t n_tiles = (n + HX_TM - 1) / HX_TM;
   const int64_t t0 = n_tiles * blockIdx.x / gridDim.x, t1 = n_tiles * (blockIdx.x + 1) / gridDim.x;
   const int64_t my_tiles = t1 - t0;
-  const int64_t s0 = 2 * t0 - 1;  // the first window segment (rows 64 s0 ...)
+  const int64_t s0 = t0 - 1;  // the first window segment (rows 64 s0 ...); tile t reads t - 1 .. t + 1
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < HX_NSEG; ++i) mbar_init(smem_u32(&seg_full[i]), 1);
-    mbar_init(smem_u32(&mean_done[0]), HX_PRODUCERS);
+    for (int i = 0; i < 2; ++i) mbar_init(smem_u32(&mean_done[i]), HX_PRODUCERS);
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&a_full[i]), HX_PRODUCERS);
       mbar_init(smem_u32(&a_empty[i]), 1);
@@ -105,7 +117,7 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hex_window_kernel(
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------ MMA issuer
-      const uint32_t idesc = make_idesc(BN);
+      const uint32_t idesc = HX_IDESC;
       bool ok = true;
       for (int64_t i = 0; ok && i < my_tiles && !*abort; ++i) {
         const uint32_t tb = i & 1, tph = (i >> 1) & 1;
@@ -120,7 +132,7 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hex_window_kernel(
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(a_smem + s * A_KB_BYTES), b0 = smem_u32(w_smem + s * W_KB_BYTES);
+          const uint32_t a0 = smem_u32(a_smem + s * HX_A_KB), b0 = smem_u32(w_smem + s * W_KB_BYTES);
 #pragma unroll
           for (int j = 0; j < BK / 16; ++j)
             umma(d, smem_desc(a0 + j * 32), smem_desc(b0 + j * 32), idesc, (kb | j) != 0);
@@ -155,13 +167,16 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hex_window_kernel(
           mbar_arrive(bar);  // a segment before row 0 or past the last row: nothing to copy
         }
       };
-      for (int64_t s = s0; s < s0 + HX_NSEG; ++s) load_seg(s);
-      for (int64_t i = 0; i + 1 < my_tiles && !*abort; ++i) {
-        // tile t0 + i no longer needs its first two segments once its mean is formed
-        if (!mbar_wait(smem_u32(&mean_done[0]), i & 1, abort)) break;
-        const int64_t t = t0 + i;
-        load_seg(2 * t + 3);
-        load_seg(2 * t + 4);
+      // Only segments some tile waits for are copied (the last tile reads up
+      // to segment t0 + my_tiles), so no copy outlives the CTA.
+      const int64_t s_last = t0 + my_tiles;
+      for (int64_t s = s0; my_tiles > 0 && s < s0 + HX_NSEG && s <= s_last; ++s) load_seg(s);
+      for (int64_t i = 0; t0 + i + 3 <= s_last && !*abort; ++i) {
+        // once tile t0 + i's mean is formed its first segment is free: the
+        // slot takes segment t + 3, read from tile t + 2 on, while tile t + 1
+        // runs on segments already in place
+        if (!mbar_wait(smem_u32(&mean_done[i & 1]), (i >> 1) & 1, abort)) break;
+        load_seg(t0 + i + 3);
       }
     }
   } else if (warp <= HX_PRODUCERS) {
@@ -175,14 +190,14 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hex_window_kernel(
     // row with no branch.
     const int pw = warp - 1;
     const int sub = lane >> 3, c8 = lane & 7;  // 4 rows per warp step, 8 lanes (16 B each) per row
-    constexpr int GROUPS = (BM / 4 + HX_PRODUCERS - 1) / HX_PRODUCERS;
+    constexpr int GROUPS = (HX_TM / 4 + HX_PRODUCERS - 1) / HX_PRODUCERS;
     int raw[GROUPS][HEX_SLOTS];
     auto fetch = [&](int64_t t) {
 #pragma unroll
       for (int k = 0; k < GROUPS; ++k) {
         const int g = pw + HX_PRODUCERS * k;
-        const int64_t row = t * BM + g * 4 + sub;
-        const bool live = g < BM / 4 && row < n;
+        const int64_t row = t * HX_TM + g * 4 + sub;
+        const bool live = g < HX_TM / 4 && row < n;
 #pragma unroll
         for (int j = 0; j < HEX_SLOTS; ++j) raw[k][j] = live ? __ldg(nbr + row * HEX_SLOTS + j) : -1;
       }
@@ -190,8 +205,8 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hex_window_kernel(
     if (my_tiles > 0) fetch(t0);
     bool ok = true;
     for (int64_t i = 0; ok && i < my_tiles && !*abort; ++i) {
-      const int64_t t = t0 + i, r0 = t * BM;
-      const int64_t wbase = r0 - HX_SEG;  // first row of the window (segment 2t - 1)
+      const int64_t t = t0 + i, r0 = t * HX_TM;
+      const int64_t wbase = r0 - HX_SEG;  // first row of the window (segment t - 1)
       int code[GROUPS][HEX_SLOTS];
       float inv[GROUPS];
 #pragma unroll
@@ -205,8 +220,8 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hex_window_kernel(
             report(ERR_INDEX);
           } else if (nb >= 0) {
             const int64_t wr = nb - wbase;
-            if (wr >= 0 && wr < HX_NSEG * HX_SEG) {
-              const int slot = (int)((2 * t - 1 + wr / HX_SEG - s0) & (HX_NSEG - 1));
+            if (wr >= 0 && wr < HX_WIN * HX_SEG) {
+              const int slot = (int)((t - 1 + wr / HX_SEG - s0) & (HX_NSEG - 1));
               c = slot * HX_SEG_BYTES + (int)(nb & (HX_SEG - 1)) * (KDIM * 2);
             } else {
               c = -2 - (int)nb;
@@ -224,8 +239,8 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hex_window_kernel(
         for (int j = 0; j < HEX_SLOTS; ++j) far_row |= code[k][j] < 0;
       const bool far = __any_sync(0xffffffffu, far_row);
       if (i + 1 < my_tiles) fetch(t + 1);  // in flight during this tile
-      // this tile's new segments (all four for the first tile)
-      for (int64_t s = (i == 0 ? s0 : 2 * t + 1); s <= 2 * t + 2; ++s) {
+      // this tile's new segment (all three for the first tile)
+      for (int64_t s = (i == 0 ? s0 : t + 1); s <= t + 1; ++s) {
         const int slot = (int)((s - s0) & (HX_NSEG - 1));
         if (!mbar_wait(smem_u32(&seg_full[slot]), ((s - s0) >> 2) & 1, abort)) {
           ok = false;
@@ -240,12 +255,12 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hex_window_kernel(
           ok = false;
           break;
         }
-        uint8_t* abuf = a_smem + s * A_KB_BYTES;
+        uint8_t* abuf = a_smem + s * HX_A_KB;
         const uint8_t* wk = win + kb * 128 + c8 * 16;
 #pragma unroll
         for (int k = 0; k < GROUPS; ++k) {
           const int g = pw + HX_PRODUCERS * k;
-          if (g >= BM / 4) break;
+          if (g >= HX_TM / 4) break;
           const int r = g * 4 + sub;
           float acc[8] = {};
           uint4 raw16[HEX_SLOTS];
@@ -281,7 +296,7 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hex_window_kernel(
         if (lane == 0) mbar_arrive(smem_u32(&a_full[s]));
       }
       __syncwarp();
-      if (ok && lane == 0) mbar_arrive(smem_u32(&mean_done[0]));
+      if (ok && lane == 0) mbar_arrive(smem_u32(&mean_done[i & 1]));
     }
   } else {
     // --------------------------------------------------------- epilogue
@@ -290,8 +305,10 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hex_window_kernel(
       const uint32_t tb = i & 1, tph = (i >> 1) & 1;
       if (!mbar_wait(smem_u32(&t_full[tb]), tph, abort)) break;
       tc_fence_after();
-      const int64_t row = (t0 + i) * BM + qd * 32 + lane;
-      const bool live = row < n;
+      // an M = 64 accumulator: rows 16 qd .. 16 qd + 15 in lanes 0-15 of
+      // TMEM lane quadrant qd
+      const int64_t row = (t0 + i) * HX_TM + qd * 16 + lane;
+      const bool live = lane < 16 && row < n;
       // x[r] is read back through L2 (the window slots may be refilled by
       // now), each 32-column chunk's 64 bytes requested two chunks ahead
       const uint4* xr = reinterpret_cast<const uint4*>(x + (live ? row : 0) * KDIM);
@@ -351,7 +368,7 @@ static int hex_window_launch(const void* x, int64_t n, const int32_t* nbr, const
                              void* out, int64_t ldo, cudaStream_t s) {
   if (cudaFuncSetAttribute(hex_window_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, HX_SMEM) != cudaSuccess)
     return ::mb::fail(MB_LAUNCH_FAILED, "hex_message_pass: %d bytes of shared memory refused", HX_SMEM);
-  const int64_t tiles = (n + BM - 1) / BM;
+  const int64_t tiles = (n + HX_TM - 1) / HX_TM;
   const int grid = (int)(tiles < num_sms() ? tiles : num_sms());
   hex_window_kernel<<<grid, HX_THREADS, HX_SMEM, s>>>((const __nv_bfloat16*)x, n, nbr,
                                                       (const __nv_bfloat16*)w_image, bias, (__nv_bfloat16*)out, ldo);
