@@ -29,8 +29,12 @@ def _message_case(n_pos, seed, w_std=0.05):
     return x, torch.from_numpy(nbr), w, b
 
 
-@pytest.mark.parametrize("n_pos,rows", [(8, None), (5, 1000), (3, 37)])
+@pytest.mark.parametrize("n_pos,rows", [(8, None), (5, 1000), (3, 37), (160, None)])
 def test_hex_message_pass_matches_restatement(n_pos, rows):
+    """Against the fp64 restatement: one tile per CTA for the small cases;
+    160 positions (40,960 rows, 640 tiles of 64 rows) give each persistent CTA
+    four or five tiles, so the window ring's refills, both accumulator
+    buffers and the alternating tile barriers all run."""
     x, nbr, w, b = _message_case(n_pos, 7 + n_pos)
     if rows is not None:  # a row count off the 128-row tile, neighbours clipped to it
         x, nbr = x[:rows].contiguous(), nbr[:rows].clone()
