@@ -262,7 +262,6 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hex_window_kernel(
           const int g = pw + HX_PRODUCERS * k;
           if (g >= HX_TM / 4) break;
           const int r = g * 4 + sub;
-          float acc[8] = {};
           uint4 raw16[HEX_SLOTS];
           if (!far) {
 #pragma unroll
@@ -275,20 +274,23 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hex_window_kernel(
                                 : __ldg(reinterpret_cast<const uint4*>(x + (int64_t)(-2 - c) * KDIM + kb * BK) + c8);
             }
           }
+          // sums in packed f32x2 pairs (the same fp32 adds, in the same order)
+          uint64_t acc2[4] = {0, 0, 0, 0};
 #pragma unroll
           for (int j = 0; j < HEX_SLOTS; ++j) {
-            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw16[j]);
+            const uint32_t wd[4] = {raw16[j].x, raw16[j].y, raw16[j].z, raw16[j].w};
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f = __bfloat1622float2(h[e]);
-              acc[2 * e] += f.x;
-              acc[2 * e + 1] += f.y;
-            }
+            for (int e = 0; e < 4; ++e) acc2[e] = radius::add2(acc2[e], radius::bf2(wd[e]));
           }
           uint4 w4;
           __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w4);
+          const uint64_t inv2 = radius::pack2(inv[k], inv[k]);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) hw[e] = __floats2bfloat162_rn(acc[2 * e] * inv[k], acc[2 * e + 1] * inv[k]);
+          for (int e = 0; e < 4; ++e) {
+            float lo, hi;
+            radius::unpack2(radius::mul2(acc2[e], inv2), lo, hi);
+            hw[e] = __floats2bfloat162_rn(lo, hi);
+          }
           *reinterpret_cast<uint4*>(abuf + r * 128 + ((c8 ^ (r & 7)) << 4)) = w4;
         }
         fence_proxy_async();  // generic-proxy stores -> visible to the tensor cores
