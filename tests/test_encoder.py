@@ -67,6 +67,21 @@ def test_empty_board_and_single_stone():
         _assert_same_batch(enc.encode(case), mb.collate([mb.from_spec(s) for s in case]))
 
 
+def test_spread_out_position_takes_the_hash_index():
+    """Two stone groups 3,000 cells apart: the bounding box exceeds the dense
+    grid's 4M cells, so every lookup goes through the hash table instead of
+    grid offsets; the arrays must not change. Mixed with a compact position
+    (dense path) in one batch."""
+    _library_built()
+    far = PositionSpec(np.array([[0, 0], [1, 0], [3000, -1500], [3001, -1500], [3000, -1499]]),
+                       np.array([0, 1, 0, 1, 1]), 0,
+                       np.array([[2, 0], [0, 1], [-1, 0], [-3, 4], [3002, -1500], [2999, -1500], [3003, -1505]]), 1)
+    near = eng.random_positions(1, 20, 40, seed=9)[0]
+    for case in ([far], [far, near], [near, far]):
+        _assert_same_batch(enc.encode(case), mb.collate([mb.from_spec(s) for s in case]))
+        _assert_same_batch(enc.encode(case, threads=2), mb.collate([mb.from_spec(s) for s in case]))
+
+
 def test_refusals_match_the_builder():
     _library_built()
     good = eng.random_positions(1, 10, 20, seed=6)[0]
